@@ -1,0 +1,54 @@
+"""Test helpers: oracle construction and a call-logging proxy (test infrastructure)."""
+
+from __future__ import annotations
+
+from fast_dllm_relax_b200.config import ModelConfig
+from oracle.model import OracleConfig, OracleModel
+
+
+def oracle_config(cfg: ModelConfig) -> OracleConfig:
+    return OracleConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size,
+                        intermediate_size=cfg.intermediate_size, num_hidden_layers=cfg.num_hidden_layers,
+                        num_attention_heads=cfg.num_attention_heads,
+                        num_key_value_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
+                        rms_norm_eps=cfg.rms_norm_eps, rope_theta=cfg.rope_theta,
+                        tie_word_embeddings=cfg.tie_word_embeddings, bd_size=cfg.bd_size)
+
+
+def make_oracle(cfg: ModelConfig, params, dtype: str) -> OracleModel:
+    return OracleModel(oracle_config(cfg), params, dtype)
+
+
+class LoggingOracle:
+    """Wraps an OracleModel and logs calls in the golden call-log format
+    [name, rows, cache_offset, prefix_len]."""
+
+    def __init__(self, model: OracleModel):
+        self.m = model
+        self.cfg = model.cfg
+        self.dtype = model.dtype
+        self.calls: list[list] = []
+
+    def embed(self, ids):
+        self.calls.append(["embed", int(ids.shape[0]), -1, -1])
+        return self.m.embed(ids)
+
+    def forward_hidden(self, x, bias):
+        self.calls.append(["forward_hidden", int(x.shape[1]), -1, -1])
+        return self.m.forward_hidden(x, bias)
+
+    def get_logits(self, h):
+        self.calls.append(["get_logits", int(h.shape[1]), -1, -1])
+        return self.m.get_logits(h)
+
+    def build_prefix_cache(self, x, bias, k, v):
+        self.calls.append(["build_prefix_cache", int(x.shape[1]), -1, -1])
+        return self.m.build_prefix_cache(x, bias, k, v)
+
+    def forward_cached(self, x, k, v, off, plen, write_rel=0, attend_rel=None):
+        self.calls.append(["forward_cached", int(x.shape[1]), int(off), int(plen)])
+        return self.m.forward_cached(x, k, v, off, plen, write_rel, attend_rel)
+
+    def forward_block_partial(self, x, k, v, off, plen, rp):
+        self.calls.append([f"forward_block_partial_rp{rp}", int(x.shape[1]), int(off), int(plen)])
+        return self.m.forward_block_partial(x, k, v, off, plen, rp)
