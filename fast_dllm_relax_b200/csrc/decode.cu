@@ -1,0 +1,237 @@
+// Device-resident block-diffusion decode driver (greedy, threshold-parallel unmasking).
+//
+// Follows fast_dllm_relax/runtime.py:591-880 (relax_greedy_generate) for prompts of at least one
+// block: the block-aligned prompt fast path (:679-708), the prefix-cache rebuild rule (:718-739),
+// the sub-block refinement loop with the full / partial step choice (:748-805), the length and stop
+// checks (:655-669, :839-849) and block-append (:851-878).  What differs is where the work runs:
+// the token ids of the active block live on the device, each step is embed -> 28-layer cached
+// forward -> fused lm_head + confidence -> unmask kernel (the unmask kernel writes the chosen
+// tokens into the device block), and the host reads back only the step's window (status, tokens,
+// unmask flags: ~70 bytes) to drive the loop.  The reference instead copies the fp32 logits'
+// reductions back and decides in Python (runtime.py:176-181, 796-805).
+#include <cstring>
+
+#include "handle.h"
+
+using namespace fdllm;
+
+namespace {
+
+constexpr int kWin = 32;                  // max sub-block width read back per step
+constexpr int kHostInts = 2 + 2 * kWin;   // pinned read-back: status[2], window tokens, unmask flags
+
+struct Driver {
+  fdllm_handle* h;
+  cudaStream_t s;
+  int bs, sbs, mask_id, stop;
+  double thr;
+  bool block_cache;
+  int cap = 0;
+  int prefix_len = 0;
+  int32_t st[4] = {0, 0, 0, 0};  // unmask_updates, block_recomputes, partial_recomputes, block_appends
+
+  int* host() { return h->dec.host; }
+
+  int setup(int n0, int max_new) {
+    const fdllm_config& c = h->cfg;
+    cap = static_cast<int>((static_cast<long long>(n0) + max_new + bs - 1) / bs * bs + bs);
+    if (cap > c.max_positions) return fail(FDLLM_ERR_INVALID, "prompt + max_new_tokens exceeds max_positions");
+    const size_t cache_bytes = static_cast<size_t>(c.num_hidden_layers) * cap * c.num_key_value_heads * c.head_dim * h->esz;
+    FDLLM_TRY(h->dec.k.ensure(cache_bytes));
+    FDLLM_TRY(h->dec.v.ensure(cache_bytes));
+    FDLLM_TRY(h->dec.ids.ensure(static_cast<size_t>(cap)));
+    FDLLM_TRY(h->dec.block.ensure(static_cast<size_t>(bs)));
+    FDLLM_TRY(h->dec.x.ensure(static_cast<size_t>(cap) * c.hidden_size * h->esz));
+    FDLLM_TRY(h->dec.hid.ensure(static_cast<size_t>(bs) * c.hidden_size * h->esz));
+    FDLLM_TRY(h->dec.cids.ensure(static_cast<size_t>(bs)));
+    FDLLM_TRY(h->dec.cmax.ensure(static_cast<size_t>(bs)));
+    FDLLM_TRY(h->dec.out.ensure(2 + 2 * kWin));
+    if (h->dec.host == nullptr) CUDA_TRY(cudaMallocHost(&h->dec.host, kHostInts * sizeof(int)));
+    return FDLLM_OK;
+  }
+
+  // build_prefix_cache_from_ids (runtime.py:266-323): rows [0, n) of a fresh cache.
+  int prefill(const int* ids, int n) {
+    prefix_len = 0;
+    if (n == 0) return FDLLM_OK;
+    CUDA_TRY(cudaMemcpyAsync(h->dec.ids.p, ids, n * sizeof(int), cudaMemcpyHostToDevice, s));
+    CUDA_TRY(launch_embed(h->dec.ids.p, n, h->embed, h->cfg.vocab_size, h->cfg.hidden_size, h->dec.x.p, h->dtype,
+                          h->err.p, s));
+    FDLLM_TRY(dense_forward(h, h->dec.x.p, nullptr, n, h->dec.k.p, h->dec.v.p, cap, false, nullptr, s));
+    prefix_len = n;
+    return FDLLM_OK;
+  }
+
+  int upload_block(const int* ids) {
+    CUDA_TRY(cudaMemcpyAsync(h->dec.block.p, ids, bs * sizeof(int), cudaMemcpyHostToDevice, s));
+    return FDLLM_OK;
+  }
+
+  // forward_cached / forward_block_partial_rp{s0} over the device block (runtime.py:333-343, 398-433)
+  int forward(int s0, int rows, int write_rel) {
+    CUDA_TRY(launch_embed(h->dec.block.p + s0, rows, h->embed, h->cfg.vocab_size, h->cfg.hidden_size, h->dec.x.p,
+                          h->dtype, h->err.p, s));
+    fdllm_request r{h->dec.k.p, h->dec.v.p, cap, rows, prefix_len, write_rel, bs, prefix_len + write_rel, nullptr};
+    std::vector<ReqDesc> reqs(1);
+    FDLLM_TRY(cached_desc(h, r, 0, &reqs[0]));
+    FDLLM_TRY(forward_core(h, h->dec.x.p, rows, reqs, nullptr, 0, 0, h->dec.hid.p, s));
+    return confidence_locked(h, h->dec.hid.p, rows, h->dec.cids.p, h->dec.cmax.p, nullptr, nullptr, s);
+  }
+
+  // Unmask on the device, read back the window.  Returns the number of tokens unmasked.
+  int unmask(int rows, int s0, int len, bool partial, int* x_window) {
+    int* out = h->dec.out.p;
+    CUDA_TRY(launch_unmask(h->dec.cids.p, h->dec.cmax.p, rows, h->dec.block.p, s0, len, partial ? 1 : 0, mask_id, thr,
+                           out + 2, nullptr, out + 2 + kWin, out, s));
+    CUDA_TRY(cudaMemcpyAsync(host(), out, (2 + 2 * kWin) * sizeof(int), cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaStreamSynchronize(s));
+    const int* hb = host();
+    for (int j = 0; j < len; ++j)
+      if (hb[2 + kWin + j]) x_window[j] = hb[2 + j];
+    st[0] += hb[1];
+    return FDLLM_OK;
+  }
+
+  // Last row's unshifted argmax after a committing forward (runtime.py:181).
+  int last_token(int* tok) {
+    CUDA_TRY(cudaMemcpyAsync(host(), h->dec.cids.p + bs - 1, sizeof(int), cudaMemcpyDeviceToHost, s));
+    CUDA_TRY(cudaStreamSynchronize(s));
+    *tok = host()[0];
+    return FDLLM_OK;
+  }
+};
+
+bool has_completed_stop(const std::vector<int>& seq, size_t plen, int stop, int mask_id) {
+  if (stop < 0) return false;
+  for (size_t i = plen; i < seq.size(); ++i) {
+    if (seq[i] == stop) {
+      for (size_t j = plen; j < i; ++j)
+        if (seq[j] == mask_id) return false;
+      return true;
+    }
+  }
+  return false;
+}
+
+}  // namespace
+
+extern "C" int fdllm_generate(fdllm_handle* h, const int32_t* prompt, int prompt_len, int max_new_tokens,
+                              int block_size, int small_block_size, double threshold, int use_block_cache, int mask_id,
+                              int stop_token, int32_t* out_tokens, int* n_out, int32_t* stats, float* timing_ms,
+                              void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (prompt == nullptr || out_tokens == nullptr || n_out == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
+  if (max_new_tokens < 0) return fail(FDLLM_ERR_INVALID, "max_new_tokens must be non-negative.");
+  if (block_size != h->cfg.bd_size) return fail(FDLLM_ERR_INVALID, "block_size must equal the model's bd_size");
+  if (small_block_size <= 0 || small_block_size > kWin || block_size % small_block_size != 0)
+    return fail(FDLLM_ERR_INVALID, "small_block_size must divide block_size and be at most 32");
+  if (prompt_len < block_size)
+    return fail(FDLLM_ERR_UNSUPPORTED, "prompts shorter than one block take the stateless path (forward_hidden); "
+                                       "use the Python runtime for them");
+  std::lock_guard<std::mutex> lock(h->mu);
+  Driver d{h, static_cast<cudaStream_t>(stream), block_size, small_block_size, mask_id, stop_token, threshold,
+           use_block_cache != 0};
+  const int bs = block_size, sbs = small_block_size;
+  std::vector<int> gen(prompt, prompt + prompt_len);
+  const size_t n0 = gen.size();
+  FDLLM_TRY(d.setup(prompt_len, max_new_tokens));
+  bool kv_valid = false;
+  cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+  bool prefill_marked = false;
+  if (timing_ms) {
+    for (auto& e : ev) CUDA_TRY(cudaEventCreate(&e));
+    CUDA_TRY(cudaEventRecord(ev[0], d.s));
+  }
+  auto mark_prefill = [&]() -> int {
+    if (timing_ms && !prefill_marked) CUDA_TRY(cudaEventRecord(ev[1], d.s));
+    prefill_marked = true;
+    return FDLLM_OK;
+  };
+
+  auto finish = [&](const std::vector<int>& toks) -> int {
+    size_t end = std::min(toks.size(), n0 + static_cast<size_t>(max_new_tokens));
+    int n = 0;
+    for (size_t i = n0; i < end; ++i) {
+      if (toks[i] == mask_id) break;
+      out_tokens[n++] = toks[i];
+    }
+    *n_out = n;
+    if (stats) std::memcpy(stats, d.st, sizeof(d.st));
+    if (timing_ms) {
+      FDLLM_TRY(mark_prefill());
+      CUDA_TRY(cudaEventRecord(ev[2], d.s));
+      CUDA_TRY(cudaEventSynchronize(ev[2]));
+      CUDA_TRY(cudaEventElapsedTime(&timing_ms[0], ev[0], ev[1]));
+      CUDA_TRY(cudaEventElapsedTime(&timing_ms[1], ev[0], ev[2]));
+      for (auto& e : ev) cudaEventDestroy(e);
+    }
+    return FDLLM_OK;
+  };
+
+  if (n0 % bs == 0 && max_new_tokens > 0) {
+    const int lb = static_cast<int>(n0) - bs;
+    FDLLM_TRY(d.prefill(gen.data(), lb));
+    FDLLM_TRY(d.upload_block(gen.data() + lb));
+    FDLLM_TRY(d.forward(0, bs, 0));
+    d.prefix_len += bs;  // commit
+    int nxt = 0;
+    FDLLM_TRY(d.last_token(&nxt));
+    d.st[1] += 1;
+    d.st[3] += 1;
+    gen.push_back(nxt);
+    if (stop_token >= 0 && nxt == stop_token) return finish(gen);
+  }
+
+  while (gen.size() - n0 < static_cast<size_t>(max_new_tokens)) {
+    const size_t plen = gen.size();
+    std::vector<int> x(gen);
+    x.resize(plen + (bs - plen % bs), mask_id);
+    const int a0 = static_cast<int>(x.size()) - bs;
+    if (a0 != d.prefix_len) {
+      FDLLM_TRY(d.prefill(x.data(), a0));
+      kv_valid = false;
+    }
+    FDLLM_TRY(mark_prefill());  // the reference's prefill boundary (runtime.py:741-746)
+    FDLLM_TRY(d.upload_block(x.data() + a0));
+    bool length_done = false;
+    for (int s0 = 0; s0 < bs && !length_done; s0 += sbs) {
+      const int s1 = std::min(bs, s0 + sbs);
+      while (true) {
+        bool any_mask = false;
+        for (int j = s0; j < s1; ++j) any_mask |= (x[a0 + j] == mask_id);
+        if (!any_mask) break;
+        if (has_completed_stop(x, plen, stop_token, mask_id)) return finish(x);
+        const bool partial = d.block_cache && kv_valid && x[a0 + s0] != mask_id;
+        if (partial) {
+          FDLLM_TRY(d.forward(s0, s1 - s0, s0));
+          FDLLM_TRY(d.unmask(s1 - s0, s0, s1 - s0, true, x.data() + a0 + s0));
+          d.st[2] += 1;
+        } else {
+          FDLLM_TRY(d.forward(0, bs, 0));
+          FDLLM_TRY(d.unmask(bs, s0, s1 - s0, false, x.data() + a0 + s0));
+          kv_valid = d.block_cache;
+        }
+        d.st[1] += 1;
+        if (x.size() - n0 >= static_cast<size_t>(max_new_tokens)) {
+          length_done = true;
+          break;
+        }
+      }
+      if (x.size() - n0 >= static_cast<size_t>(max_new_tokens)) length_done = true;
+    }
+    gen = x;
+    if (gen.size() - n0 >= static_cast<size_t>(max_new_tokens)) break;
+    if (has_completed_stop(gen, n0, stop_token, mask_id)) break;
+    // block-append: the completed block is already on the device (the unmask kernel kept it)
+    FDLLM_TRY(d.forward(0, bs, 0));
+    d.prefix_len += bs;
+    int nxt = 0;
+    FDLLM_TRY(d.last_token(&nxt));
+    kv_valid = false;
+    d.st[1] += 1;
+    gen.push_back(nxt);
+    d.st[3] += 1;
+    if (stop_token >= 0 && nxt == stop_token) break;
+  }
+  return finish(gen);
+}

@@ -1,0 +1,345 @@
+// Small kernels around the projections and attention: embedding gather, RMSNorm, RoPE tables,
+// per-call request preparation, confidence / log-softmax reductions and the unmask decision.
+#include <math.h>
+
+#include <atomic>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fdllm {
+
+static std::atomic<long long> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
+
+// ---- embed (model/cuda.py:698-699) ----------------------------------------------------------
+template <typename T>
+__global__ void embed_kernel(const int* __restrict__ ids, const T* __restrict__ table, int vocab, int hidden,
+                             T* __restrict__ out, int* err) {
+  const int i = blockIdx.x;
+  const int id = ids[i];
+  const bool ok = id >= 0 && id < vocab;
+  if (!ok && threadIdx.x == 0) report_error(err, kErrTokenRange);
+  const T* src = table + static_cast<size_t>(ok ? id : 0) * hidden;
+  T* dst = out + static_cast<size_t>(i) * hidden;
+  for (int j = threadIdx.x; j < hidden; j += blockDim.x) dst[j] = ok ? src[j] : from_f<T>(0.f);
+}
+
+int launch_embed(const int* ids, int n, const void* table, int vocab, int hidden, void* out, int dtype, int* err,
+                 cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  if (dtype == 1)
+    embed_kernel<bf16><<<n, 256, 0, s>>>(ids, static_cast<const bf16*>(table), vocab, hidden, static_cast<bf16*>(out), err);
+  else
+    embed_kernel<float><<<n, 256, 0, s>>>(ids, static_cast<const float*>(table), vocab, hidden, static_cast<float*>(out), err);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// ---- RMSNorm (model/cuda.py:269-275): fp32 mean square, rsqrt, cast, then x weight ------------
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < nw; ++w) t += red[w];  // fixed order: deterministic
+  __syncthreads();
+  return t;
+}
+
+template <typename T>
+__global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ out, int hidden,
+                               float eps) {
+  __shared__ float red[32];
+  const T* xr = x + static_cast<size_t>(blockIdx.x) * hidden;
+  T* orow = out + static_cast<size_t>(blockIdx.x) * hidden;
+  float ss = 0.f;
+  for (int j = threadIdx.x; j < hidden; j += blockDim.x) {
+    const float v = to_f<T>(xr[j]);
+    ss = fmaf(v, v, ss);
+  }
+  const float var = block_sum(ss, red) / static_cast<float>(hidden);
+  const float rs = rsqrtf(var + eps);
+  for (int j = threadIdx.x; j < hidden; j += blockDim.x) {
+    const float xn = round_t<T>(to_f<T>(xr[j]) * rs);
+    orow[j] = from_f<T>(to_f<T>(w[j]) * xn);
+  }
+}
+
+int launch_rmsnorm(const void* x, const void* w, void* out, int rows, int hidden, float eps, int dtype,
+                   cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  if (dtype == 1)
+    rmsnorm_kernel<bf16><<<rows, 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w),
+                                              static_cast<bf16*>(out), hidden, eps);
+  else
+    rmsnorm_kernel<float><<<rows, 256, 0, s>>>(static_cast<const float*>(x), static_cast<const float*>(w),
+                                               static_cast<float*>(out), hidden, eps);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// ---- RoPE tables (model/cuda.py:278-300): inv_freq = exp(-ln(theta) * i / half) in fp32 ----------
+template <typename T>
+__global__ void rope_table_kernel(T* cos_t, T* sin_t, int max_pos, int half, float neg_log_theta) {
+  const size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<size_t>(max_pos) * half) return;
+  const int pos = static_cast<int>(idx / half), i = static_cast<int>(idx % half);
+  const float exponent = (neg_log_theta * static_cast<float>(i)) / static_cast<float>(half);
+  const float inv_freq = expf(exponent);
+  const float f = static_cast<float>(pos) * inv_freq;
+  cos_t[idx] = from_f<T>(cosf(f));
+  sin_t[idx] = from_f<T>(sinf(f));
+}
+
+int launch_rope_tables(void* cos_t, void* sin_t, int max_pos, int hd, float theta, int dtype, cudaStream_t s) {
+  const int half = hd / 2;
+  const size_t n = static_cast<size_t>(max_pos) * half;
+  const int blocks = static_cast<int>((n + 255) / 256);
+  const float nl = static_cast<float>(-log(static_cast<double>(theta)));
+  if (dtype == 1)
+    rope_table_kernel<bf16><<<blocks, 256, 0, s>>>(static_cast<bf16*>(cos_t), static_cast<bf16*>(sin_t), max_pos, half, nl);
+  else
+    rope_table_kernel<float><<<blocks, 256, 0, s>>>(static_cast<float*>(cos_t), static_cast<float*>(sin_t), max_pos, half, nl);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// ---- per-call request preparation --------------------------------------------------------------
+__global__ void prepare_kernel(const ReqBatch b, ReqDesc* table, TokenMaps tok, int max_pos, int* err) {
+  const int i = blockIdx.x;
+  if (i >= b.n) return;
+  const ReqDesc r = b.r[i];
+  if (threadIdx.x == 0) table[b.first + i] = r;
+  const int p0 = (r.rope_off != nullptr) ? *r.rope_off : r.rope_base;
+  for (int j = threadIdx.x; j < r.n_q; j += blockDim.x) {
+    const int t = r.q_tok0 + j;
+    int pos = p0 + j;
+    if (pos < 0 || pos >= max_pos) {
+      report_error(err, kErrPositionRange);
+      pos = pos < 0 ? 0 : max_pos - 1;
+    }
+    const int row = r.write_start + j;
+    if (row < 0 || row >= r.cap) report_error(err, kErrCacheRange);
+    tok.req[t] = b.first + i;
+    tok.pos[t] = pos;
+    tok.row[t] = row;
+  }
+}
+
+int launch_prepare(const ReqBatch& b, ReqDesc* dev_table, TokenMaps tok, int max_pos, int* err, cudaStream_t s) {
+  if (b.n <= 0) return cudaSuccess;
+  prepare_kernel<<<b.n, 128, 0, s>>>(b, dev_table, tok, max_pos, err);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// ---- confidence (model/metal.py:316-374): first-index argmax, maxp = 1 / sum exp(l - max) -------
+struct Top {
+  float m;
+  int i;
+  float s;
+};
+
+__device__ __forceinline__ Top merge_top(Top a, Top b) {
+  Top r;
+  r.m = fmaxf(a.m, b.m);
+  r.i = (a.m > b.m) ? a.i : ((b.m > a.m) ? b.i : min(a.i, b.i));
+  const float sa = (a.m == -INFINITY) ? 0.f : a.s * expf(a.m - r.m);
+  const float sb = (b.m == -INFINITY) ? 0.f : b.s * expf(b.m - r.m);
+  r.s = sa + sb;
+  return r;
+}
+
+__device__ __forceinline__ Top warp_merge(Top t) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    Top o;
+    o.m = __shfl_xor_sync(0xffffffffu, t.m, off);
+    o.i = __shfl_xor_sync(0xffffffffu, t.i, off);
+    o.s = __shfl_xor_sync(0xffffffffu, t.s, off);
+    t = merge_top(t, o);
+  }
+  return t;
+}
+
+// Partials from the fused lm_head epilogue: [rows, n_slabs, 4] = (max, argmax bits, sum, target).
+__global__ void conf_combine_kernel(const float* __restrict__ part, int rows, int n_slabs, int* ids, float* maxp) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (row >= rows) return;
+  Top t{-INFINITY, 0x7fffffff, 0.f};
+  for (int sl = lane; sl < n_slabs; sl += 32) {
+    const float* p = part + (static_cast<size_t>(row) * n_slabs + sl) * 4;
+    t = merge_top(t, Top{p[0], __float_as_int(p[1]), p[2]});
+  }
+  t = warp_merge(t);
+  if (lane == 0) {
+    ids[row] = t.i;
+    maxp[row] = 1.0f / t.s;
+  }
+}
+
+int launch_conf_combine(const float* part, int rows, int n_slabs, int* ids, float* maxp, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  conf_combine_kernel<<<(rows + 7) / 8, 256, 0, s>>>(part, rows, n_slabs, ids, maxp);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// The same reduction over materialised fp32 logits [rows, vocab] (three passes per row).
+__global__ void conf_logits_kernel(const float* __restrict__ logits, int vocab, int* ids, float* maxp) {
+  __shared__ float red_m[32];
+  __shared__ int red_i[32];
+  __shared__ float red_s[32];
+  const float* l = logits + static_cast<size_t>(blockIdx.x) * vocab;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  float m = -INFINITY;
+  int mi = 0x7fffffff;
+  for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+    const float v = l[j];
+    if (v > m) { m = v; mi = j; }  // ascending j per thread: first index kept on ties
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, mi, off);
+    if (om > m || (om == m && oi < mi)) { m = om; mi = oi; }
+  }
+  if (lane == 0) { red_m[warp] = m; red_i[warp] = mi; }
+  __syncthreads();
+  m = red_m[0];
+  mi = red_i[0];
+  for (int w = 1; w < nw; ++w)
+    if (red_m[w] > m || (red_m[w] == m && red_i[w] < mi)) { m = red_m[w]; mi = red_i[w]; }
+  float s = 0.f;
+  for (int j = threadIdx.x; j < vocab; j += blockDim.x) s += expf(l[j] - m);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) red_s[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < nw; ++w) tot += red_s[w];
+    ids[blockIdx.x] = mi;
+    maxp[blockIdx.x] = 1.0f / tot;
+  }
+}
+
+int launch_conf_from_logits(const float* logits, int rows, int vocab, int* ids, float* maxp, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  conf_logits_kernel<<<rows, 512, 0, s>>>(logits, vocab, ids, maxp);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// log_softmax(logits)[target] per row from the fused partials (runners.py:877-881 on the device).
+__global__ void lse_combine_kernel(const float* __restrict__ part, int rows, int n_slabs, float* logprob) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (row >= rows) return;
+  Top t{-INFINITY, 0x7fffffff, 0.f};
+  float tgt = 0.f;
+  for (int sl = lane; sl < n_slabs; sl += 32) {
+    const float* p = part + (static_cast<size_t>(row) * n_slabs + sl) * 4;
+    t = merge_top(t, Top{p[0], __float_as_int(p[1]), p[2]});
+    tgt += p[3];  // exactly one slab holds the target's logit, the others hold 0
+  }
+  t = warp_merge(t);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) tgt += __shfl_xor_sync(0xffffffffu, tgt, off);
+  if (lane == 0) logprob[row] = tgt - (t.m + logf(t.s));
+}
+
+int launch_lse_combine(const float* part, int rows, int n_slabs, float* logprob, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  lse_combine_kernel<<<(rows + 7) / 8, 256, 0, s>>>(part, rows, n_slabs, logprob);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// ---- unmask decision (runtime.py:158-181 shift, 794-805 rule), one warp ------------------------
+// ids / maxp: unshifted per-row argmax and confidence of `rows` hidden rows.  Row i of the block
+// window takes row i-1's prediction (row 0 its own).  Full steps read the window
+// [sub_start, sub_start+sub_len) of the shifted rows; partial steps use all `rows` (= sub_len).
+// Masked positions whose confidence exceeds the threshold are unmasked; if none does, the first
+// masked position with the largest confidence is.  `block` (the active block's token ids) is
+// updated in place.  status[0] = masks left in the window, status[1] = positions unmasked.
+__global__ void unmask_kernel(const int* __restrict__ ids, const float* __restrict__ maxp, int rows, int* block,
+                              int sub_start, int sub_len, int partial, int mask_id, double threshold, int* out_tok,
+                              float* out_conf, int* out_unmask, int* status) {
+  const int j = threadIdx.x;  // window position
+  const bool in = j < sub_len;
+  int tok = 0;
+  float conf = -INFINITY;
+  bool masked = false;
+  if (in) {
+    const int src_row = partial ? j : sub_start + j;       // row of the shifted array
+    const int row = src_row > 0 ? src_row - 1 : 0;          // its unshifted source row
+    if (row < rows) {
+      tok = ids[row];
+      conf = maxp[row];
+    }
+    masked = block[sub_start + j] == mask_id;
+  }
+  const bool above = masked && static_cast<double>(conf) > threshold;
+  const unsigned any_above = __ballot_sync(0xffffffffu, above);
+  bool take = above;
+  if (any_above == 0u) {
+    // first masked position with the largest confidence (np.argmax over the masked list)
+    float best = masked ? conf : -INFINITY;
+    int best_j = masked ? j : 0x7fffffff;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+      const int oj = __shfl_xor_sync(0xffffffffu, best_j, off);
+      if (ob > best || (ob == best && oj < best_j)) { best = ob; best_j = oj; }
+    }
+    take = masked && (j == best_j);
+  }
+  if (in) {
+    if (take) block[sub_start + j] = tok;
+    if (out_tok) out_tok[j] = tok;
+    if (out_conf) out_conf[j] = conf;
+    if (out_unmask) out_unmask[j] = take ? 1 : 0;
+  }
+  const unsigned left = __ballot_sync(0xffffffffu, masked && !take);
+  const unsigned took = __ballot_sync(0xffffffffu, take);
+  if (j == 0 && status) {
+    status[0] = __popc(left);
+    status[1] = __popc(took);
+  }
+}
+
+int launch_unmask(const int* ids, const float* maxp, int rows, int* block, int sub_start, int sub_len, int partial,
+                  int mask_id, double threshold, int* out_tok, float* out_conf, int* out_unmask, int* status,
+                  cudaStream_t s) {
+  if (sub_len <= 0 || sub_len > 32) return cudaErrorInvalidValue;
+  unmask_kernel<<<1, 32, 0, s>>>(ids, maxp, rows, block, sub_start, sub_len, partial, mask_id,
+                                 threshold, out_tok, out_conf, out_unmask, status);
+  count_launch();
+  return cudaGetLastError();
+}
+
+// ---- bounded-wait self test: spin on a flag that nothing sets; give up and report ----------
+__global__ void wait_test_kernel(const volatile int* flag, int* err, unsigned long long limit_ns) {
+  const uint64_t t0 = global_timer_ns();
+  while (*flag == 0) {
+    if (global_timer_ns() - t0 > limit_ns) {
+      report_error(err, kErrTimeoutTest);
+      return;
+    }
+    __nanosleep(1000);
+  }
+}
+
+int launch_wait_test(int* flag, int* err, unsigned long long limit_ns, cudaStream_t s) {
+  wait_test_kernel<<<1, 1, 0, s>>>(flag, err, limit_ns);
+  count_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace fdllm

@@ -1,0 +1,137 @@
+// Internal host-side state of a library handle, shared by model.cu and decode.cu.
+#pragma once
+
+#include <algorithm>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/fdllm_sm100.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace fdllm {
+
+int fail(int code, const std::string& msg);
+
+#define CUDA_TRY(expr)                                                                       \
+  do {                                                                                       \
+    cudaError_t _e = static_cast<cudaError_t>(expr);                                         \
+    if (_e != cudaSuccess)                                                                   \
+      return ::fdllm::fail(FDLLM_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
+  } while (0)
+
+#define FDLLM_TRY(expr)            \
+  do {                             \
+    int _r = (expr);               \
+    if (_r != FDLLM_OK) return _r; \
+  } while (0)
+
+// ---- handle ------------------------------------------------------------------------------
+struct Weight {
+  const void* ptr = nullptr;
+  int rows = 0, cols = 0;
+  bool paired = false;
+  CUtensorMap map{};
+};
+
+struct LayerW {
+  Weight qkv, o, gu, down;
+  const void* qkv_b = nullptr;
+  const void* ln1 = nullptr;
+  const void* ln2 = nullptr;
+};
+
+template <typename P>
+struct DevBuf {
+  P* p = nullptr;
+  size_t n = 0;  // elements
+  int ensure(size_t want, bool zero = false) {
+    if (want <= n) return FDLLM_OK;
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+    size_t cap = std::max<size_t>(want, 256);
+    cudaError_t e = cudaMalloc(&p, cap * sizeof(P));
+    if (e != cudaSuccess) return fail(FDLLM_ERR_CUDA, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+    if (zero) {
+      e = cudaMemset(p, 0, cap * sizeof(P));
+      if (e != cudaSuccess) return fail(FDLLM_ERR_CUDA, std::string("cudaMemset: ") + cudaGetErrorString(e));
+    }
+    n = cap;
+    return FDLLM_OK;
+  }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    n = 0;
+  }
+  size_t bytes() const { return n * sizeof(P); }
+};
+
+struct DecodeState {
+  DevBuf<uint8_t> k, v;        // caches of the native driver
+  DevBuf<int> ids;             // prefill / block token ids
+  DevBuf<int> block;           // active block ids (bd_size)
+  DevBuf<uint8_t> x, hid;      // embeddings in / hidden out
+  DevBuf<int> cids;            // confidence ids
+  DevBuf<float> cmax;          // confidence values
+  DevBuf<int> out;             // [0..1] status, [2..] window tokens, then unmask flags
+  int* host = nullptr;         // pinned read-back buffer
+};
+
+}  // namespace fdllm
+
+using fdllm::DecodeState;
+using fdllm::DevBuf;
+using fdllm::LayerW;
+using fdllm::ReqDesc;
+using fdllm::Weight;
+
+struct fdllm_handle {
+  fdllm_config cfg{};
+  int device = 0;
+  int dtype = FDLLM_BFLOAT16;
+  size_t esz = 2;
+  int num_sms = 148;
+  bool bound = false;
+  std::mutex mu;
+
+  const void* embed = nullptr;
+  const void* final_norm = nullptr;
+  Weight lm;
+  std::vector<LayerW> layers;
+
+  DevBuf<uint8_t> rope_cos, rope_sin;
+  DevBuf<int> err;
+
+  // workspace (grown on demand; never inside a captured region)
+  DevBuf<uint8_t> h, xn, q, attn, act, scratch_k, scratch_v;
+  DevBuf<int> tok_req, tok_pos, tok_row, tmp_ids, targets;
+  DevBuf<ReqDesc> reqs;
+  DevBuf<float> splitk, attn_po, attn_pl, conf_part, tmp_maxp;
+  DevBuf<int> counters;
+  DecodeState dec;
+
+  // per-launch CUDA-event timing of the projection GEMM (fdllm_profile_enable / _read)
+  bool prof = false;
+  std::vector<cudaEvent_t> prof_ev;
+  size_t prof_used = 0;
+  double prof_bytes = 0.0, prof_flops = 0.0;
+};
+
+
+namespace fdllm {
+
+size_t round_up(size_t x, size_t m);
+long long layer_stride(const fdllm_handle* h, int cap);
+int check_handle(fdllm_handle* h);
+int forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDesc>& reqs, const float* bias, int ld_bias,
+                 int causal_block, void* out, cudaStream_t s);
+int dense_forward(fdllm_handle* h, const void* x, const float* bias, int T, void* k, void* v, int cap, bool scratch,
+                  void* out, cudaStream_t s);
+int cached_desc(fdllm_handle* h, const fdllm_request& r, int q_tok0, ReqDesc* d);
+int confidence_locked(fdllm_handle* h, const void* hidden, int rows, int32_t* ids, float* maxp,
+                      const int32_t* targets, float* logprob, cudaStream_t s);
+
+}  // namespace fdllm

@@ -1,0 +1,130 @@
+// Kernel-facing structures and launcher declarations shared by the .cu files of the library.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fdllm {
+
+// One request of a (possibly batched) forward call, as the device sees it.  Token rows of all
+// requests are concatenated: request r owns activation rows [q_tok0, q_tok0 + n_q).
+struct ReqDesc {
+  void* k;                  // KV cache base [layers, 1, cap, kv_heads, head_dim] (or a per-layer scratch)
+  void* v;
+  long long layer_stride;   // elements between consecutive layers of k / v (0 for a per-layer scratch)
+  int cap;                  // cache rows
+  int q_tok0;               // first activation row of this request
+  int n_q;                  // activation rows (tokens) of this request
+  int write_start;          // cache row that receives token 0's K/V
+  int attend_len;           // attention keys are cache rows [0, attend_len)
+  int rope_base;            // RoPE position of token 0 when rope_off is null
+  const int* rope_off;      // device int32 position of token 0 (the reference's cache_offset), or null
+  int pad;
+};
+
+constexpr int kMaxReqsPerLaunch = 48;  // keeps ReqBatch under the classic 4 KB parameter limit
+
+struct ReqBatch {
+  ReqDesc r[kMaxReqsPerLaunch];
+  int n;
+  int first;  // index of r[0] in the device request table
+};
+
+// Per-token data derived from the requests once per forward call (prepare kernel).
+struct TokenMaps {
+  int* req;    // [M] request index
+  int* pos;    // [M] RoPE position
+  int* row;    // [M] cache row receiving this token's K/V
+};
+
+enum EpiKind : int {
+  kEpiStore = 0,      // out[t, f] = T(acc)
+  kEpiQkvRope = 1,    // + bias, RoPE on q/k, q -> qout, k/v -> caches (per-token rows)
+  kEpiResidual = 2,   // resid[t, f] = T(resid + T(acc))
+  kEpiSiluMul = 3,    // paired gate/up slab: out[t, j] = T(T(silu(T(gate))) * T(up))
+  kEpiLogitsF32 = 4,  // out_f32[t, f] = float(T(acc))
+  kEpiConf = 5,       // per (token, slab): max, first argmax, sum exp(v - max) of float(T(acc))
+  kEpiLseGather = 6,  // kEpiConf plus the logit of a per-token target id
+};
+
+struct Epilogue {
+  int kind;
+  int layer;
+  void* out;                // Store / SiluMul: [M, ld_out] in T; LogitsF32: float [M, ld_out]
+  int ld_out;
+  const void* bias;         // QkvRope: [N] in T
+  void* resid;              // Residual: [M, ld_resid] in T
+  int ld_resid;
+  // QkvRope
+  void* qout;               // [M, hq*hd] in T
+  const void* rope_cos;     // [max_pos, hd/2] in T
+  const void* rope_sin;
+  int max_pos;
+  int hq, hkv, hd;
+  const ReqDesc* reqs;      // device request table
+  TokenMaps tok;
+  // Conf / LseGather
+  float* part;              // [M, n_slabs, 4]: max, argmax (as int bits), sum exp, target logit
+  const int* target;        // LseGather: [M] target ids
+};
+
+struct GemmArgs {
+  int M, N, K;              // tokens, output features (weight rows), reduction
+  int paired;               // gate/up pairing (N = 2*I; slab s covers rows [64s, 64s+64) and I + same)
+  int n_slabs;              // N / 128 (or I / 64 when paired)
+  int n_tok_tiles;
+  int splits;               // split-K factor
+  int kb_per_split;         // 64-wide k blocks per split
+  float* partials;          // split-K workspace
+  int* counters;            // split-K arrival counters [n_slabs * n_tok_tiles] (self-resetting)
+  int* err;
+  Epilogue epi;
+};
+
+struct AttnArgs {
+  const void* q;            // [M, hq*hd] in T
+  void* out;                // [M, hq*hd] in T
+  const ReqDesc* reqs;      // device request table
+  int n_reqs;
+  int layer;
+  int hq, hkv, hd;
+  float scale;
+  const float* bias;        // dense path: [n_q, ld_bias] fp32 additive bias of request 0, or null
+  int ld_bias;
+  int causal_block;         // > 0 and bias null: implicit block-causal mask (query block >= key block)
+  int n_splits;             // key splits per (request, kv head, q tile)
+  int split_len;            // keys per split (multiple of 64)
+  float* part_o;            // [n_splits, M, hq, hd]
+  float* part_lse;          // [n_splits, M, hq]
+  int m_total;              // M: activation rows of all requests
+  int* err;
+};
+
+// ---- launch accounting ---------------------------------------------------------------------
+void count_launch(int n = 1);
+long long launch_count();
+
+// ---- launchers (return a cudaError_t) --------------------------------------------------------
+int launch_gemm_tc(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int nt, cudaStream_t s);
+int launch_gemm_simt_f32(const GemmArgs& a, const float* W, const float* X, cudaStream_t s);
+int gemm_tc_smem_bytes(int nt);
+int gemm_tc_stages(int nt);
+
+int launch_attention(const AttnArgs& a, int max_q, int dtype, cudaStream_t s);
+
+int launch_embed(const int* ids, int n, const void* table, int vocab, int hidden, void* out, int dtype, int* err,
+                 cudaStream_t s);
+int launch_rmsnorm(const void* x, const void* w, void* out, int rows, int hidden, float eps, int dtype,
+                   cudaStream_t s);
+int launch_rope_tables(void* cos_t, void* sin_t, int max_pos, int hd, float theta, int dtype, cudaStream_t s);
+int launch_prepare(const ReqBatch& b, ReqDesc* dev_table, TokenMaps tok, int max_pos, int* err, cudaStream_t s);
+int launch_conf_combine(const float* part, int rows, int n_slabs, int* ids, float* maxp, cudaStream_t s);
+int launch_conf_from_logits(const float* logits, int rows, int vocab, int* ids, float* maxp, cudaStream_t s);
+int launch_lse_combine(const float* part, int rows, int n_slabs, float* logprob, cudaStream_t s);
+int launch_unmask(const int* ids, const float* maxp, int rows, int* block, int sub_start, int sub_len,
+                  int partial, int mask_id, double threshold, int* out_tok, float* out_conf, int* out_unmask,
+                  int* status, cudaStream_t s);
+int launch_wait_test(int* flag, int* err, unsigned long long limit_ns, cudaStream_t s);
+
+}  // namespace fdllm

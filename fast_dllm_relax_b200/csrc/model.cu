@@ -1,0 +1,677 @@
+// Host runtime of the sm_100a library: the handle (device, config, bound parameters, TMA
+// descriptors, RoPE tables, workspace), the layer schedule of the nine entry points, the batched
+// cached forward, the device-side confidence / unmask path, the device-resident decode driver and
+// the C ABI declared in include/fdllm_sm100.h.
+//
+// Layer schedule (model/cuda.py:545-579, 639-666), one launch each:
+//   rmsnorm(h) -> qkv GEMM [+bias, RoPE, K/V append] -> attention -> o GEMM [+= h]
+//   -> rmsnorm(h) -> gate_up GEMM [SiLU * up] -> down GEMM [+= h]
+// then the final rmsnorm.  Nothing returns to the host between layers.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "handle.h"
+
+using namespace fdllm;
+
+// ---- error plumbing ------------------------------------------------------------------------
+static thread_local std::string g_last_error;
+
+int fdllm::fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  // Consume the runtime's per-thread error state so that a failed call is not reported again by the
+  // next launch's cudaGetLastError() (sticky device faults stay visible regardless).
+  if (code == FDLLM_ERR_CUDA) (void)cudaGetLastError();
+  return code;
+}
+
+// ---- TMA descriptor encoding (driver entry point fetched through the runtime) ----------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2D bf16 [rows, cols] row-major tensor, box of box_rows x 64 columns, 128-byte swizzle.
+static int make_map(CUtensorMap* map, const void* base, int rows, int cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(FDLLM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return fail(FDLLM_ERR_INVALID, "TMA base must be 16-byte aligned");
+  if (cols % 64 != 0) return fail(FDLLM_ERR_UNSUPPORTED, "GEMM reduction dim must be a multiple of 64");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FDLLM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return FDLLM_OK;
+}
+
+size_t fdllm::round_up(size_t x, size_t m) { return (x + m - 1) / m * m; }
+
+// ---- GEMM dispatch -------------------------------------------------------------------------
+static int pick_nt(int M) {
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  return 256;
+}
+
+// Events for one profiled launch (reused across reads).
+static int prof_events(fdllm_handle* h, cudaEvent_t* e0, cudaEvent_t* e1) {
+  while (h->prof_ev.size() < h->prof_used + 2) {
+    cudaEvent_t e;
+    CUDA_TRY(cudaEventCreate(&e));
+    h->prof_ev.push_back(e);
+  }
+  *e0 = h->prof_ev[h->prof_used];
+  *e1 = h->prof_ev[h->prof_used + 1];
+  h->prof_used += 2;
+  return FDLLM_OK;
+}
+
+// Algorithmic HBM bytes of one projection launch: weights + activations in + outputs.
+static double gemm_bytes(const fdllm_handle* h, const GemmArgs& g) {
+  const double e = static_cast<double>(h->esz);
+  double out = 0.0;
+  switch (g.epi.kind) {
+    case kEpiSiluMul: out = static_cast<double>(g.M) * (g.N / 2) * e; break;
+    case kEpiResidual: out = 2.0 * g.M * g.N * e; break;
+    case kEpiLogitsF32: out = 4.0 * g.M * g.N; break;
+    case kEpiConf:
+    case kEpiLseGather: out = 16.0 * g.M * g.n_slabs; break;
+    default: out = static_cast<double>(g.M) * g.N * e; break;
+  }
+  return static_cast<double>(g.N) * g.K * e + static_cast<double>(g.M) * g.K * e + out;
+}
+
+static int timed_launch(fdllm_handle* h, const GemmArgs& g, cudaStream_t s, int (*launch)(const GemmArgs&, const void*, const void*, int, cudaStream_t),
+                        const void* a0, const void* a1, int nt) {
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (h->prof) {
+    FDLLM_TRY(prof_events(h, &e0, &e1));
+    CUDA_TRY(cudaEventRecord(e0, s));
+  }
+  CUDA_TRY(launch(g, a0, a1, nt, s));
+  if (h->prof) {
+    CUDA_TRY(cudaEventRecord(e1, s));
+    h->prof_bytes += gemm_bytes(h, g);
+    h->prof_flops += 2.0 * g.M * static_cast<double>(g.N) * g.K;
+  }
+  return FDLLM_OK;
+}
+
+static int launch_tc_thunk(const GemmArgs& g, const void* a, const void* b, int nt, cudaStream_t s) {
+  return launch_gemm_tc(g, *static_cast<const CUtensorMap*>(a), *static_cast<const CUtensorMap*>(b), nt, s);
+}
+
+static int launch_simt_thunk(const GemmArgs& g, const void* w, const void* x, int, cudaStream_t s) {
+  return launch_gemm_simt_f32(g, static_cast<const float*>(w), static_cast<const float*>(x), s);
+}
+
+static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epilogue epi, cudaStream_t s) {
+  GemmArgs g{};
+  g.M = M;
+  g.N = w.rows;
+  g.K = w.cols;
+  g.paired = w.paired ? 1 : 0;
+  g.err = h->err.p;
+  g.epi = epi;
+  if (M <= 0) return FDLLM_OK;
+  if (h->dtype == FDLLM_FLOAT32) {
+    g.n_slabs = w.paired ? (g.N / 2 + 63) / 64 : (g.N + 127) / 128;
+    g.n_tok_tiles = (M + 31) / 32;
+    g.splits = 1;
+    g.kb_per_split = 0;
+    if (epi.kind == kEpiConf || epi.kind == kEpiLseGather) g.n_slabs = (g.N + 127) / 128;
+    return timed_launch(h, g, s, launch_simt_thunk, w.ptr, X, 0);
+  }
+  const int nt = pick_nt(M);
+  g.n_tok_tiles = (M + nt - 1) / nt;
+  g.n_slabs = w.paired ? (g.N / 2) / 64 : g.N / 128;
+  const int kblocks = g.K / 64;
+  const int tiles = g.n_slabs * g.n_tok_tiles;
+  int splits = 1;
+  if (tiles < h->num_sms) {
+    splits = std::max(1, std::min(kblocks, h->num_sms / tiles));
+    const int kpb = (kblocks + splits - 1) / splits;
+    splits = (kblocks + kpb - 1) / kpb;
+  }
+  g.splits = splits;
+  g.kb_per_split = (kblocks + splits - 1) / splits;
+  if (splits > 1) {
+    FDLLM_TRY(h->splitk.ensure(static_cast<size_t>(tiles) * splits * nt * 128));
+    FDLLM_TRY(h->counters.ensure(static_cast<size_t>(tiles), true));
+    g.partials = h->splitk.p;
+    g.counters = h->counters.p;
+  }
+  CUtensorMap tmB;
+  FDLLM_TRY(make_map(&tmB, X, M, g.K, nt));
+  return timed_launch(h, g, s, launch_tc_thunk, &w.map, &tmB, nt);
+}
+
+// ---- workspace ----------------------------------------------------------------------------
+static int ensure_ws(fdllm_handle* h, int M, int nreq) {
+  const fdllm_config& c = h->cfg;
+  const size_t m = round_up(static_cast<size_t>(std::max(M, 1)), 64);
+  const size_t qd = static_cast<size_t>(c.num_attention_heads) * c.head_dim;
+  FDLLM_TRY(h->h.ensure(m * c.hidden_size * h->esz));
+  FDLLM_TRY(h->xn.ensure(m * std::max<size_t>(c.hidden_size, c.intermediate_size) * h->esz));
+  FDLLM_TRY(h->q.ensure(m * qd * h->esz));
+  FDLLM_TRY(h->attn.ensure(m * qd * h->esz));
+  FDLLM_TRY(h->act.ensure(m * c.intermediate_size * h->esz));
+  FDLLM_TRY(h->tok_req.ensure(m));
+  FDLLM_TRY(h->tok_pos.ensure(m));
+  FDLLM_TRY(h->tok_row.ensure(m));
+  FDLLM_TRY(h->tmp_ids.ensure(m));
+  FDLLM_TRY(h->tmp_maxp.ensure(m));
+  FDLLM_TRY(h->targets.ensure(m));
+  FDLLM_TRY(h->reqs.ensure(static_cast<size_t>(std::max(nreq, 1))));
+  return FDLLM_OK;
+}
+
+static TokenMaps token_maps(fdllm_handle* h) { return TokenMaps{h->tok_req.p, h->tok_pos.p, h->tok_row.p}; }
+
+// ---- the layer stack ----------------------------------------------------------------------
+// x: [M, hidden] input embeddings; reqs: host descriptors (q_tok0 / n_q filled); bias: dense fp32
+// bias of request 0 (or null), causal_block: implicit block-causal mask when bias is null.
+int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDesc>& reqs, const float* bias,
+                        int ld_bias, int causal_block, void* out, cudaStream_t s) {
+  const fdllm_config& c = h->cfg;
+  const int nreq = static_cast<int>(reqs.size());
+  FDLLM_TRY(ensure_ws(h, M, nreq));
+  for (int first = 0; first < nreq; first += kMaxReqsPerLaunch) {
+    ReqBatch b{};
+    b.n = std::min(kMaxReqsPerLaunch, nreq - first);
+    b.first = first;
+    for (int i = 0; i < b.n; ++i) b.r[i] = reqs[first + i];
+    CUDA_TRY(launch_prepare(b, h->reqs.p, token_maps(h), c.max_positions, h->err.p, s));
+  }
+  const size_t row_bytes = static_cast<size_t>(c.hidden_size) * h->esz;
+  CUDA_TRY(cudaMemcpyAsync(h->h.p, x, M * row_bytes, cudaMemcpyDeviceToDevice, s));
+
+  int max_q = 0, max_l = 0;
+  for (const ReqDesc& r : reqs) {
+    max_q = std::max(max_q, r.n_q);
+    max_l = std::max(max_l, r.attend_len);
+  }
+  // key splits for the attention: enough CTAs to cover the SMs at small batch
+  const int qtiles = (max_q + 15) / 16;
+  const int base_ctas = qtiles * c.num_key_value_heads * nreq;
+  int n_splits = 1, split_len = std::max(64, static_cast<int>(round_up(std::max(max_l, 1), 64)));
+  if (h->dtype == FDLLM_BFLOAT16 && bias == nullptr && causal_block == 0 && base_ctas < h->num_sms) {
+    const int want = std::min((2 * h->num_sms + base_ctas - 1) / base_ctas, (max_l + 63) / 64);
+    if (want > 1) {
+      split_len = static_cast<int>(round_up((max_l + want - 1) / want, 64));
+      n_splits = (max_l + split_len - 1) / split_len;
+    }
+  }
+  if (n_splits > 1) {
+    FDLLM_TRY(h->attn_po.ensure(static_cast<size_t>(n_splits) * M * c.num_attention_heads * c.head_dim));
+    FDLLM_TRY(h->attn_pl.ensure(static_cast<size_t>(n_splits) * M * c.num_attention_heads));
+  }
+
+  Epilogue base{};
+  base.hq = c.num_attention_heads;
+  base.hkv = c.num_key_value_heads;
+  base.hd = c.head_dim;
+  base.reqs = h->reqs.p;
+  base.tok = token_maps(h);
+  base.rope_cos = h->rope_cos.p;
+  base.rope_sin = h->rope_sin.p;
+  base.max_pos = c.max_positions;
+
+  for (int l = 0; l < c.num_hidden_layers; ++l) {
+    const LayerW& L = h->layers[l];
+    CUDA_TRY(launch_rmsnorm(h->h.p, L.ln1, h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s));
+    Epilogue e = base;
+    e.kind = kEpiQkvRope;
+    e.layer = l;
+    e.bias = L.qkv_b;
+    e.qout = h->q.p;
+    FDLLM_TRY(run_gemm(h, L.qkv, h->xn.p, M, e, s));
+
+    AttnArgs a{};
+    a.q = h->q.p;
+    a.out = h->attn.p;
+    a.reqs = h->reqs.p;
+    a.n_reqs = nreq;
+    a.layer = l;
+    a.hq = c.num_attention_heads;
+    a.hkv = c.num_key_value_heads;
+    a.hd = c.head_dim;
+    a.scale = 1.0f / std::sqrt(static_cast<float>(c.head_dim));
+    a.bias = bias;
+    a.ld_bias = ld_bias;
+    a.causal_block = causal_block;
+    a.n_splits = n_splits;
+    a.split_len = split_len;
+    a.part_o = h->attn_po.p;
+    a.part_lse = h->attn_pl.p;
+    a.m_total = M;
+    a.err = h->err.p;
+    CUDA_TRY(launch_attention(a, max_q, h->dtype, s));
+
+    e = base;
+    e.kind = kEpiResidual;
+    e.resid = h->h.p;
+    e.ld_resid = c.hidden_size;
+    FDLLM_TRY(run_gemm(h, L.o, h->attn.p, M, e, s));
+
+    CUDA_TRY(launch_rmsnorm(h->h.p, L.ln2, h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s));
+    e = base;
+    e.kind = kEpiSiluMul;
+    e.out = h->act.p;
+    e.ld_out = c.intermediate_size;
+    FDLLM_TRY(run_gemm(h, L.gu, h->xn.p, M, e, s));
+
+    e = base;
+    e.kind = kEpiResidual;
+    e.resid = h->h.p;
+    e.ld_resid = c.hidden_size;
+    FDLLM_TRY(run_gemm(h, L.down, h->act.p, M, e, s));
+  }
+  // out == null (build_prefix_cache): the final hidden states are not needed; xn is free by now.
+  CUDA_TRY(launch_rmsnorm(h->h.p, h->final_norm, out ? out : h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s));
+  return FDLLM_OK;
+}
+
+long long fdllm::layer_stride(const fdllm_handle* h, int cap) {
+  return static_cast<long long>(cap) * h->cfg.num_key_value_heads * h->cfg.head_dim;
+}
+
+int fdllm::check_handle(fdllm_handle* h) {
+  if (h == nullptr) return fail(FDLLM_ERR_INVALID, "null handle");
+  if (!h->bound) return fail(FDLLM_ERR_UNBOUND, "parameters are not bound (call fdllm_bind_params)");
+  cudaError_t e = cudaSetDevice(h->device);
+  if (e != cudaSuccess) return fail(FDLLM_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+  return FDLLM_OK;
+}
+
+// Validate one cached request (runtime.py:56-57, 69-70, 258-263) and fill its descriptor.
+int fdllm::cached_desc(fdllm_handle* h, const fdllm_request& r, int q_tok0, ReqDesc* d) {
+  if (r.rows <= 0) return fail(FDLLM_ERR_INVALID, "rows must be positive");
+  if (r.k_cache == nullptr || r.v_cache == nullptr) return fail(FDLLM_ERR_INVALID, "null KV cache");
+  const long long write_start = static_cast<long long>(r.prefix_len) + r.write_rel;
+  const long long attend_len = static_cast<long long>(r.prefix_len) + r.attend_rel;
+  if (r.prefix_len < 0 || write_start < 0 || write_start + r.rows > r.cap)
+    return fail(FDLLM_ERR_INVALID, "KV write [" + std::to_string(write_start) + ", " +
+                                       std::to_string(write_start + r.rows) + ") outside cache capacity " +
+                                       std::to_string(r.cap));
+  if (write_start + r.rows > attend_len)
+    return fail(FDLLM_ERR_INVALID, "KV write [" + std::to_string(write_start) + ", " +
+                                       std::to_string(write_start + r.rows) + ") past the attended rows [0, " +
+                                       std::to_string(attend_len) + ")");
+  if (attend_len > r.cap)
+    return fail(FDLLM_ERR_INVALID, "cached call needs " + std::to_string(attend_len) +
+                                       " rows; cache capacity is " + std::to_string(r.cap));
+  if (r.cache_offset_dev == nullptr &&
+      (r.cache_offset_host < 0 || r.cache_offset_host + r.rows > h->cfg.max_positions))
+    return fail(FDLLM_ERR_INVALID, "RoPE positions exceed max_positions");
+  ReqDesc x{};
+  x.k = r.k_cache;
+  x.v = r.v_cache;
+  x.layer_stride = layer_stride(h, r.cap);
+  x.cap = r.cap;
+  x.q_tok0 = q_tok0;
+  x.n_q = r.rows;
+  x.write_start = static_cast<int>(write_start);
+  x.attend_len = static_cast<int>(attend_len);
+  x.rope_base = r.cache_offset_host;
+  x.rope_off = r.cache_offset_dev;
+  *d = x;
+  return FDLLM_OK;
+}
+
+// ---- the C ABI ---------------------------------------------------------------------------
+extern "C" {
+
+int fdllm_abi_version(void) { return FDLLM_ABI_VERSION; }
+
+const char* fdllm_last_error(void) { return g_last_error.c_str(); }
+
+int fdllm_create(const fdllm_config* cfg, int device, fdllm_handle** out) {
+  if (cfg == nullptr || out == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
+  *out = nullptr;
+  const fdllm_config& c = *cfg;
+  if (c.dtype != FDLLM_FLOAT32 && c.dtype != FDLLM_BFLOAT16) return fail(FDLLM_ERR_UNSUPPORTED, "dtype must be fp32 or bf16");
+  if (c.hidden_size <= 0 || c.num_hidden_layers <= 0 || c.num_attention_heads <= 0 || c.num_key_value_heads <= 0 ||
+      c.num_attention_heads % c.num_key_value_heads != 0 || c.head_dim % 32 != 0 || c.head_dim > 128)
+    return fail(FDLLM_ERR_UNSUPPORTED, "unsupported head layout (head_dim must be 32/64/96/128, heads % kv_heads == 0)");
+  if (c.max_positions <= 0 || c.bd_size <= 0 || c.bd_size > 32) return fail(FDLLM_ERR_INVALID, "bad max_positions / bd_size");
+  const int qkv = (c.num_attention_heads + 2 * c.num_key_value_heads) * c.head_dim;
+  if (c.dtype == FDLLM_BFLOAT16) {
+    if (c.hidden_size % 128 || qkv % 128 || c.intermediate_size % 128 || c.vocab_size % 128 ||
+        (c.num_attention_heads * c.head_dim) % 128 || 128 % c.head_dim)
+      return fail(FDLLM_ERR_UNSUPPORTED, "bf16 tcgen05 path needs hidden, qkv, intermediate and vocab sizes "
+                                         "divisible by 128 and head_dim dividing 128");
+  } else if (c.hidden_size % 32 || c.intermediate_size % 32 || (c.num_attention_heads * c.head_dim) % 32 ||
+             qkv % 128 || 128 % c.head_dim) {
+    return fail(FDLLM_ERR_UNSUPPORTED, "fp32 path needs sizes divisible by 32, qkv by 128, head_dim dividing 128");
+  }
+  CUDA_TRY(cudaSetDevice(device));
+  fdllm_handle* h = new fdllm_handle();
+  h->cfg = c;
+  h->device = device;
+  h->dtype = c.dtype;
+  h->esz = c.dtype == FDLLM_BFLOAT16 ? 2 : 4;
+  cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device);
+  const size_t tab = static_cast<size_t>(c.max_positions) * (c.head_dim / 2) * h->esz;
+  int r = h->rope_cos.ensure(tab);
+  if (r == FDLLM_OK) r = h->rope_sin.ensure(tab);
+  if (r == FDLLM_OK) r = h->err.ensure(4, true);
+  if (r != FDLLM_OK) {
+    fdllm_destroy(h);
+    return r;
+  }
+  cudaError_t e = static_cast<cudaError_t>(
+      launch_rope_tables(h->rope_cos.p, h->rope_sin.p, c.max_positions, c.head_dim, c.rope_theta, h->dtype, 0));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    fdllm_destroy(h);
+    return fail(FDLLM_ERR_CUDA, std::string("rope tables: ") + cudaGetErrorString(e));
+  }
+  *out = h;
+  return FDLLM_OK;
+}
+
+int fdllm_destroy(fdllm_handle* h) {
+  if (h == nullptr) return FDLLM_OK;
+  cudaSetDevice(h->device);
+  cudaDeviceSynchronize();
+  for (auto* b : {&h->rope_cos, &h->rope_sin, &h->h, &h->xn, &h->q, &h->attn, &h->act, &h->scratch_k, &h->scratch_v,
+                  &h->dec.k, &h->dec.v, &h->dec.x, &h->dec.hid})
+    b->release();
+  for (auto* b : {&h->err, &h->tok_req, &h->tok_pos, &h->tok_row, &h->tmp_ids, &h->targets, &h->counters, &h->dec.ids,
+                  &h->dec.block, &h->dec.cids, &h->dec.out})
+    b->release();
+  for (auto* b : {&h->splitk, &h->attn_po, &h->attn_pl, &h->conf_part, &h->tmp_maxp, &h->dec.cmax}) b->release();
+  h->reqs.release();
+  if (h->dec.host) cudaFreeHost(h->dec.host);
+  for (cudaEvent_t e : h->prof_ev) cudaEventDestroy(e);
+  delete h;
+  return FDLLM_OK;
+}
+
+int fdllm_bind_params(fdllm_handle* h, const void* const* ptrs, int n) {
+  if (h == nullptr || ptrs == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
+  std::lock_guard<std::mutex> lock(h->mu);
+  const fdllm_config& c = h->cfg;
+  const int expect = 1 + 7 * c.num_hidden_layers + 1 + (c.tie_word_embeddings ? 0 : 1);
+  if (n != expect)
+    return fail(FDLLM_ERR_INVALID, "expected " + std::to_string(expect) + " params, got " + std::to_string(n));
+  for (int i = 0; i < n; ++i)
+    if (ptrs[i] == nullptr || (reinterpret_cast<uintptr_t>(ptrs[i]) & 15) != 0)
+      return fail(FDLLM_ERR_INVALID, "param " + std::to_string(i) + " is null or not 16-byte aligned");
+  CUDA_TRY(cudaSetDevice(h->device));
+  const int qkv = (c.num_attention_heads + 2 * c.num_key_value_heads) * c.head_dim;
+  const int qd = c.num_attention_heads * c.head_dim;
+  h->embed = ptrs[0];
+  h->layers.assign(c.num_hidden_layers, LayerW{});
+  for (int l = 0; l < c.num_hidden_layers; ++l) {
+    const void* const* p = ptrs + 1 + 7 * l;
+    LayerW& L = h->layers[l];
+    L.qkv = Weight{p[0], qkv, c.hidden_size, false, {}};
+    L.qkv_b = p[1];
+    L.o = Weight{p[2], c.hidden_size, qd, false, {}};
+    L.gu = Weight{p[3], 2 * c.intermediate_size, c.hidden_size, true, {}};
+    L.down = Weight{p[4], c.hidden_size, c.intermediate_size, false, {}};
+    L.ln1 = p[5];
+    L.ln2 = p[6];
+  }
+  h->final_norm = ptrs[1 + 7 * c.num_hidden_layers];
+  h->lm = Weight{c.tie_word_embeddings ? ptrs[0] : ptrs[n - 1], c.vocab_size, c.hidden_size, false, {}};
+  if (h->dtype == FDLLM_BFLOAT16) {
+    for (LayerW& L : h->layers) {
+      FDLLM_TRY(make_map(&L.qkv.map, L.qkv.ptr, L.qkv.rows, L.qkv.cols, 128));
+      FDLLM_TRY(make_map(&L.o.map, L.o.ptr, L.o.rows, L.o.cols, 128));
+      FDLLM_TRY(make_map(&L.gu.map, L.gu.ptr, L.gu.rows, L.gu.cols, 64));
+      FDLLM_TRY(make_map(&L.down.map, L.down.ptr, L.down.rows, L.down.cols, 128));
+    }
+    FDLLM_TRY(make_map(&h->lm.map, h->lm.ptr, h->lm.rows, h->lm.cols, 128));
+  }
+  h->bound = true;
+  return FDLLM_OK;
+}
+
+int fdllm_embed(fdllm_handle* h, const int32_t* ids, int n, void* out, void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (n < 0 || (n > 0 && (ids == nullptr || out == nullptr))) return fail(FDLLM_ERR_INVALID, "bad embed arguments");
+  std::lock_guard<std::mutex> lock(h->mu);
+  CUDA_TRY(launch_embed(ids, n, h->embed, h->cfg.vocab_size, h->cfg.hidden_size, out, h->dtype, h->err.p,
+                        static_cast<cudaStream_t>(stream)));
+  return FDLLM_OK;
+}
+
+}  // extern "C"
+
+int fdllm::dense_forward(fdllm_handle* h, const void* x, const float* bias, int T, void* k, void* v, int cap,
+                         bool scratch, void* out, cudaStream_t s) {
+  const fdllm_config& c = h->cfg;
+  ReqDesc d{};
+  if (scratch) {
+    const size_t bytes = static_cast<size_t>(T) * c.num_key_value_heads * c.head_dim * h->esz;
+    FDLLM_TRY(h->scratch_k.ensure(bytes));
+    FDLLM_TRY(h->scratch_v.ensure(bytes));
+    d.k = h->scratch_k.p;
+    d.v = h->scratch_v.p;
+    d.layer_stride = 0;
+    d.cap = T;
+  } else {
+    d.k = k;
+    d.v = v;
+    d.layer_stride = layer_stride(h, cap);
+    d.cap = cap;
+  }
+  d.q_tok0 = 0;
+  d.n_q = T;
+  d.write_start = 0;
+  d.attend_len = T;
+  d.rope_base = 0;
+  d.rope_off = nullptr;
+  std::vector<ReqDesc> reqs{d};
+  return forward_core(h, x, T, reqs, bias, T, bias == nullptr ? c.bd_size : 0, out, s);
+}
+
+extern "C" {
+
+
+int fdllm_forward_hidden(fdllm_handle* h, const void* x, const float* bias, int T, void* out, void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (T <= 0 || x == nullptr || out == nullptr) return fail(FDLLM_ERR_INVALID, "bad forward_hidden arguments");
+  if (T > h->cfg.max_positions) return fail(FDLLM_ERR_INVALID, "sequence longer than max_positions");
+  std::lock_guard<std::mutex> lock(h->mu);
+  return dense_forward(h, x, bias, T, nullptr, nullptr, 0, true, out, static_cast<cudaStream_t>(stream));
+}
+
+int fdllm_build_prefix_cache(fdllm_handle* h, const void* x, const float* bias, int P, void* k, void* v, int cap,
+                             void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (P <= 0 || x == nullptr || k == nullptr || v == nullptr) return fail(FDLLM_ERR_INVALID, "bad build_prefix_cache arguments");
+  if (P > cap) return fail(FDLLM_ERR_INVALID, "KV write [0, " + std::to_string(P) + ") outside cache capacity " + std::to_string(cap));
+  if (P > h->cfg.max_positions) return fail(FDLLM_ERR_INVALID, "prefix longer than max_positions");
+  std::lock_guard<std::mutex> lock(h->mu);
+  return dense_forward(h, x, bias, P, k, v, cap, false, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int fdllm_forward_cached(fdllm_handle* h, const void* x, int rows, void* k, void* v, int cap,
+                         const int32_t* cache_offset_dev, int prefix_len, int write_rel, int attend_rel, void* out,
+                         void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (x == nullptr || out == nullptr) return fail(FDLLM_ERR_INVALID, "null activation pointer");
+  fdllm_request r{k, v, cap, rows, prefix_len, write_rel, attend_rel, prefix_len + write_rel, cache_offset_dev};
+  std::vector<ReqDesc> reqs(1);
+  FDLLM_TRY(cached_desc(h, r, 0, &reqs[0]));
+  std::lock_guard<std::mutex> lock(h->mu);
+  return forward_core(h, x, rows, reqs, nullptr, 0, 0, out, static_cast<cudaStream_t>(stream));
+}
+
+int fdllm_forward_cached_batch(fdllm_handle* h, const fdllm_request* reqs_host, int n, const void* x, void* out,
+                               void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (n <= 0 || reqs_host == nullptr || x == nullptr || out == nullptr) return fail(FDLLM_ERR_INVALID, "bad batch arguments");
+  std::vector<ReqDesc> reqs(n);
+  int tok = 0;
+  for (int i = 0; i < n; ++i) {
+    FDLLM_TRY(cached_desc(h, reqs_host[i], tok, &reqs[i]));
+    tok += reqs_host[i].rows;
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  return forward_core(h, x, tok, reqs, nullptr, 0, 0, out, static_cast<cudaStream_t>(stream));
+}
+
+int fdllm_get_logits(fdllm_handle* h, const void* hidden, int rows, float* logits, void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (rows <= 0 || hidden == nullptr || logits == nullptr) return fail(FDLLM_ERR_INVALID, "bad get_logits arguments");
+  std::lock_guard<std::mutex> lock(h->mu);
+  Epilogue e{};
+  e.kind = kEpiLogitsF32;
+  e.out = logits;
+  e.ld_out = h->cfg.vocab_size;
+  return run_gemm(h, h->lm, hidden, rows, e, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+int fdllm::confidence_locked(fdllm_handle* h, const void* hidden, int rows, int32_t* ids, float* maxp,
+                             const int32_t* targets, float* logprob, cudaStream_t s) {
+  const int n_slabs = (h->cfg.vocab_size + 127) / 128;
+  FDLLM_TRY(h->conf_part.ensure(static_cast<size_t>(rows) * n_slabs * 4));
+  Epilogue e{};
+  e.kind = targets ? kEpiLseGather : kEpiConf;
+  e.part = h->conf_part.p;
+  e.target = targets;
+  FDLLM_TRY(run_gemm(h, h->lm, hidden, rows, e, s));
+  if (targets) {
+    CUDA_TRY(launch_lse_combine(h->conf_part.p, rows, n_slabs, logprob, s));
+  } else {
+    CUDA_TRY(launch_conf_combine(h->conf_part.p, rows, n_slabs, ids, maxp, s));
+  }
+  return FDLLM_OK;
+}
+
+extern "C" {
+
+
+int fdllm_confidence(fdllm_handle* h, const void* hidden, int rows, int32_t* ids, float* maxp, void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (rows <= 0 || hidden == nullptr || ids == nullptr || maxp == nullptr) return fail(FDLLM_ERR_INVALID, "bad confidence arguments");
+  std::lock_guard<std::mutex> lock(h->mu);
+  return confidence_locked(h, hidden, rows, ids, maxp, nullptr, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int fdllm_confidence_from_logits(fdllm_handle* h, const float* logits, int rows, int32_t* ids, float* maxp,
+                                 void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (rows <= 0 || logits == nullptr || ids == nullptr || maxp == nullptr) return fail(FDLLM_ERR_INVALID, "bad arguments");
+  std::lock_guard<std::mutex> lock(h->mu);
+  CUDA_TRY(launch_conf_from_logits(logits, rows, h->cfg.vocab_size, ids, maxp, static_cast<cudaStream_t>(stream)));
+  return FDLLM_OK;
+}
+
+int fdllm_token_logprob(fdllm_handle* h, const void* hidden, int rows, const int32_t* targets, float* logprob,
+                        void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (rows <= 0 || hidden == nullptr || targets == nullptr || logprob == nullptr) return fail(FDLLM_ERR_INVALID, "bad arguments");
+  std::lock_guard<std::mutex> lock(h->mu);
+  return confidence_locked(h, hidden, rows, nullptr, nullptr, targets, logprob, static_cast<cudaStream_t>(stream));
+}
+
+int fdllm_unmask(fdllm_handle* h, const int32_t* ids, const float* maxp, int rows, int32_t* block_tokens, int sub_start,
+                 int sub_len, int partial, int mask_id, double threshold, int32_t* out_tokens, float* out_conf,
+                 int32_t* out_unmask, int32_t* status, void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (ids == nullptr || maxp == nullptr || block_tokens == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
+  if (sub_len <= 0 || sub_len > 32 || sub_start < 0 || sub_start + sub_len > h->cfg.bd_size)
+    return fail(FDLLM_ERR_INVALID, "bad unmask window");
+  if (partial ? rows != sub_len : rows < sub_start + sub_len) return fail(FDLLM_ERR_INVALID, "rows do not cover the window");
+  CUDA_TRY(launch_unmask(ids, maxp, rows, block_tokens, sub_start, sub_len, partial, mask_id, threshold, out_tokens,
+                         out_conf, out_unmask, status, static_cast<cudaStream_t>(stream)));
+  return FDLLM_OK;
+}
+
+int fdllm_device_error(fdllm_handle* h, int* code) {
+  if (h == nullptr || code == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
+  CUDA_TRY(cudaSetDevice(h->device));
+  CUDA_TRY(cudaDeviceSynchronize());
+  CUDA_TRY(cudaMemcpy(code, h->err.p, sizeof(int), cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemset(h->err.p, 0, sizeof(int)));
+  return FDLLM_OK;
+}
+
+int fdllm_wait_selftest(fdllm_handle* h, unsigned long long limit_ns, int* code) {
+  if (h == nullptr || code == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
+  CUDA_TRY(cudaSetDevice(h->device));
+  int* flag = nullptr;
+  CUDA_TRY(cudaMalloc(&flag, sizeof(int)));
+  cudaMemset(flag, 0, sizeof(int));
+  cudaError_t e = static_cast<cudaError_t>(launch_wait_test(flag, h->err.p, limit_ns, 0));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(flag);
+  if (e != cudaSuccess) return fail(FDLLM_ERR_CUDA, std::string("wait self test: ") + cudaGetErrorString(e));
+  return fdllm_device_error(h, code);
+}
+
+long long fdllm_kernel_launches(void) { return launch_count(); }
+
+int fdllm_profile_enable(fdllm_handle* h, int enable) {
+  if (h == nullptr) return fail(FDLLM_ERR_INVALID, "null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->prof = enable != 0;
+  return FDLLM_OK;
+}
+
+int fdllm_profile_read(fdllm_handle* h, double* out4) {
+  if (h == nullptr || out4 == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
+  std::lock_guard<std::mutex> lock(h->mu);
+  CUDA_TRY(cudaSetDevice(h->device));
+  double ms = 0.0;
+  for (size_t i = 0; i + 1 < h->prof_used; i += 2) {
+    CUDA_TRY(cudaEventSynchronize(h->prof_ev[i + 1]));
+    float t = 0.f;
+    CUDA_TRY(cudaEventElapsedTime(&t, h->prof_ev[i], h->prof_ev[i + 1]));
+    ms += t;
+  }
+  out4[0] = ms;
+  out4[1] = h->prof_bytes;
+  out4[2] = static_cast<double>(h->prof_used / 2);
+  out4[3] = h->prof_flops;
+  h->prof_used = 0;
+  h->prof_bytes = h->prof_flops = 0.0;
+  return FDLLM_OK;
+}
+
+long long fdllm_workspace_bytes(fdllm_handle* h) {
+  if (h == nullptr) return 0;
+  long long t = 0;
+  for (auto* b : {&h->h, &h->xn, &h->q, &h->attn, &h->act, &h->scratch_k, &h->scratch_v, &h->rope_cos, &h->rope_sin,
+                  &h->dec.k, &h->dec.v, &h->dec.x, &h->dec.hid})
+    t += static_cast<long long>(b->bytes());
+  for (auto* b : {&h->splitk, &h->attn_po, &h->attn_pl, &h->conf_part, &h->tmp_maxp, &h->dec.cmax})
+    t += static_cast<long long>(b->bytes());
+  for (auto* b : {&h->err, &h->tok_req, &h->tok_pos, &h->tok_row, &h->tmp_ids, &h->targets, &h->counters, &h->dec.ids,
+                  &h->dec.block, &h->dec.cids, &h->dec.out})
+    t += static_cast<long long>(b->bytes());
+  return t + static_cast<long long>(h->reqs.bytes());
+}
+
+}  // extern "C"
