@@ -322,8 +322,7 @@ template <int HD>
 static int launch_mma(const AttnArgs& a, int max_q, cudaStream_t s) {
   const int G = a.hq / a.hkv;
   constexpr int smem = 4 * kKT * HD * 2;
-  cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
+  cudaError_t e;
   dim3 grid((max_q + kQT - 1) / kQT, a.hkv, a.n_reqs * a.n_splits);
   attn_mma_kernel<HD><<<grid, G * 32, smem, s>>>(a);
   count_launch();
@@ -332,6 +331,16 @@ static int launch_mma(const AttnArgs& a, int max_q, cudaStream_t s) {
   attn_combine_kernel<bf16><<<dim3(a.m_total, a.hq), 128, 0, s>>>(a);
   count_launch();
   return cudaGetLastError();
+}
+
+int init_gemm_tc_attributes();
+
+int init_kernel_attributes() {
+  cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * kKT * 128 * 2);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * kKT * 64 * 2);
+  if (e == cudaSuccess) e = static_cast<cudaError_t>(init_gemm_tc_attributes());
+  return e;
 }
 
 int launch_attention(const AttnArgs& a, int max_q, int dtype, cudaStream_t s) {

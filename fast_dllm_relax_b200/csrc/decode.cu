@@ -9,6 +9,7 @@
 // tokens into the device block), and the host reads back only the step's window (status, tokens,
 // unmask flags: ~70 bytes) to drive the loop.  The reference instead copies the fp32 logits'
 // reductions back and decides in Python (runtime.py:176-181, 796-805).
+#include <algorithm>
 #include <cstring>
 
 #include "handle.h"
@@ -22,7 +23,7 @@ constexpr int kHostInts = 2 + 2 * kWin;   // pinned read-back: status[2], window
 
 struct Driver {
   fdllm_handle* h;
-  cudaStream_t s;
+  cudaStream_t s;  // the handle's own non-blocking decode stream (capturable)
   int bs, sbs, mask_id, stop;
   double thr;
   bool block_cache;
@@ -34,8 +35,11 @@ struct Driver {
 
   int setup(int n0, int max_new) {
     const fdllm_config& c = h->cfg;
-    cap = static_cast<int>((static_cast<long long>(n0) + max_new + bs - 1) / bs * bs + bs);
-    if (cap > c.max_positions) return fail(FDLLM_ERR_INVALID, "prompt + max_new_tokens exceeds max_positions");
+    const long long need = (static_cast<long long>(n0) + max_new + bs - 1) / bs * bs + bs;
+    // Capacity rounded up to 512 rows so that repeated calls reuse the captured step graphs.
+    cap = static_cast<int>((need + 511) / 512 * 512);
+    if (need > c.max_positions) return fail(FDLLM_ERR_INVALID, "prompt + max_new_tokens exceeds max_positions");
+    cap = std::min(cap, std::max(static_cast<int>(need), c.max_positions));
     const size_t cache_bytes = static_cast<size_t>(c.num_hidden_layers) * cap * c.num_key_value_heads * c.head_dim * h->esz;
     FDLLM_TRY(h->dec.k.ensure(cache_bytes));
     FDLLM_TRY(h->dec.v.ensure(cache_bytes));
@@ -45,8 +49,17 @@ struct Driver {
     FDLLM_TRY(h->dec.hid.ensure(static_cast<size_t>(bs) * c.hidden_size * h->esz));
     FDLLM_TRY(h->dec.cids.ensure(static_cast<size_t>(bs)));
     FDLLM_TRY(h->dec.cmax.ensure(static_cast<size_t>(bs)));
-    FDLLM_TRY(h->dec.out.ensure(2 + 2 * kWin));
+    FDLLM_TRY(h->dec.out.ensure(kHostInts));
+    FDLLM_TRY(h->dec.plen.ensure(1));
     if (h->dec.host == nullptr) CUDA_TRY(cudaMallocHost(&h->dec.host, kHostInts * sizeof(int)));
+    if (h->dec.host_params == nullptr) CUDA_TRY(cudaMallocHost(&h->dec.host_params, 16 * sizeof(int)));
+    if (h->dec.stream == nullptr) CUDA_TRY(cudaStreamCreateWithFlags(&h->dec.stream, cudaStreamNonBlocking));
+    s = h->dec.stream;
+    if (h->dec.graph_cache_ptr != h->dec.k.p || h->dec.graph_cap != cap) {
+      release_step_graphs(h);
+      h->dec.graph_cache_ptr = h->dec.k.p;
+      h->dec.graph_cap = cap;
+    }
     return FDLLM_OK;
   }
 
@@ -67,24 +80,107 @@ struct Driver {
     return FDLLM_OK;
   }
 
-  // forward_cached / forward_block_partial_rp{s0} over the device block (runtime.py:333-343, 398-433)
-  int forward(int s0, int rows, int write_rel) {
-    CUDA_TRY(launch_embed(h->dec.block.p + s0, rows, h->embed, h->cfg.vocab_size, h->cfg.hidden_size, h->dec.x.p,
-                          h->dtype, h->err.p, s));
-    fdllm_request r{h->dec.k.p, h->dec.v.p, cap, rows, prefix_len, write_rel, bs, prefix_len + write_rel, nullptr};
-    std::vector<ReqDesc> reqs(1);
-    FDLLM_TRY(cached_desc(h, r, 0, &reqs[0]));
-    FDLLM_TRY(forward_core(h, h->dec.x.p, rows, reqs, nullptr, 0, 0, h->dec.hid.p, s));
-    return confidence_locked(h, h->dec.hid.p, rows, h->dec.cids.p, h->dec.cmax.p, nullptr, nullptr, s);
+  // The device work of one step: embed the block rows, the cached forward (write_rel = s0 for a
+  // partial step; the prefix length is read from h->dec.plen), the fused lm_head + confidence, then
+  // either the unmask of window [s0, s0+len) or (append) the last row's token; results are copied
+  // to the pinned host buffer.  Recorded once per step shape into a CUDA graph.
+  int record(int kind, int s0, int len) {
+    const bool partial = kind == 1;
+    const int rows = partial ? len : bs;
+    CUDA_TRY(launch_embed(h->dec.block.p + (partial ? s0 : 0), rows, h->embed, h->cfg.vocab_size, h->cfg.hidden_size,
+                          h->dec.x.p, h->dtype, h->err.p, s));
+    ReqDesc d{};
+    d.k = h->dec.k.p;
+    d.v = h->dec.v.p;
+    d.layer_stride = layer_stride(h, cap);
+    d.cap = cap;
+    d.q_tok0 = 0;
+    d.n_q = rows;
+    d.plen_dev = h->dec.plen.p;
+    d.write_rel = partial ? s0 : 0;
+    d.attend_rel = bs;
+    std::vector<ReqDesc> reqs{d};
+    FDLLM_TRY(forward_core(h, h->dec.x.p, rows, reqs, nullptr, 0, 0, h->dec.hid.p, s, cap));
+    FDLLM_TRY(confidence_locked(h, h->dec.hid.p, rows, h->dec.cids.p, h->dec.cmax.p, nullptr, nullptr, s));
+    int* out = h->dec.out.p;
+    if (kind == 2) {
+      CUDA_TRY(cudaMemcpyAsync(host(), h->dec.cids.p + bs - 1, sizeof(int), cudaMemcpyDeviceToHost, s));
+    } else {
+      CUDA_TRY(launch_unmask(h->dec.cids.p, h->dec.cmax.p, rows, h->dec.block.p, s0, len, partial ? 1 : 0, mask_id,
+                             thr, out + 2, nullptr, out + 2 + kWin, out, s));
+      CUDA_TRY(cudaMemcpyAsync(host(), out, kHostInts * sizeof(int), cudaMemcpyDeviceToHost, s));
+    }
+    return FDLLM_OK;
   }
 
-  // Unmask on the device, read back the window.  Returns the number of tokens unmasked.
-  int unmask(int rows, int s0, int len, bool partial, int* x_window) {
-    int* out = h->dec.out.p;
-    CUDA_TRY(launch_unmask(h->dec.cids.p, h->dec.cmax.p, rows, h->dec.block.p, s0, len, partial ? 1 : 0, mask_id, thr,
-                           out + 2, nullptr, out + 2 + kWin, out, s));
-    CUDA_TRY(cudaMemcpyAsync(host(), out, (2 + 2 * kWin) * sizeof(int), cudaMemcpyDeviceToHost, s));
+  // Replay (capturing on first use) the graph of one step shape, then wait for its results.
+  int run_step(int kind, int s0, int len) {
+    h->dec.host_params[0] = prefix_len;
+    CUDA_TRY(cudaMemcpyAsync(h->dec.plen.p, h->dec.host_params, sizeof(int), cudaMemcpyHostToDevice, s));
+    const long long key = ((static_cast<long long>(kind) * 64 + s0) * 64 + len) * 2 + (h->prof ? 1 : 0);
+    StepGraph* g = nullptr;
+    for (auto& kv : h->dec.graphs)
+      if (kv.first == key) g = &kv.second;
+    if (g != nullptr && g->gen != g_ws_generation.load()) {  // a workspace buffer moved since capture
+      release_step_graphs(h);
+      g = nullptr;
+    }
+    if (g != nullptr && (g->mask_id != mask_id || g->thr != thr)) {  // other unmask parameters
+      release_step_graphs(h);
+      g = nullptr;
+    }
+    if (g == nullptr) {
+      FDLLM_TRY(reserve_workspace(h, bs, 1, cap));  // nothing may allocate while capturing
+      const unsigned long long gen = g_ws_generation.load();
+      h->cap_prof.clear();
+      h->capturing = true;
+      CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
+      const int rc = record(kind, s0, len);
+      cudaGraph_t graph = nullptr;
+      const cudaError_t ec = cudaStreamEndCapture(s, &graph);
+      h->capturing = false;
+      if (rc != FDLLM_OK || ec != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        for (auto& pp : h->cap_prof) {
+          cudaEventDestroy(pp.e0);
+          cudaEventDestroy(pp.e1);
+        }
+        h->cap_prof.clear();
+        return rc != FDLLM_OK ? rc : fail(FDLLM_ERR_CUDA, std::string("stream capture: ") + cudaGetErrorString(ec));
+      }
+      if (g_ws_generation.load() != gen) {  // something allocated while recording: refuse the graph
+        cudaGraphDestroy(graph);
+        return fail(FDLLM_ERR_CUDA, "workspace reallocated during stream capture");
+      }
+      StepGraph sg;
+      sg.gen = gen;
+      sg.mask_id = mask_id;
+      sg.thr = thr;
+      const cudaError_t ei = cudaGraphInstantiate(&sg.exec, graph, 0);
+      cudaGraphDestroy(graph);
+      sg.prof.swap(h->cap_prof);
+      if (ei != cudaSuccess) return fail(FDLLM_ERR_CUDA, std::string("cudaGraphInstantiate: ") + cudaGetErrorString(ei));
+      h->dec.graphs.emplace_back(key, std::move(sg));
+      g = &h->dec.graphs.back().second;
+    }
+    CUDA_TRY(cudaGraphLaunch(g->exec, s));
     CUDA_TRY(cudaStreamSynchronize(s));
+    if (h->prof) {
+      for (const ProfPair& pp : g->prof) {
+        float t = 0.f;
+        CUDA_TRY(cudaEventElapsedTime(&t, pp.e0, pp.e1));
+        h->prof_ms_extra += t;
+        h->prof_bytes += pp.bytes;
+        h->prof_flops += pp.flops;
+        h->prof_launch_extra += 1;
+      }
+    }
+    return FDLLM_OK;
+  }
+
+  // One refinement step; copies the unmasked tokens of the window into the host sequence.
+  int refine(bool partial, int s0, int len, int* x_window) {
+    FDLLM_TRY(run_step(partial ? 1 : 0, s0, len));
     const int* hb = host();
     for (int j = 0; j < len; ++j)
       if (hb[2 + kWin + j]) x_window[j] = hb[2 + j];
@@ -92,10 +188,9 @@ struct Driver {
     return FDLLM_OK;
   }
 
-  // Last row's unshifted argmax after a committing forward (runtime.py:181).
-  int last_token(int* tok) {
-    CUDA_TRY(cudaMemcpyAsync(host(), h->dec.cids.p + bs - 1, sizeof(int), cudaMemcpyDeviceToHost, s));
-    CUDA_TRY(cudaStreamSynchronize(s));
+  // Block-append: the committing forward; returns the last row's unshifted argmax (runtime.py:181).
+  int append(int* tok) {
+    FDLLM_TRY(run_step(2, 0, bs));
     *tok = host()[0];
     return FDLLM_OK;
   }
@@ -129,8 +224,8 @@ extern "C" int fdllm_generate(fdllm_handle* h, const int32_t* prompt, int prompt
     return fail(FDLLM_ERR_UNSUPPORTED, "prompts shorter than one block take the stateless path (forward_hidden); "
                                        "use the Python runtime for them");
   std::lock_guard<std::mutex> lock(h->mu);
-  Driver d{h, static_cast<cudaStream_t>(stream), block_size, small_block_size, mask_id, stop_token, threshold,
-           use_block_cache != 0};
+  CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));  // the caller's prior work is done
+  Driver d{h, nullptr, block_size, small_block_size, mask_id, stop_token, threshold, use_block_cache != 0};
   const int bs = block_size, sbs = small_block_size;
   std::vector<int> gen(prompt, prompt + prompt_len);
   const size_t n0 = gen.size();
@@ -172,10 +267,9 @@ extern "C" int fdllm_generate(fdllm_handle* h, const int32_t* prompt, int prompt
     const int lb = static_cast<int>(n0) - bs;
     FDLLM_TRY(d.prefill(gen.data(), lb));
     FDLLM_TRY(d.upload_block(gen.data() + lb));
-    FDLLM_TRY(d.forward(0, bs, 0));
-    d.prefix_len += bs;  // commit
     int nxt = 0;
-    FDLLM_TRY(d.last_token(&nxt));
+    FDLLM_TRY(d.append(&nxt));
+    d.prefix_len += bs;  // commit
     d.st[1] += 1;
     d.st[3] += 1;
     gen.push_back(nxt);
@@ -202,13 +296,10 @@ extern "C" int fdllm_generate(fdllm_handle* h, const int32_t* prompt, int prompt
         if (!any_mask) break;
         if (has_completed_stop(x, plen, stop_token, mask_id)) return finish(x);
         const bool partial = d.block_cache && kv_valid && x[a0 + s0] != mask_id;
+        FDLLM_TRY(d.refine(partial, s0, s1 - s0, x.data() + a0 + s0));
         if (partial) {
-          FDLLM_TRY(d.forward(s0, s1 - s0, s0));
-          FDLLM_TRY(d.unmask(s1 - s0, s0, s1 - s0, true, x.data() + a0 + s0));
           d.st[2] += 1;
         } else {
-          FDLLM_TRY(d.forward(0, bs, 0));
-          FDLLM_TRY(d.unmask(bs, s0, s1 - s0, false, x.data() + a0 + s0));
           kv_valid = d.block_cache;
         }
         d.st[1] += 1;
@@ -223,10 +314,9 @@ extern "C" int fdllm_generate(fdllm_handle* h, const int32_t* prompt, int prompt
     if (gen.size() - n0 >= static_cast<size_t>(max_new_tokens)) break;
     if (has_completed_stop(gen, n0, stop_token, mask_id)) break;
     // block-append: the completed block is already on the device (the unmask kernel kept it)
-    FDLLM_TRY(d.forward(0, bs, 0));
-    d.prefix_len += bs;
     int nxt = 0;
-    FDLLM_TRY(d.last_token(&nxt));
+    FDLLM_TRY(d.append(&nxt));
+    d.prefix_len += bs;
     kv_valid = false;
     d.st[1] += 1;
     gen.push_back(nxt);
@@ -234,4 +324,15 @@ extern "C" int fdllm_generate(fdllm_handle* h, const int32_t* prompt, int prompt
     if (stop_token >= 0 && nxt == stop_token) break;
   }
   return finish(gen);
+}
+
+void fdllm::release_step_graphs(fdllm_handle* h) {
+  for (auto& kv : h->dec.graphs) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    for (auto& pp : kv.second.prof) {
+      cudaEventDestroy(pp.e0);
+      cudaEventDestroy(pp.e1);
+    }
+  }
+  h->dec.graphs.clear();
 }

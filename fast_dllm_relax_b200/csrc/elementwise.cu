@@ -112,7 +112,17 @@ int launch_rope_tables(void* cos_t, void* sin_t, int max_pos, int hd, float thet
 __global__ void prepare_kernel(const ReqBatch b, ReqDesc* table, TokenMaps tok, int max_pos, int* err) {
   const int i = blockIdx.x;
   if (i >= b.n) return;
-  const ReqDesc r = b.r[i];
+  ReqDesc r = b.r[i];
+  if (r.plen_dev != nullptr) {
+    const int P = *r.plen_dev;
+    r.write_start = P + r.write_rel;
+    r.attend_len = P + r.attend_rel;
+    if (r.rope_off == nullptr) r.rope_base = P + r.write_rel;
+    if (P < 0 || r.attend_len > r.cap || r.write_start + r.n_q > r.cap) {
+      if (threadIdx.x == 0) report_error(err, kErrCacheRange);
+      r.attend_len = min(max(r.attend_len, 0), r.cap);
+    }
+  }
   if (threadIdx.x == 0) table[b.first + i] = r;
   const int p0 = (r.rope_off != nullptr) ? *r.rope_off : r.rope_base;
   for (int j = threadIdx.x; j < r.n_q; j += blockDim.x) {

@@ -196,12 +196,24 @@ __global__ void __launch_bounds__(128, 1)
 template <int NT>
 static int launch_nt(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, cudaStream_t s) {
   using C = TcCfg<NT>;
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-  if (e != cudaSuccess) return e;
   dim3 grid(a.n_slabs, a.n_tok_tiles, a.splits);
   gemm_tc_kernel<NT><<<grid, 128, C::kSmem, s>>>(tmA, tmB, a);
   count_launch();
   return cudaGetLastError();
+}
+
+template <int NT>
+static cudaError_t set_attr() {
+  return cudaFuncSetAttribute(gemm_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<NT>::kSmem);
+}
+
+int init_gemm_tc_attributes() {
+  cudaError_t e = set_attr<16>();
+  if (e == cudaSuccess) e = set_attr<32>();
+  if (e == cudaSuccess) e = set_attr<64>();
+  if (e == cudaSuccess) e = set_attr<128>();
+  if (e == cudaSuccess) e = set_attr<256>();
+  return e;
 }
 
 int gemm_tc_smem_bytes(int nt) {

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -42,12 +43,17 @@ struct LayerW {
   const void* ln2 = nullptr;
 };
 
+// Bumped whenever any workspace buffer is reallocated: captured graphs recorded before a bump hold
+// stale pointers and are recaptured.
+extern std::atomic<unsigned long long> g_ws_generation;
+
 template <typename P>
 struct DevBuf {
   P* p = nullptr;
   size_t n = 0;  // elements
   int ensure(size_t want, bool zero = false) {
     if (want <= n) return FDLLM_OK;
+    g_ws_generation.fetch_add(1);
     if (p) cudaFree(p);
     p = nullptr;
     n = 0;
@@ -69,6 +75,20 @@ struct DevBuf {
   size_t bytes() const { return n * sizeof(P); }
 };
 
+struct ProfPair {
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  double bytes = 0.0, flops = 0.0;
+};
+
+// One captured decode step (see decode.cu).
+struct StepGraph {
+  cudaGraphExec_t exec = nullptr;
+  unsigned long long gen = 0;  // g_ws_generation at capture
+  int mask_id = 0;             // unmask parameters baked into the captured launch
+  double thr = 0.0;
+  std::vector<ProfPair> prof;
+};
+
 struct DecodeState {
   DevBuf<uint8_t> k, v;        // caches of the native driver
   DevBuf<int> ids;             // prefill / block token ids
@@ -78,6 +98,12 @@ struct DecodeState {
   DevBuf<float> cmax;          // confidence values
   DevBuf<int> out;             // [0..1] status, [2..] window tokens, then unmask flags
   int* host = nullptr;         // pinned read-back buffer
+  int* host_params = nullptr;  // pinned step parameters (prefix length)
+  DevBuf<int> plen;            // device prefix length read by the captured steps
+  cudaStream_t stream = nullptr;
+  std::vector<std::pair<long long, StepGraph>> graphs;  // keyed step graphs
+  const void* graph_cache_ptr = nullptr;                // caches the graphs were captured against
+  int graph_cap = 0;
 };
 
 }  // namespace fdllm
@@ -118,6 +144,11 @@ struct fdllm_handle {
   std::vector<cudaEvent_t> prof_ev;
   size_t prof_used = 0;
   double prof_bytes = 0.0, prof_flops = 0.0;
+  double prof_ms_extra = 0.0;       // accumulated from replayed graphs
+  long long prof_launch_extra = 0;
+  // stream capture in progress: profiled launches get graph-owned events
+  bool capturing = false;
+  std::vector<fdllm::ProfPair> cap_prof;
 };
 
 
@@ -127,7 +158,9 @@ size_t round_up(size_t x, size_t m);
 long long layer_stride(const fdllm_handle* h, int cap);
 int check_handle(fdllm_handle* h);
 int forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDesc>& reqs, const float* bias, int ld_bias,
-                 int causal_block, void* out, cudaStream_t s);
+                 int causal_block, void* out, cudaStream_t s, int max_l_hint = 0);
+int reserve_workspace(fdllm_handle* h, int M, int nreq, int max_l);
+void release_step_graphs(fdllm_handle* h);
 int dense_forward(fdllm_handle* h, const void* x, const float* bias, int T, void* k, void* v, int cap, bool scratch,
                   void* out, cudaStream_t s);
 int cached_desc(fdllm_handle* h, const fdllm_request& r, int q_tok0, ReqDesc* d);

@@ -20,7 +20,11 @@ struct ReqDesc {
   int attend_len;           // attention keys are cache rows [0, attend_len)
   int rope_base;            // RoPE position of token 0 when rope_off is null
   const int* rope_off;      // device int32 position of token 0 (the reference's cache_offset), or null
-  int pad;
+  // When plen_dev is set, the prepare kernel derives write_start / attend_len / rope_base from the
+  // device prefix length (a captured CUDA graph replays unchanged while the prefix grows).
+  const int* plen_dev;
+  int write_rel;
+  int attend_rel;
 };
 
 constexpr int kMaxReqsPerLaunch = 48;  // keeps ReqBatch under the classic 4 KB parameter limit
@@ -112,6 +116,7 @@ int gemm_tc_smem_bytes(int nt);
 int gemm_tc_stages(int nt);
 
 int launch_attention(const AttnArgs& a, int max_q, int dtype, cudaStream_t s);
+int init_kernel_attributes();  // opt-in shared memory sizes; once per device, before any capture
 
 int launch_embed(const int* ids, int n, const void* table, int vocab, int hidden, void* out, int dtype, int* err,
                  cudaStream_t s);

@@ -19,6 +19,8 @@
 
 using namespace fdllm;
 
+std::atomic<unsigned long long> fdllm::g_ws_generation{0};
+
 // ---- error plumbing ------------------------------------------------------------------------
 static thread_local std::string g_last_error;
 
@@ -108,14 +110,28 @@ static int timed_launch(fdllm_handle* h, const GemmArgs& g, cudaStream_t s, int 
                         const void* a0, const void* a1, int nt) {
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   if (h->prof) {
-    FDLLM_TRY(prof_events(h, &e0, &e1));
-    CUDA_TRY(cudaEventRecord(e0, s));
+    if (h->capturing) {  // the graph owns these events; its replays re-record them
+      ProfPair pp;
+      CUDA_TRY(cudaEventCreate(&pp.e0));
+      CUDA_TRY(cudaEventCreate(&pp.e1));
+      pp.bytes = gemm_bytes(h, g);
+      pp.flops = 2.0 * g.M * static_cast<double>(g.N) * g.K;
+      h->cap_prof.push_back(pp);
+      e0 = pp.e0;
+      e1 = pp.e1;
+    } else {
+      FDLLM_TRY(prof_events(h, &e0, &e1));
+    }
+    // While capturing, only an "external" record becomes a real event-record node of the graph.
+    CUDA_TRY(cudaEventRecordWithFlags(e0, s, h->capturing ? cudaEventRecordExternal : cudaEventRecordDefault));
   }
   CUDA_TRY(launch(g, a0, a1, nt, s));
   if (h->prof) {
-    CUDA_TRY(cudaEventRecord(e1, s));
-    h->prof_bytes += gemm_bytes(h, g);
-    h->prof_flops += 2.0 * g.M * static_cast<double>(g.N) * g.K;
+    CUDA_TRY(cudaEventRecordWithFlags(e1, s, h->capturing ? cudaEventRecordExternal : cudaEventRecordDefault));
+    if (!h->capturing) {
+      h->prof_bytes += gemm_bytes(h, g);
+      h->prof_flops += 2.0 * g.M * static_cast<double>(g.N) * g.K;
+    }
   }
   return FDLLM_OK;
 }
@@ -128,45 +144,78 @@ static int launch_simt_thunk(const GemmArgs& g, const void* w, const void* x, in
   return launch_gemm_simt_f32(g, static_cast<const float*>(w), static_cast<const float*>(x), s);
 }
 
-static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epilogue epi, cudaStream_t s) {
-  GemmArgs g{};
-  g.M = M;
-  g.N = w.rows;
-  g.K = w.cols;
-  g.paired = w.paired ? 1 : 0;
-  g.err = h->err.p;
-  g.epi = epi;
-  if (M <= 0) return FDLLM_OK;
+// Grid, token tile and split-K plan of one projection (no side effects).
+static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g) {
+  g->M = M;
+  g->N = w.rows;
+  g->K = w.cols;
+  g->paired = w.paired ? 1 : 0;
   if (h->dtype == FDLLM_FLOAT32) {
-    g.n_slabs = w.paired ? (g.N / 2 + 63) / 64 : (g.N + 127) / 128;
-    g.n_tok_tiles = (M + 31) / 32;
-    g.splits = 1;
-    g.kb_per_split = 0;
-    if (epi.kind == kEpiConf || epi.kind == kEpiLseGather) g.n_slabs = (g.N + 127) / 128;
-    return timed_launch(h, g, s, launch_simt_thunk, w.ptr, X, 0);
+    g->n_slabs = w.paired ? (g->N / 2 + 63) / 64 : (g->N + 127) / 128;
+    g->n_tok_tiles = (M + 31) / 32;
+    g->splits = 1;
+    g->kb_per_split = 0;
+    return 32;
   }
   const int nt = pick_nt(M);
-  g.n_tok_tiles = (M + nt - 1) / nt;
-  g.n_slabs = w.paired ? (g.N / 2) / 64 : g.N / 128;
-  const int kblocks = g.K / 64;
-  const int tiles = g.n_slabs * g.n_tok_tiles;
+  g->n_tok_tiles = (M + nt - 1) / nt;
+  g->n_slabs = w.paired ? (g->N / 2) / 64 : g->N / 128;
+  const int kblocks = g->K / 64;
+  const int tiles = g->n_slabs * g->n_tok_tiles;
   int splits = 1;
   if (tiles < h->num_sms) {
     splits = std::max(1, std::min(kblocks, h->num_sms / tiles));
     const int kpb = (kblocks + splits - 1) / splits;
     splits = (kblocks + kpb - 1) / kpb;
   }
-  g.splits = splits;
-  g.kb_per_split = (kblocks + splits - 1) / splits;
-  if (splits > 1) {
-    FDLLM_TRY(h->splitk.ensure(static_cast<size_t>(tiles) * splits * nt * 128));
-    FDLLM_TRY(h->counters.ensure(static_cast<size_t>(tiles), true));
+  g->splits = splits;
+  g->kb_per_split = (kblocks + splits - 1) / splits;
+  return nt;
+}
+
+// Split-K workspace a plan needs (floats, counters).
+static void gemm_workspace(const GemmArgs& g, int nt, size_t* floats, size_t* counters) {
+  const size_t tiles = static_cast<size_t>(g.n_slabs) * g.n_tok_tiles;
+  *floats = g.splits > 1 ? tiles * g.splits * nt * 128 : 0;
+  *counters = g.splits > 1 ? tiles : 0;
+}
+
+static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epilogue epi, cudaStream_t s) {
+  if (M <= 0) return FDLLM_OK;
+  GemmArgs g{};
+  const int nt = plan_gemm(h, w, M, &g);
+  g.err = h->err.p;
+  g.epi = epi;
+  if (h->dtype == FDLLM_FLOAT32) return timed_launch(h, g, s, launch_simt_thunk, w.ptr, X, 0);
+  if (g.splits > 1) {
+    size_t nf, nc;
+    gemm_workspace(g, nt, &nf, &nc);
+    FDLLM_TRY(h->splitk.ensure(nf));
+    FDLLM_TRY(h->counters.ensure(nc, true));
     g.partials = h->splitk.p;
     g.counters = h->counters.p;
   }
   CUtensorMap tmB;
   FDLLM_TRY(make_map(&tmB, X, M, g.K, nt));
   return timed_launch(h, g, s, launch_tc_thunk, &w.map, &tmB, nt);
+}
+
+// Key-split plan of the attention: enough CTAs to cover the SMs at small batch.  `max_l` is the
+// longest key range the launch may see (the cache capacity for a replayable graph).
+static void plan_attention(const fdllm_handle* h, int max_q, int max_l, int nreq, bool dense, int* n_splits,
+                           int* split_len) {
+  const fdllm_config& c = h->cfg;
+  const int qtiles = (max_q + 15) / 16;
+  const int base_ctas = qtiles * c.num_key_value_heads * nreq;
+  *n_splits = 1;
+  *split_len = std::max(64, static_cast<int>(round_up(std::max(max_l, 1), 64)));
+  if (h->dtype == FDLLM_BFLOAT16 && !dense && base_ctas < h->num_sms) {
+    const int want = std::min((2 * h->num_sms + base_ctas - 1) / base_ctas, (max_l + 63) / 64);
+    if (want > 1) {
+      *split_len = static_cast<int>(round_up((max_l + want - 1) / want, 64));
+      *n_splits = (max_l + *split_len - 1) / *split_len;
+    }
+  }
 }
 
 // ---- workspace ----------------------------------------------------------------------------
@@ -194,8 +243,39 @@ static TokenMaps token_maps(fdllm_handle* h) { return TokenMaps{h->tok_req.p, h-
 // ---- the layer stack ----------------------------------------------------------------------
 // x: [M, hidden] input embeddings; reqs: host descriptors (q_tok0 / n_q filled); bias: dense fp32
 // bias of request 0 (or null), causal_block: implicit block-causal mask when bias is null.
+int fdllm::reserve_workspace(fdllm_handle* h, int M, int nreq, int max_l) {
+  FDLLM_TRY(ensure_ws(h, M, nreq));
+  const fdllm_config& c = h->cfg;
+  size_t nf = 0, nc = 0;
+  std::vector<const Weight*> ws{&h->lm};
+  for (const LayerW& L : h->layers) {
+    ws.push_back(&L.qkv);
+    ws.push_back(&L.o);
+    ws.push_back(&L.gu);
+    ws.push_back(&L.down);
+  }
+  for (const Weight* w : ws) {
+    GemmArgs g{};
+    const int nt = plan_gemm(h, *w, M, &g);
+    size_t f, n;
+    gemm_workspace(g, nt, &f, &n);
+    nf = std::max(nf, f);
+    nc = std::max(nc, n);
+  }
+  if (nf) FDLLM_TRY(h->splitk.ensure(nf));
+  if (nc) FDLLM_TRY(h->counters.ensure(nc, true));
+  int n_splits, split_len;
+  plan_attention(h, M, max_l, nreq, false, &n_splits, &split_len);
+  if (n_splits > 1) {
+    FDLLM_TRY(h->attn_po.ensure(static_cast<size_t>(n_splits) * M * c.num_attention_heads * c.head_dim));
+    FDLLM_TRY(h->attn_pl.ensure(static_cast<size_t>(n_splits) * M * c.num_attention_heads));
+  }
+  FDLLM_TRY(h->conf_part.ensure(static_cast<size_t>(M) * ((c.vocab_size + 127) / 128) * 4));
+  return FDLLM_OK;
+}
+
 int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDesc>& reqs, const float* bias,
-                        int ld_bias, int causal_block, void* out, cudaStream_t s) {
+                        int ld_bias, int causal_block, void* out, cudaStream_t s, int max_l_hint) {
   const fdllm_config& c = h->cfg;
   const int nreq = static_cast<int>(reqs.size());
   FDLLM_TRY(ensure_ws(h, M, nreq));
@@ -212,19 +292,11 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
   int max_q = 0, max_l = 0;
   for (const ReqDesc& r : reqs) {
     max_q = std::max(max_q, r.n_q);
-    max_l = std::max(max_l, r.attend_len);
+    max_l = std::max(max_l, r.plen_dev ? r.cap : r.attend_len);
   }
-  // key splits for the attention: enough CTAs to cover the SMs at small batch
-  const int qtiles = (max_q + 15) / 16;
-  const int base_ctas = qtiles * c.num_key_value_heads * nreq;
-  int n_splits = 1, split_len = std::max(64, static_cast<int>(round_up(std::max(max_l, 1), 64)));
-  if (h->dtype == FDLLM_BFLOAT16 && bias == nullptr && causal_block == 0 && base_ctas < h->num_sms) {
-    const int want = std::min((2 * h->num_sms + base_ctas - 1) / base_ctas, (max_l + 63) / 64);
-    if (want > 1) {
-      split_len = static_cast<int>(round_up((max_l + want - 1) / want, 64));
-      n_splits = (max_l + split_len - 1) / split_len;
-    }
-  }
+  if (max_l_hint > 0) max_l = max_l_hint;
+  int n_splits, split_len;
+  plan_attention(h, max_q, max_l, nreq, bias != nullptr || causal_block != 0, &n_splits, &split_len);
   if (n_splits > 1) {
     FDLLM_TRY(h->attn_po.ensure(static_cast<size_t>(n_splits) * M * c.num_attention_heads * c.head_dim));
     FDLLM_TRY(h->attn_pl.ensure(static_cast<size_t>(n_splits) * M * c.num_attention_heads));
@@ -369,6 +441,7 @@ int fdllm_create(const fdllm_config* cfg, int device, fdllm_handle** out) {
     return fail(FDLLM_ERR_UNSUPPORTED, "fp32 path needs sizes divisible by 32, qkv by 128, head_dim dividing 128");
   }
   CUDA_TRY(cudaSetDevice(device));
+  CUDA_TRY(init_kernel_attributes());
   fdllm_handle* h = new fdllm_handle();
   h->cfg = c;
   h->device = device;
@@ -407,7 +480,11 @@ int fdllm_destroy(fdllm_handle* h) {
   for (auto* b : {&h->splitk, &h->attn_po, &h->attn_pl, &h->conf_part, &h->tmp_maxp, &h->dec.cmax}) b->release();
   h->reqs.release();
   if (h->dec.host) cudaFreeHost(h->dec.host);
+  if (h->dec.host_params) cudaFreeHost(h->dec.host_params);
   for (cudaEvent_t e : h->prof_ev) cudaEventDestroy(e);
+  release_step_graphs(h);
+  h->dec.plen.release();
+  if (h->dec.stream) cudaStreamDestroy(h->dec.stream);
   delete h;
   return FDLLM_OK;
 }
@@ -651,12 +728,13 @@ int fdllm_profile_read(fdllm_handle* h, double* out4) {
     CUDA_TRY(cudaEventElapsedTime(&t, h->prof_ev[i], h->prof_ev[i + 1]));
     ms += t;
   }
-  out4[0] = ms;
+  out4[0] = ms + h->prof_ms_extra;
   out4[1] = h->prof_bytes;
-  out4[2] = static_cast<double>(h->prof_used / 2);
+  out4[2] = static_cast<double>(h->prof_used / 2 + h->prof_launch_extra);
   out4[3] = h->prof_flops;
   h->prof_used = 0;
-  h->prof_bytes = h->prof_flops = 0.0;
+  h->prof_bytes = h->prof_flops = h->prof_ms_extra = 0.0;
+  h->prof_launch_extra = 0;
   return FDLLM_OK;
 }
 
