@@ -22,6 +22,7 @@ namespace fdllm {
 
 constexpr int kQT = 16;  // query tokens per CTA
 constexpr int kKT = 64;  // keys per shared-memory tile
+constexpr int kMaxSplits = kMaxAttnSplits;
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -57,6 +58,8 @@ __device__ __forceinline__ uint32_t tile_off(int key, int c) {
 
 template <int HD>
 __global__ void attn_mma_kernel(const AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int kChunks = HD / 8;          // 16-byte chunks per key row
   constexpr int kTileBytes = kKT * HD * 2;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -257,27 +260,51 @@ __global__ void attn_mma_kernel(const AttnArgs a) {
 // Merge key splits: out = sum_s w_s o_s / sum_s w_s with w_s = exp(lse_s - max lse).
 template <typename T>
 __global__ void attn_combine_kernel(const AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  // Split weights w_s = exp(lse_s - max) computed once into shared memory (warp 0), then every
+  // thread sums its head_dim element over the splits with independent, unrolled loads.
+  __shared__ float w[kMaxSplits];
+  __shared__ float inv_den;
   const int tok = blockIdx.x, qh = blockIdx.y;
-  float mx = -INFINITY;
-  for (int s = 0; s < a.n_splits; ++s)
-    mx = fmaxf(mx, a.part_lse[(static_cast<size_t>(s) * a.m_total + tok) * a.hq + qh]);
-  for (int d = threadIdx.x; d < a.hd; d += blockDim.x) {
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < a.n_splits; ++s) {
-      const size_t rowi = (static_cast<size_t>(s) * a.m_total + tok) * a.hq + qh;
-      const float lse = a.part_lse[rowi];
-      const float w = (lse == -INFINITY) ? 0.f : expf(lse - mx);
-      num += w * a.part_o[rowi * a.hd + d];
-      den += w;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x < 32) {
+    float l[kMaxSplits / 32];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kMaxSplits / 32; ++i) {
+      const int s = lane + 32 * i;
+      l[i] = s < a.n_splits ? a.part_lse[(static_cast<size_t>(s) * a.m_total + tok) * a.hq + qh] : -INFINITY;
+      mx = fmaxf(mx, l[i]);
     }
-    static_cast<T*>(a.out)[static_cast<size_t>(tok) * a.hq * a.hd + qh * a.hd + d] =
-        from_f<T>(den > 0.f ? num / den : 0.f);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float den = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxSplits / 32; ++i) {
+      const float wi = (l[i] == -INFINITY) ? 0.f : expf(l[i] - mx);
+      w[lane + 32 * i] = wi;
+      den += wi;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
+    if (lane == 0) inv_den = den > 0.f ? 1.f / den : 0.f;
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < a.hd; d += blockDim.x) {
+    float num = 0.f;
+#pragma unroll 8
+    for (int s = 0; s < a.n_splits; ++s)
+      num += w[s] * a.part_o[((static_cast<size_t>(s) * a.m_total + tok) * a.hq + qh) * a.hd + d];
+    static_cast<T*>(a.out)[static_cast<size_t>(tok) * a.hq * a.hd + qh * a.hd + d] = from_f<T>(num * inv_den);
   }
 }
 
 // CUDA-core attention: one warp per (token, query head); dims split over lanes (hd <= 128).
 template <typename T>
 __global__ void attn_simt_kernel(const AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int req = blockIdx.z;
   const ReqDesc r = a.reqs[req];
@@ -324,13 +351,9 @@ static int launch_mma(const AttnArgs& a, int max_q, cudaStream_t s) {
   constexpr int smem = 4 * kKT * HD * 2;
   cudaError_t e;
   dim3 grid((max_q + kQT - 1) / kQT, a.hkv, a.n_reqs * a.n_splits);
-  attn_mma_kernel<HD><<<grid, G * 32, smem, s>>>(a);
-  count_launch();
-  e = cudaGetLastError();
+  e = launch_k(attn_mma_kernel<HD>, grid, dim3(G * 32), smem, s, a);
   if (e != cudaSuccess || a.n_splits == 1) return e;
-  attn_combine_kernel<bf16><<<dim3(a.m_total, a.hq), 128, 0, s>>>(a);
-  count_launch();
-  return cudaGetLastError();
+  return launch_k(attn_combine_kernel<bf16>, dim3(a.m_total, a.hq), dim3(128), 0, s, a);
 }
 
 int init_gemm_tc_attributes();
@@ -353,10 +376,8 @@ int launch_attention(const AttnArgs& a, int max_q, int dtype, cudaStream_t s) {
   b.n_splits = 1;
   const int per_block = 4;
   dim3 grid((max_q * a.hq + per_block - 1) / per_block, 1, a.n_reqs);
-  if (dtype == 1) attn_simt_kernel<bf16><<<grid, per_block * 32, 0, s>>>(b);
-  else attn_simt_kernel<float><<<grid, per_block * 32, 0, s>>>(b);
-  count_launch();
-  return cudaGetLastError();
+  if (dtype == 1) return launch_k(attn_simt_kernel<bf16>, grid, dim3(per_block * 32), 0, s, b);
+  return launch_k(attn_simt_kernel<float>, grid, dim3(per_block * 32), 0, s, b);
 }
 
 }  // namespace fdllm

@@ -134,6 +134,7 @@ struct Driver {
       const unsigned long long gen = g_ws_generation.load();
       h->cap_prof.clear();
       h->capturing = true;
+      const long long launches_before = launch_count();
       CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
       const int rc = record(kind, s0, len);
       cudaGraph_t graph = nullptr;
@@ -156,6 +157,9 @@ struct Driver {
       sg.gen = gen;
       sg.mask_id = mask_id;
       sg.thr = thr;
+      // recorded launches did not run; they are counted when the graph replays
+      sg.n_kernels = static_cast<int>(launch_count() - launches_before);
+      count_launch(-sg.n_kernels);
       const cudaError_t ei = cudaGraphInstantiate(&sg.exec, graph, 0);
       cudaGraphDestroy(graph);
       sg.prof.swap(h->cap_prof);
@@ -164,6 +168,7 @@ struct Driver {
       g = &h->dec.graphs.back().second;
     }
     CUDA_TRY(cudaGraphLaunch(g->exec, s));
+    count_launch(g->n_kernels);
     CUDA_TRY(cudaStreamSynchronize(s));
     if (h->prof) {
       for (const ProfPair& pp : g->prof) {

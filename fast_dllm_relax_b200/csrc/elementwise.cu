@@ -3,6 +3,7 @@
 #include <math.h>
 
 #include <atomic>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -13,10 +14,20 @@ static std::atomic<long long> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("FDLLM_PDL");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
 // ---- embed (model/cuda.py:698-699) ----------------------------------------------------------
 template <typename T>
 __global__ void embed_kernel(const int* __restrict__ ids, const T* __restrict__ table, int vocab, int hidden,
                              T* __restrict__ out, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x;
   const int id = ids[i];
   const bool ok = id >= 0 && id < vocab;
@@ -30,11 +41,10 @@ int launch_embed(const int* ids, int n, const void* table, int vocab, int hidden
                  cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   if (dtype == 1)
-    embed_kernel<bf16><<<n, 256, 0, s>>>(ids, static_cast<const bf16*>(table), vocab, hidden, static_cast<bf16*>(out), err);
-  else
-    embed_kernel<float><<<n, 256, 0, s>>>(ids, static_cast<const float*>(table), vocab, hidden, static_cast<float*>(out), err);
-  count_launch();
-  return cudaGetLastError();
+    return launch_k(embed_kernel<bf16>, dim3(n), dim3(256), 0, s, ids, static_cast<const bf16*>(table), vocab, hidden,
+                    static_cast<bf16*>(out), err);
+  return launch_k(embed_kernel<float>, dim3(n), dim3(256), 0, s, ids, static_cast<const float*>(table), vocab, hidden,
+                  static_cast<float*>(out), err);
 }
 
 // ---- RMSNorm (model/cuda.py:269-275): fp32 mean square, rsqrt, cast, then x weight ------------
@@ -52,8 +62,11 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 template <typename T>
 __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ out, int hidden,
-                               float eps) {
+                               float eps, T* __restrict__ copy_to) {
   __shared__ float red[32];
+  pdl_trigger();
+  pdl_wait();
+
   const T* xr = x + static_cast<size_t>(blockIdx.x) * hidden;
   T* orow = out + static_cast<size_t>(blockIdx.x) * hidden;
   float ss = 0.f;
@@ -63,23 +76,23 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w,
   }
   const float var = block_sum(ss, red) / static_cast<float>(hidden);
   const float rs = rsqrtf(var + eps);
+  T* crow = copy_to ? copy_to + static_cast<size_t>(blockIdx.x) * hidden : nullptr;
   for (int j = threadIdx.x; j < hidden; j += blockDim.x) {
-    const float xn = round_t<T>(to_f<T>(xr[j]) * rs);
+    const T xv = xr[j];
+    const float xn = round_t<T>(to_f<T>(xv) * rs);
     orow[j] = from_f<T>(to_f<T>(w[j]) * xn);
+    if (crow) crow[j] = xv;  // the residual stream starts as a copy of the input
   }
 }
 
 int launch_rmsnorm(const void* x, const void* w, void* out, int rows, int hidden, float eps, int dtype,
-                   cudaStream_t s) {
+                   cudaStream_t s, void* copy_x_to) {
   if (rows <= 0) return cudaSuccess;
   if (dtype == 1)
-    rmsnorm_kernel<bf16><<<rows, 256, 0, s>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(w),
-                                              static_cast<bf16*>(out), hidden, eps);
-  else
-    rmsnorm_kernel<float><<<rows, 256, 0, s>>>(static_cast<const float*>(x), static_cast<const float*>(w),
-                                               static_cast<float*>(out), hidden, eps);
-  count_launch();
-  return cudaGetLastError();
+    return launch_k(rmsnorm_kernel<bf16>, dim3(rows), dim3(256), 0, s, static_cast<const bf16*>(x),
+                    static_cast<const bf16*>(w), static_cast<bf16*>(out), hidden, eps, static_cast<bf16*>(copy_x_to));
+  return launch_k(rmsnorm_kernel<float>, dim3(rows), dim3(256), 0, s, static_cast<const float*>(x),
+                  static_cast<const float*>(w), static_cast<float*>(out), hidden, eps, static_cast<float*>(copy_x_to));
 }
 
 // ---- RoPE tables (model/cuda.py:278-300): inv_freq = exp(-ln(theta) * i / half) in fp32 ----------
@@ -110,6 +123,8 @@ int launch_rope_tables(void* cos_t, void* sin_t, int max_pos, int hd, float thet
 
 // ---- per-call request preparation --------------------------------------------------------------
 __global__ void prepare_kernel(const ReqBatch b, ReqDesc* table, TokenMaps tok, int max_pos, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x;
   if (i >= b.n) return;
   ReqDesc r = b.r[i];
@@ -142,9 +157,7 @@ __global__ void prepare_kernel(const ReqBatch b, ReqDesc* table, TokenMaps tok, 
 
 int launch_prepare(const ReqBatch& b, ReqDesc* dev_table, TokenMaps tok, int max_pos, int* err, cudaStream_t s) {
   if (b.n <= 0) return cudaSuccess;
-  prepare_kernel<<<b.n, 128, 0, s>>>(b, dev_table, tok, max_pos, err);
-  count_launch();
-  return cudaGetLastError();
+  return launch_k(prepare_kernel, dim3(b.n), dim3(128), 0, s, b, dev_table, tok, max_pos, err);
 }
 
 // ---- confidence (model/metal.py:316-374): first-index argmax, maxp = 1 / sum exp(l - max) -------
@@ -178,6 +191,8 @@ __device__ __forceinline__ Top warp_merge(Top t) {
 
 // Partials from the fused lm_head epilogue: [rows, n_slabs, 4] = (max, argmax bits, sum, target).
 __global__ void conf_combine_kernel(const float* __restrict__ part, int rows, int n_slabs, int* ids, float* maxp) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + warp;
   if (row >= rows) return;
@@ -195,13 +210,13 @@ __global__ void conf_combine_kernel(const float* __restrict__ part, int rows, in
 
 int launch_conf_combine(const float* part, int rows, int n_slabs, int* ids, float* maxp, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  conf_combine_kernel<<<(rows + 7) / 8, 256, 0, s>>>(part, rows, n_slabs, ids, maxp);
-  count_launch();
-  return cudaGetLastError();
+  return launch_k(conf_combine_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, part, rows, n_slabs, ids, maxp);
 }
 
 // The same reduction over materialised fp32 logits [rows, vocab] (three passes per row).
 __global__ void conf_logits_kernel(const float* __restrict__ logits, int vocab, int* ids, float* maxp) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red_m[32];
   __shared__ int red_i[32];
   __shared__ float red_s[32];
@@ -241,13 +256,13 @@ __global__ void conf_logits_kernel(const float* __restrict__ logits, int vocab, 
 
 int launch_conf_from_logits(const float* logits, int rows, int vocab, int* ids, float* maxp, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  conf_logits_kernel<<<rows, 512, 0, s>>>(logits, vocab, ids, maxp);
-  count_launch();
-  return cudaGetLastError();
+  return launch_k(conf_logits_kernel, dim3(rows), dim3(512), 0, s, logits, vocab, ids, maxp);
 }
 
 // log_softmax(logits)[target] per row from the fused partials (runners.py:877-881 on the device).
 __global__ void lse_combine_kernel(const float* __restrict__ part, int rows, int n_slabs, float* logprob) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + warp;
   if (row >= rows) return;
@@ -266,9 +281,7 @@ __global__ void lse_combine_kernel(const float* __restrict__ part, int rows, int
 
 int launch_lse_combine(const float* part, int rows, int n_slabs, float* logprob, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  lse_combine_kernel<<<(rows + 7) / 8, 256, 0, s>>>(part, rows, n_slabs, logprob);
-  count_launch();
-  return cudaGetLastError();
+  return launch_k(lse_combine_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, part, rows, n_slabs, logprob);
 }
 
 // ---- unmask decision (runtime.py:158-181 shift, 794-805 rule), one warp ------------------------
@@ -281,6 +294,8 @@ int launch_lse_combine(const float* part, int rows, int n_slabs, float* logprob,
 __global__ void unmask_kernel(const int* __restrict__ ids, const float* __restrict__ maxp, int rows, int* block,
                               int sub_start, int sub_len, int partial, int mask_id, double threshold, int* out_tok,
                               float* out_conf, int* out_unmask, int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int j = threadIdx.x;  // window position
   const bool in = j < sub_len;
   int tok = 0;
@@ -328,10 +343,8 @@ int launch_unmask(const int* ids, const float* maxp, int rows, int* block, int s
                   int mask_id, double threshold, int* out_tok, float* out_conf, int* out_unmask, int* status,
                   cudaStream_t s) {
   if (sub_len <= 0 || sub_len > 32) return cudaErrorInvalidValue;
-  unmask_kernel<<<1, 32, 0, s>>>(ids, maxp, rows, block, sub_start, sub_len, partial, mask_id,
-                                 threshold, out_tok, out_conf, out_unmask, status);
-  count_launch();
-  return cudaGetLastError();
+  return launch_k(unmask_kernel, dim3(1), dim3(32), 0, s, ids, maxp, rows, block, sub_start, sub_len, partial, mask_id,
+                  threshold, out_tok, out_conf, out_unmask, status);
 }
 
 // ---- bounded-wait self test: spin on a flag that nothing sets; give up and report ----------

@@ -18,6 +18,8 @@ __global__ void __launch_bounds__(256) gemm_simt_f32_kernel(const float* __restr
   __shared__ float ws[kSimtK][128 + 1];
   __shared__ float xs[kSimtK][kSimtTok + 1];
   __shared__ float acc[kSimtTok * 128];
+  pdl_trigger();
+  pdl_wait();
   const int slab = blockIdx.x, tile = blockIdx.y;
   const int tok0 = tile * kSimtTok;
   const int tid = threadIdx.x;
@@ -58,15 +60,13 @@ __global__ void __launch_bounds__(256) gemm_simt_f32_kernel(const float* __restr
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[(tt * 4 + j) * 128 + tf * 4 + i] = c[i][j];
   __syncthreads();
-  gemm_epilogue<float>(g, acc, kSimtTok, tok0, slab);
+  gemm_epilogue<float>(g, acc, kSimtTok, tok0, slab, 0, kSimtTok);
 }
 
 int launch_gemm_simt_f32(const GemmArgs& a, const float* W, const float* X, cudaStream_t s) {
   if (a.K % kSimtK != 0) return cudaErrorInvalidValue;
   dim3 grid(a.n_slabs, (a.M + kSimtTok - 1) / kSimtTok, 1);
-  gemm_simt_f32_kernel<<<grid, 256, 0, s>>>(W, X, a);
-  count_launch();
-  return cudaGetLastError();
+  return launch_k(gemm_simt_f32_kernel, grid, dim3(256), 0, s, W, X, a);
 }
 
 }  // namespace fdllm

@@ -11,9 +11,9 @@
 // into a multi-stage shared-memory ring (128-byte swizzle, K-major); thread 32 issues
 // tcgen05.mma (kind::f16, fp32 accumulate in TMEM) and frees each ring slot with tcgen05.commit;
 // then all 4 warps drain the TMEM accumulator (each warp reads its 32-lane quarter with
-// tcgen05.ld) into a shared fp32 tile and run the fused epilogue.  Small grids use split-K: each
-// split writes an fp32 partial tile, and the last CTA to arrive (an atomic counter that resets
-// itself) sums the partials in split order, so results are deterministic.
+// tcgen05.ld) into a shared fp32 tile and run the fused epilogue.  Small grids use split-K over a
+// thread-block cluster: the partial tiles stay in shared memory and the cluster members reduce
+// disjoint token rows through distributed shared memory, in split order (deterministic).
 //
 // Every mbarrier wait is bounded (kWaitLimitNs); on expiry the kernel records an error code,
 // drains its own in-flight TMA copies (bounded), frees its TMEM and returns.
@@ -30,7 +30,9 @@ struct TcCfg {
   static constexpr int kA = 128 * 64 * 2;  // weight tile: 128 rows x 64 bf16
   static constexpr int kB = NT * 64 * 2;   // activation tile: NT tokens x 64 bf16
   static constexpr int kStage = kA + kB;
-  static constexpr int kStages = NT <= 16 ? 10 : (NT <= 64 ? 8 : (NT <= 128 ? 6 : 4));
+  // Ring depth: for NT <= 128 the CTA stays under ~110 KB of shared memory, so a CTA of the next
+  // projection (launched early, prefetching its weights) can sit beside a draining one on each SM.
+  static constexpr int kStages = NT <= 16 ? 6 : (NT <= 32 ? 5 : (NT <= 64 ? 4 : (NT <= 128 ? 3 : 4)));
   static constexpr int kTmemCols = NT < 32 ? 32 : NT;
   static constexpr int kAcc = NT * 128 * 4;  // fp32 epilogue tile (reuses the ring)
   static constexpr int kPipe = kStages * kStage;
@@ -56,7 +58,6 @@ __global__ void __launch_bounds__(128, 1)
   uint64_t* empty = full + C::kStages;
   uint64_t* accf = empty + C::kStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
-  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -73,7 +74,6 @@ __global__ void __launch_bounds__(128, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(accf, 1);
-    *last_flag = 0;
     mbar_fence_init();
     tma_prefetch_map(&tmA);
     tma_prefetch_map(&tmB);
@@ -86,20 +86,14 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();  // the next kernel may launch now and start streaming its own weights
 
   if (threadIdx.x == 0) {
     // ---------------- TMA producer ----------------
     const uint64_t pol_w = l2_policy_evict_first();  // weights stream through once
     const uint64_t pol_x = l2_policy_evict_last();   // activations are re-read by every slab
-    int issued = 0;
-    for (int i = 0; i < nk; ++i) {
+    auto load_a = [&](int i) {
       const int s = i % C::kStages;
-      const uint32_t ph = (i / C::kStages) & 1u;
-      if (!mbar_wait(&empty[s], ph ^ 1u)) {
-        report_error(g.err, kErrTimeoutProducer);
-        break;
-      }
-      mbar_arrive_expect_tx(&full[s], C::kStage);
       const int k0 = (kb0 + i) * 64;
       uint8_t* a = sA + s * C::kA;
       if (g.paired) {
@@ -109,7 +103,30 @@ __global__ void __launch_bounds__(128, 1)
       } else {
         tma_load_2d(a, &tmA, &full[s], k0, slab * 128, pol_w);
       }
-      tma_load_2d(sB + s * C::kB, &tmB, &full[s], k0, tok0, pol_x);
+    };
+    auto load_b = [&](int i) {
+      const int s = i % C::kStages;
+      tma_load_2d(sB + s * C::kB, &tmB, &full[s], (kb0 + i) * 64, tok0, pol_x);
+    };
+    // Weights do not depend on the previous kernel: fill the ring with them before waiting for it.
+    const int pre = min(nk, C::kStages);
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], C::kStage);  // A + B bytes; the B half lands after the wait
+      load_a(i);
+    }
+    pdl_wait();
+    for (int i = 0; i < pre; ++i) load_b(i);
+    int issued = pre;
+    for (int i = pre; i < nk; ++i) {
+      const int s = i % C::kStages;
+      const uint32_t ph = (i / C::kStages) & 1u;
+      if (!mbar_wait(&empty[s], ph ^ 1u)) {
+        report_error(g.err, kErrTimeoutProducer);
+        break;
+      }
+      mbar_arrive_expect_tx(&full[s], C::kStage);
+      load_a(i);
+      load_b(i);
       ++issued;
     }
     // Drain: every copy this thread issued must have landed before shared memory is reused.
@@ -142,6 +159,7 @@ __global__ void __launch_bounds__(128, 1)
   __syncwarp();
 
   // ---------------- epilogue: TMEM -> shared fp32 tile ----------------
+  pdl_wait();  // every thread below reads or writes memory the previous kernel may still touch
   if (!mbar_wait(accf, 0)) report_error(g.err, kErrTimeoutEpilogue);
   tc_fence_after_sync();
   __syncthreads();  // the producer's drain is complete before the ring is overwritten
@@ -165,46 +183,57 @@ __global__ void __launch_bounds__(128, 1)
     tmem_dealloc(tmem, C::kTmemCols);
   }
 
-  // ---------------- split-K: last CTA reduces in split order ----------------
+  // ---------------- split-K: reduction across the thread-block cluster ----------------
+  // The g.splits CTAs of one (slab, token tile) form one cluster.  Each keeps its fp32 partial tile
+  // in shared memory; member r then sums token rows [r*NT/S, (r+1)*NT/S) over all members' tiles,
+  // read through distributed shared memory in rank (= split) order -- deterministic, no global
+  // round trip -- and runs the epilogue for those rows only.
+  int row0 = 0, row1 = NT;
   if (g.splits > 1) {
-    float* part = g.partials + (static_cast<size_t>(slab) * g.n_tok_tiles + tile) * g.splits * (NT * 128);
-    for (int idx = threadIdx.x; idx < NT * 128; idx += blockDim.x)
-      __stcg(&part[static_cast<size_t>(split) * NT * 128 + idx], acc[idx]);
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int* ctr = g.counters + slab * g.n_tok_tiles + tile;
-      const int prev = atomicAdd(ctr, 1);
-      const int last = (prev == g.splits - 1);
-      if (last) atomicExch(ctr, 0);
-      *last_flag = last;
+    constexpr int kMaxS = 16;
+    const uint32_t S = static_cast<uint32_t>(g.splits);
+    const uint32_t rank = cluster_ctarank();
+    row0 = static_cast<int>(rank * NT / S);
+    row1 = static_cast<int>((rank + 1) * NT / S);
+    cluster_sync();  // every member's partial tile is complete
+    const uint32_t acc_addr = smem_addr(acc);
+    float4* acc4 = reinterpret_cast<float4*>(acc);
+    for (int c = row0 * 32 + threadIdx.x; c < row1 * 32; c += blockDim.x) {
+      float4 v[kMaxS];
+#pragma unroll
+      for (int m = 0; m < kMaxS; ++m)
+        v[m] = (static_cast<uint32_t>(m) < S) ? ld_dsmem_f4(map_shared_rank(acc_addr + c * 16, m))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int m = 0; m < kMaxS; ++m) {
+        if (static_cast<uint32_t>(m) < S) {
+          sum.x += v[m].x;
+          sum.y += v[m].y;
+          sum.z += v[m].z;
+          sum.w += v[m].w;
+        }
+      }
+      acc4[c] = sum;  // only this member reads or writes these rows from here on
     }
-    __syncthreads();
-    if (!*last_flag) return;
-    __threadfence();
-    for (int idx = threadIdx.x; idx < NT * 128; idx += blockDim.x) {
-      float sum = 0.f;
-      for (int s = 0; s < g.splits; ++s)
-        sum += (s == split) ? acc[idx] : __ldcg(&part[static_cast<size_t>(s) * NT * 128 + idx]);
-      acc[idx] = sum;
-    }
-    __syncthreads();
+    cluster_sync();  // no member leaves while another may still read its tile
   }
-  gemm_epilogue<bf16>(g, acc, NT, tok0, slab);
+  gemm_epilogue<bf16>(g, acc, NT, tok0, slab, row0, row1);
 }
 
 template <int NT>
 static int launch_nt(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, cudaStream_t s) {
   using C = TcCfg<NT>;
   dim3 grid(a.n_slabs, a.n_tok_tiles, a.splits);
-  gemm_tc_kernel<NT><<<grid, 128, C::kSmem, s>>>(tmA, tmB, a);
-  count_launch();
-  return cudaGetLastError();
+  return launch_kc(gemm_tc_kernel<NT>, grid, dim3(128), C::kSmem, s, a.splits, tmA, tmB, a);
 }
 
 template <int NT>
 static cudaError_t set_attr() {
-  return cudaFuncSetAttribute(gemm_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<NT>::kSmem);
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<NT>::kSmem);
+  // split-K clusters of up to 16 CTAs (above the portable 8)
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_tc_kernel<NT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
 }
 
 int init_gemm_tc_attributes() {

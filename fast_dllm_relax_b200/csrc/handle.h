@@ -86,6 +86,7 @@ struct StepGraph {
   unsigned long long gen = 0;  // g_ws_generation at capture
   int mask_id = 0;             // unmask parameters baked into the captured launch
   double thr = 0.0;
+  int n_kernels = 0;           // kernel nodes, counted as launches at every replay
   std::vector<ProfPair> prof;
 };
 
@@ -135,8 +136,7 @@ struct fdllm_handle {
   DevBuf<uint8_t> h, xn, q, attn, act, scratch_k, scratch_v;
   DevBuf<int> tok_req, tok_pos, tok_row, tmp_ids, targets;
   DevBuf<ReqDesc> reqs;
-  DevBuf<float> splitk, attn_po, attn_pl, conf_part, tmp_maxp;
-  DevBuf<int> counters;
+  DevBuf<float> attn_po, attn_pl, conf_part, tmp_maxp;
   DecodeState dec;
 
   // per-launch CUDA-event timing of the projection GEMM (fdllm_profile_enable / _read)

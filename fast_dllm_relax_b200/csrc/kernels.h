@@ -27,6 +27,7 @@ struct ReqDesc {
   int attend_rel;
 };
 
+constexpr int kMaxAttnSplits = 64;  // key splits merged by the attention combine kernel
 constexpr int kMaxReqsPerLaunch = 48;  // keeps ReqBatch under the classic 4 KB parameter limit
 
 struct ReqBatch {
@@ -78,10 +79,8 @@ struct GemmArgs {
   int paired;               // gate/up pairing (N = 2*I; slab s covers rows [64s, 64s+64) and I + same)
   int n_slabs;              // N / 128 (or I / 64 when paired)
   int n_tok_tiles;
-  int splits;               // split-K factor
+  int splits;               // split-K factor = cluster size (<= 16)
   int kb_per_split;         // 64-wide k blocks per split
-  float* partials;          // split-K workspace
-  int* counters;            // split-K arrival counters [n_slabs * n_tok_tiles] (self-resetting)
   int* err;
   Epilogue epi;
 };
@@ -105,9 +104,56 @@ struct AttnArgs {
   int* err;
 };
 
-// ---- launch accounting ---------------------------------------------------------------------
+// ---- launch accounting / programmatic dependent launch -------------------------------------
 void count_launch(int n = 1);
 long long launch_count();
+bool pdl_enabled();  // FDLLM_PDL=0 in the environment disables programmatic dependent launch
+
+// Launch `kernel` with the programmatic-stream-serialization attribute (when enabled).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// launch_k with a (1, 1, cluster_z) thread-block cluster (cluster_z == 1: no cluster).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kc(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, int cluster_z,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_z > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = static_cast<unsigned>(cluster_z);
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  count_launch();
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 // ---- launchers (return a cudaError_t) --------------------------------------------------------
 int launch_gemm_tc(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int nt, cudaStream_t s);
@@ -121,7 +167,7 @@ int init_kernel_attributes();  // opt-in shared memory sizes; once per device, b
 int launch_embed(const int* ids, int n, const void* table, int vocab, int hidden, void* out, int dtype, int* err,
                  cudaStream_t s);
 int launch_rmsnorm(const void* x, const void* w, void* out, int rows, int hidden, float eps, int dtype,
-                   cudaStream_t s);
+                   cudaStream_t s, void* copy_x_to = nullptr);
 int launch_rope_tables(void* cos_t, void* sin_t, int max_pos, int hd, float theta, int dtype, cudaStream_t s);
 int launch_prepare(const ReqBatch& b, ReqDesc* dev_table, TokenMaps tok, int max_pos, int* err, cudaStream_t s);
 int launch_conf_combine(const float* part, int rows, int n_slabs, int* ids, float* maxp, cudaStream_t s);

@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -163,21 +164,14 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
   const int kblocks = g->K / 64;
   const int tiles = g->n_slabs * g->n_tok_tiles;
   int splits = 1;
-  if (tiles < h->num_sms) {
-    splits = std::max(1, std::min(kblocks, h->num_sms / tiles));
+  if (tiles < h->num_sms) {  // split K over a cluster of at most 16 CTAs
+    splits = std::max(1, std::min({kblocks, h->num_sms / tiles, 16}));
     const int kpb = (kblocks + splits - 1) / splits;
     splits = (kblocks + kpb - 1) / kpb;
   }
   g->splits = splits;
   g->kb_per_split = (kblocks + splits - 1) / splits;
   return nt;
-}
-
-// Split-K workspace a plan needs (floats, counters).
-static void gemm_workspace(const GemmArgs& g, int nt, size_t* floats, size_t* counters) {
-  const size_t tiles = static_cast<size_t>(g.n_slabs) * g.n_tok_tiles;
-  *floats = g.splits > 1 ? tiles * g.splits * nt * 128 : 0;
-  *counters = g.splits > 1 ? tiles : 0;
 }
 
 static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epilogue epi, cudaStream_t s) {
@@ -187,14 +181,6 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
   g.err = h->err.p;
   g.epi = epi;
   if (h->dtype == FDLLM_FLOAT32) return timed_launch(h, g, s, launch_simt_thunk, w.ptr, X, 0);
-  if (g.splits > 1) {
-    size_t nf, nc;
-    gemm_workspace(g, nt, &nf, &nc);
-    FDLLM_TRY(h->splitk.ensure(nf));
-    FDLLM_TRY(h->counters.ensure(nc, true));
-    g.partials = h->splitk.p;
-    g.counters = h->counters.p;
-  }
   CUtensorMap tmB;
   FDLLM_TRY(make_map(&tmB, X, M, g.K, nt));
   return timed_launch(h, g, s, launch_tc_thunk, &w.map, &tmB, nt);
@@ -210,7 +196,7 @@ static void plan_attention(const fdllm_handle* h, int max_q, int max_l, int nreq
   *n_splits = 1;
   *split_len = std::max(64, static_cast<int>(round_up(std::max(max_l, 1), 64)));
   if (h->dtype == FDLLM_BFLOAT16 && !dense && base_ctas < h->num_sms) {
-    const int want = std::min((2 * h->num_sms + base_ctas - 1) / base_ctas, (max_l + 63) / 64);
+    const int want = std::min({(2 * h->num_sms + base_ctas - 1) / base_ctas, (max_l + 63) / 64, kMaxAttnSplits});
     if (want > 1) {
       *split_len = static_cast<int>(round_up((max_l + want - 1) / want, 64));
       *n_splits = (max_l + *split_len - 1) / *split_len;
@@ -246,24 +232,6 @@ static TokenMaps token_maps(fdllm_handle* h) { return TokenMaps{h->tok_req.p, h-
 int fdllm::reserve_workspace(fdllm_handle* h, int M, int nreq, int max_l) {
   FDLLM_TRY(ensure_ws(h, M, nreq));
   const fdllm_config& c = h->cfg;
-  size_t nf = 0, nc = 0;
-  std::vector<const Weight*> ws{&h->lm};
-  for (const LayerW& L : h->layers) {
-    ws.push_back(&L.qkv);
-    ws.push_back(&L.o);
-    ws.push_back(&L.gu);
-    ws.push_back(&L.down);
-  }
-  for (const Weight* w : ws) {
-    GemmArgs g{};
-    const int nt = plan_gemm(h, *w, M, &g);
-    size_t f, n;
-    gemm_workspace(g, nt, &f, &n);
-    nf = std::max(nf, f);
-    nc = std::max(nc, n);
-  }
-  if (nf) FDLLM_TRY(h->splitk.ensure(nf));
-  if (nc) FDLLM_TRY(h->counters.ensure(nc, true));
   int n_splits, split_len;
   plan_attention(h, M, max_l, nreq, false, &n_splits, &split_len);
   if (n_splits > 1) {
@@ -286,8 +254,6 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     for (int i = 0; i < b.n; ++i) b.r[i] = reqs[first + i];
     CUDA_TRY(launch_prepare(b, h->reqs.p, token_maps(h), c.max_positions, h->err.p, s));
   }
-  const size_t row_bytes = static_cast<size_t>(c.hidden_size) * h->esz;
-  CUDA_TRY(cudaMemcpyAsync(h->h.p, x, M * row_bytes, cudaMemcpyDeviceToDevice, s));
 
   int max_q = 0, max_l = 0;
   for (const ReqDesc& r : reqs) {
@@ -314,7 +280,9 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
 
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const LayerW& L = h->layers[l];
-    CUDA_TRY(launch_rmsnorm(h->h.p, L.ln1, h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s));
+    // layer 0 reads the input embeddings and starts the residual stream h as their copy
+    CUDA_TRY(launch_rmsnorm(l == 0 ? x : h->h.p, L.ln1, h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s,
+                            l == 0 ? h->h.p : nullptr));
     Epilogue e = base;
     e.kind = kEpiQkvRope;
     e.layer = l;
@@ -474,10 +442,10 @@ int fdllm_destroy(fdllm_handle* h) {
   for (auto* b : {&h->rope_cos, &h->rope_sin, &h->h, &h->xn, &h->q, &h->attn, &h->act, &h->scratch_k, &h->scratch_v,
                   &h->dec.k, &h->dec.v, &h->dec.x, &h->dec.hid})
     b->release();
-  for (auto* b : {&h->err, &h->tok_req, &h->tok_pos, &h->tok_row, &h->tmp_ids, &h->targets, &h->counters, &h->dec.ids,
+  for (auto* b : {&h->err, &h->tok_req, &h->tok_pos, &h->tok_row, &h->tmp_ids, &h->targets, &h->dec.ids,
                   &h->dec.block, &h->dec.cids, &h->dec.out})
     b->release();
-  for (auto* b : {&h->splitk, &h->attn_po, &h->attn_pl, &h->conf_part, &h->tmp_maxp, &h->dec.cmax}) b->release();
+  for (auto* b : {&h->attn_po, &h->attn_pl, &h->conf_part, &h->tmp_maxp, &h->dec.cmax}) b->release();
   h->reqs.release();
   if (h->dec.host) cudaFreeHost(h->dec.host);
   if (h->dec.host_params) cudaFreeHost(h->dec.host_params);
@@ -744,9 +712,9 @@ long long fdllm_workspace_bytes(fdllm_handle* h) {
   for (auto* b : {&h->h, &h->xn, &h->q, &h->attn, &h->act, &h->scratch_k, &h->scratch_v, &h->rope_cos, &h->rope_sin,
                   &h->dec.k, &h->dec.v, &h->dec.x, &h->dec.hid})
     t += static_cast<long long>(b->bytes());
-  for (auto* b : {&h->splitk, &h->attn_po, &h->attn_pl, &h->conf_part, &h->tmp_maxp, &h->dec.cmax})
+  for (auto* b : {&h->attn_po, &h->attn_pl, &h->conf_part, &h->tmp_maxp, &h->dec.cmax})
     t += static_cast<long long>(b->bytes());
-  for (auto* b : {&h->err, &h->tok_req, &h->tok_pos, &h->tok_row, &h->tmp_ids, &h->targets, &h->counters, &h->dec.ids,
+  for (auto* b : {&h->err, &h->tok_req, &h->tok_pos, &h->tok_row, &h->tmp_ids, &h->targets, &h->dec.ids,
                   &h->dec.block, &h->dec.cids, &h->dec.out})
     t += static_cast<long long>(b->bytes());
   return t + static_cast<long long>(h->reqs.bytes());
