@@ -10,8 +10,8 @@
 // shared memory serves all G heads.  K/V tiles of 64 keys are double-buffered with cp.async into a
 // XOR-swizzled layout and read with ldmatrix; QK^T and PV run on mma.sync m16n8k16 (bf16 in,
 // fp32 accumulate) with an online (flash) softmax in registers and quad shuffles for the row
-// reductions.  Long key ranges are split across CTAs; a combine kernel merges the splits by their
-// log-sum-exp.
+// reductions.  Long key ranges are split across the CTAs of a thread-block cluster, which merge
+// their partial outputs by log-sum-exp through distributed shared memory.
 // fp32: a CUDA-core kernel, one warp per (token, head), online softmax with warp-shuffle dots.
 #include <algorithm>
 
@@ -22,7 +22,6 @@ namespace fdllm {
 
 constexpr int kQT = 16;  // query tokens per CTA
 constexpr int kKT = 64;  // keys per shared-memory tile
-constexpr int kMaxSplits = kMaxAttnSplits;
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -75,8 +74,11 @@ __global__ void attn_mma_kernel(const AttnArgs a) {
   const int tq0 = qtile * kQT;
   if (tq0 >= r.n_q) return;
   const int L = r.attend_len;
-  const int key0 = split * a.split_len;
-  int key1 = min(L, key0 + a.split_len);
+  // Keys split evenly over this request's own length (read on the device, so a captured graph
+  // adapts as the prefix grows); a.split_len is a lower bound.
+  const int split_len = a.n_splits == 1 ? L : max(a.split_len, ((L + a.n_splits - 1) / a.n_splits + 63) / 64 * 64);
+  const int key0 = split * split_len;
+  int key1 = min(L, key0 + split_len);
   const bool implicit_mask = (a.bias == nullptr && a.causal_block > 0);
   if (implicit_mask) {  // keys past the last query's block are masked for every row of this tile
     const int tq_last = min(tq0 + kQT, r.n_q) - 1;
@@ -242,61 +244,60 @@ __global__ void attn_mma_kernel(const AttnArgs a) {
       }
     }
   } else {
+    // Key splits of one (request, query tile, KV head) form a thread-block cluster.  Each member
+    // leaves its normalized partial O and log-sum-exp in shared memory (the K/V tiles are no longer
+    // needed); member r then merges query rows [r*R/S, (r+1)*R/S) over all members through
+    // distributed shared memory: out = sum_s w_s o_s / sum_s w_s, w_s = exp(lse_s - max lse).
+    __shared__ float s_lse[kQT * 8];
+    float* o_s = reinterpret_cast<float*>(smem);  // [16 * G][HD] fp32
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      if (!valid_row[h]) continue;
+      const int rr = warp * 16 + g8 + h * 8;
       const float inv = l_run[h] > 0.f ? 1.f / l_run[h] : 0.f;
-      const size_t rowi = (static_cast<size_t>(split) * a.m_total + tok_row[h]) * a.hq + qh_row[h];
-      float* op = a.part_o + rowi * HD;
 #pragma unroll
-      for (int n = 0; n < HD / 8; ++n) {
-        *reinterpret_cast<float2*>(op + n * 8 + 2 * t4) = make_float2(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
+      for (int n = 0; n < HD / 8; ++n)
+        *reinterpret_cast<float2*>(o_s + rr * HD + n * 8 + 2 * t4) = make_float2(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
+      if (t4 == 0) s_lse[rr] = (valid_row[h] && l_run[h] > 0.f) ? m_run[h] + logf(l_run[h]) : -INFINITY;
+    }
+    cluster_sync();  // every member's partial is in its shared memory
+    constexpr int kMaxS = kMaxAttnSplits;
+    const uint32_t S = static_cast<uint32_t>(a.n_splits);
+    const uint32_t rank = cluster_ctarank();
+    const int rows = kQT * G;
+    const int r0 = static_cast<int>(rank * rows / S), r1 = static_cast<int>((rank + 1) * rows / S);
+    const uint32_t o_addr = smem_addr(o_s), lse_addr = smem_addr(s_lse);
+    bf16* out = static_cast<bf16*>(a.out);
+    for (int idx = threadIdx.x; idx < (r1 - r0) * (HD / 4); idx += blockDim.x) {
+      const int rr = r0 + idx / (HD / 4), c4 = idx % (HD / 4);
+      const int tq = tq0 + rr / G;
+      if (tq >= r.n_q) continue;
+      float l[kMaxS];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int m = 0; m < kMaxS; ++m) {
+        l[m] = (static_cast<uint32_t>(m) < S) ? ld_dsmem_f32(map_shared_rank(lse_addr + rr * 4, m)) : -INFINITY;
+        mx = fmaxf(mx, l[m]);
       }
-      if (t4 == 0) a.part_lse[rowi] = (l_run[h] > 0.f) ? m_run[h] + logf(l_run[h]) : -INFINITY;
+      float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+      float den = 0.f;
+#pragma unroll
+      for (int m = 0; m < kMaxS; ++m) {
+        if (static_cast<uint32_t>(m) < S && l[m] != -INFINITY) {
+          const float w = expf(l[m] - mx);
+          const float4 v = ld_dsmem_f4(map_shared_rank(o_addr + (rr * HD + c4 * 4) * 4, m));
+          num.x += w * v.x;
+          num.y += w * v.y;
+          num.z += w * v.z;
+          num.w += w * v.w;
+          den += w;
+        }
+      }
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      bf16* op = out + static_cast<size_t>(r.q_tok0 + tq) * (a.hq * HD) + (kvh * G + rr % G) * HD + c4 * 4;
+      *reinterpret_cast<__nv_bfloat162*>(op) = __floats2bfloat162_rn(num.x * inv, num.y * inv);
+      *reinterpret_cast<__nv_bfloat162*>(op + 2) = __floats2bfloat162_rn(num.z * inv, num.w * inv);
     }
-  }
-}
-
-// Merge key splits: out = sum_s w_s o_s / sum_s w_s with w_s = exp(lse_s - max lse).
-template <typename T>
-__global__ void attn_combine_kernel(const AttnArgs a) {
-  pdl_trigger();
-  pdl_wait();
-  // Split weights w_s = exp(lse_s - max) computed once into shared memory (warp 0), then every
-  // thread sums its head_dim element over the splits with independent, unrolled loads.
-  __shared__ float w[kMaxSplits];
-  __shared__ float inv_den;
-  const int tok = blockIdx.x, qh = blockIdx.y;
-  const int lane = threadIdx.x & 31;
-  if (threadIdx.x < 32) {
-    float l[kMaxSplits / 32];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < kMaxSplits / 32; ++i) {
-      const int s = lane + 32 * i;
-      l[i] = s < a.n_splits ? a.part_lse[(static_cast<size_t>(s) * a.m_total + tok) * a.hq + qh] : -INFINITY;
-      mx = fmaxf(mx, l[i]);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    float den = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxSplits / 32; ++i) {
-      const float wi = (l[i] == -INFINITY) ? 0.f : expf(l[i] - mx);
-      w[lane + 32 * i] = wi;
-      den += wi;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) den += __shfl_xor_sync(0xffffffffu, den, off);
-    if (lane == 0) inv_den = den > 0.f ? 1.f / den : 0.f;
-  }
-  __syncthreads();
-  for (int d = threadIdx.x; d < a.hd; d += blockDim.x) {
-    float num = 0.f;
-#pragma unroll 8
-    for (int s = 0; s < a.n_splits; ++s)
-      num += w[s] * a.part_o[((static_cast<size_t>(s) * a.m_total + tok) * a.hq + qh) * a.hd + d];
-    static_cast<T*>(a.out)[static_cast<size_t>(tok) * a.hq * a.hd + qh * a.hd + d] = from_f<T>(num * inv_den);
+    cluster_sync();  // no member leaves while another may still read its shared memory
   }
 }
 
@@ -351,9 +352,8 @@ static int launch_mma(const AttnArgs& a, int max_q, cudaStream_t s) {
   constexpr int smem = 4 * kKT * HD * 2;
   cudaError_t e;
   dim3 grid((max_q + kQT - 1) / kQT, a.hkv, a.n_reqs * a.n_splits);
-  e = launch_k(attn_mma_kernel<HD>, grid, dim3(G * 32), smem, s, a);
-  if (e != cudaSuccess || a.n_splits == 1) return e;
-  return launch_k(attn_combine_kernel<bf16>, dim3(a.m_total, a.hq), dim3(128), 0, s, a);
+  e = launch_kc(attn_mma_kernel<HD>, grid, dim3(G * 32), smem, s, a.n_splits, a);
+  return e;
 }
 
 int init_gemm_tc_attributes();
@@ -362,6 +362,8 @@ int init_kernel_attributes() {
   cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * kKT * 128 * 2);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * kKT * 64 * 2);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e == cudaSuccess) e = static_cast<cudaError_t>(init_gemm_tc_attributes());
   return e;
 }

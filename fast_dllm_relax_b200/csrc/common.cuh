@@ -125,6 +125,12 @@ __device__ __forceinline__ uint32_t map_shared_rank(uint32_t addr, uint32_t rank
   return r;
 }
 
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -132,6 +138,11 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
                : "r"(addr)
                : "memory");
   return v;
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA / tcgen05).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // ---- TMA (bulk tensor copies; plain CTA-local loads, no cluster forms) -----------------------

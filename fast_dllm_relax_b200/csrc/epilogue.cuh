@@ -45,7 +45,9 @@ constexpr int kEpiBatch = 4;  // chunks in flight per thread
 
 // Rows [row0, row1) of the tile are processed (a split-K cluster member owns a share of the rows).
 template <typename T>
-__device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, int slab, int row0, int row1) {
+// s_epi: 5120 bytes of shared scratch owned by the calling kernel.
+__device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, int slab, int row0, int row1,
+                              unsigned char* s_epi) {
   const Epilogue& e = g.epi;
   const int nthr = blockDim.x;
   const int tid = threadIdx.x;
@@ -79,13 +81,16 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
     }
     case kEpiResidual: {
       T* h = static_cast<T*>(e.resid);
+      const T* hs = e.resid_src ? static_cast<const T*>(e.resid_src) : h;
+      float* s_ss = reinterpret_cast<float*>(s_epi);  // [nt <= 64][CPR] chunk sums of squares
+      const bool want_ss = e.ss_out != nullptr && nt <= 64;
       for (int c0 = cbeg + tid; c0 < cend; c0 += nthr * kEpiBatch) {
         Chunk<T> r[kEpiBatch];
 #pragma unroll
         for (int b = 0; b < kEpiBatch; ++b) {  // loads first
           const int c = c0 + b * nthr;
           const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
-          if (c < cend && tok < g.M && F0 < g.N) r[b] = ld_chunk(h + (size_t)tok * e.ld_resid + F0);
+          if (c < cend && tok < g.M && F0 < g.N) r[b] = ld_chunk(hs + (size_t)tok * e.ld_resid + F0);
         }
 #pragma unroll
         for (int b = 0; b < kEpiBatch; ++b) {
@@ -93,9 +98,25 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
           const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
           if (c >= cend || tok >= g.M || F0 >= g.N) continue;
           Chunk<T> o;
+          float ss = 0.f;
 #pragma unroll
-          for (int v = 0; v < V; ++v) o.e[v] = from_f<T>(to_f<T>(r[b].e[v]) + round_t<T>(acc[t * 128 + f0 + v]));
+          for (int v = 0; v < V; ++v) {
+            o.e[v] = from_f<T>(to_f<T>(r[b].e[v]) + round_t<T>(acc[t * 128 + f0 + v]));
+            const float f = to_f<T>(o.e[v]);
+            ss = fmaf(f, f, ss);
+          }
           st_chunk(h + (size_t)tok * e.ld_resid + F0, o);
+          if (want_ss) s_ss[t * CPR + (c % CPR)] = ss;
+        }
+      }
+      if (want_ss) {  // per-row sum over this slab's 128 features, in chunk order (deterministic)
+        __syncthreads();
+        for (int t = row0 + tid; t < row1; t += nthr) {
+          const int tok = tok0 + t;
+          if (tok >= g.M) continue;
+          float ss = 0.f;
+          for (int j = 0; j < CPR; ++j) ss += s_ss[t * CPR + j];
+          e.ss_out[(size_t)tok * e.ss_ld + slab] = ss;
         }
       }
       break;
@@ -122,9 +143,9 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
     case kEpiQkvRope: {
       // Per-token destinations (RoPE position, cache row, K / V bases) once per tile, in shared
       // memory, so the element loop below carries no dependent global loads.
-      __shared__ int s_pos[256];
-      __shared__ T* s_kb[256];
-      __shared__ T* s_vb[256];
+      int* s_pos = reinterpret_cast<int*>(s_epi);                 // [256]
+      T** s_kb = reinterpret_cast<T**>(s_epi + 1024);            // [256]
+      T** s_vb = reinterpret_cast<T**>(s_epi + 1024 + 2048);     // [256]
       const T* bias = static_cast<const T*>(e.bias);
       for (int t = row0 + tid; t < row1; t += nthr) {
         const int tok = tok0 + t;

@@ -18,6 +18,7 @@ __global__ void __launch_bounds__(256) gemm_simt_f32_kernel(const float* __restr
   __shared__ float ws[kSimtK][128 + 1];
   __shared__ float xs[kSimtK][kSimtTok + 1];
   __shared__ float acc[kSimtTok * 128];
+  __shared__ __align__(16) unsigned char s_epi[5120];
   pdl_trigger();
   pdl_wait();
   const int slab = blockIdx.x, tile = blockIdx.y;
@@ -60,7 +61,7 @@ __global__ void __launch_bounds__(256) gemm_simt_f32_kernel(const float* __restr
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[(tt * 4 + j) * 128 + tf * 4 + i] = c[i][j];
   __syncthreads();
-  gemm_epilogue<float>(g, acc, kSimtTok, tok0, slab, 0, kSimtTok);
+  gemm_epilogue<float>(g, acc, kSimtTok, tok0, slab, 0, kSimtTok, s_epi);
 }
 
 int launch_gemm_simt_f32(const GemmArgs& a, const float* W, const float* X, cudaStream_t s) {

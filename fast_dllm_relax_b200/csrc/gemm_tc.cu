@@ -32,12 +32,12 @@ struct TcCfg {
   static constexpr int kStage = kA + kB;
   // Ring depth: for NT <= 128 the CTA stays under ~110 KB of shared memory, so a CTA of the next
   // projection (launched early, prefetching its weights) can sit beside a draining one on each SM.
-  static constexpr int kStages = NT <= 16 ? 6 : (NT <= 32 ? 5 : (NT <= 64 ? 4 : (NT <= 128 ? 3 : 4)));
+  static constexpr int kStages = NT <= 32 ? 5 : (NT <= 64 ? 4 : (NT <= 128 ? 3 : 4));
   static constexpr int kTmemCols = NT < 32 ? 32 : NT;
   static constexpr int kAcc = NT * 128 * 4;  // fp32 epilogue tile (reuses the ring)
   static constexpr int kPipe = kStages * kStage;
   static constexpr int kRegion = kPipe > kAcc ? kPipe : kAcc;
-  static constexpr int kBarBytes = 256;
+  static constexpr int kBarBytes = 512;  // barriers, TMEM slot, fused-norm row scales (NT <= 64)
   static constexpr int kSmem = 1024 + kRegion + kBarBytes;
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "MMA N must be a multiple of 16 in [16, 256]");
   static_assert(kA % 1024 == 0 && kB % 1024 == 0, "tiles must keep 1024-byte alignment");
@@ -57,7 +57,9 @@ __global__ void __launch_bounds__(128, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(base + C::kRegion);
   uint64_t* empty = full + C::kStages;
   uint64_t* accf = empty + C::kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* ready = accf + 1;  // fused-norm mode: B tile normalized in place, MMA may read it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ready + C::kStages);
+  __shared__ __align__(16) unsigned char s_epi[5120];  // epilogue scratch; norm weights in the mainloop
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -71,6 +73,7 @@ __global__ void __launch_bounds__(128, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 2);  // one arrival per normalizing warp
       mbar_init(&empty[s], 1);
     }
     mbar_init(accf, 1);
@@ -136,13 +139,60 @@ __global__ void __launch_bounds__(128, 1)
         break;
       }
     }
+  } else if (warp >= 2 && g.norm_x != nullptr) {
+    // ---------------- B normalizers (fused RMSNorm), warps 2 and 3 ----------------
+    // The B tile arrives by TMA un-normalized; these warps rewrite it in place as
+    // xn = T(w * T(x * rs)) (model/cuda.py:269-275) and then release it to the MMA issuer.
+    // rs[t] = rsqrt(mean(x[t]^2) + eps) comes from the per-slab sums of squares that the residual
+    // epilogue producing x left behind; the norm weights are staged in shared memory once.
+    const int wt = threadIdx.x - 64;  // 0..63
+    float* rs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(full) + 256);  // NT (<= 64) floats
+    bf16* s_w = reinterpret_cast<bf16*>(s_epi);                                      // K (<= 2560) weights
+    pdl_wait();
+    const int nrow = min(NT, g.M - tok0);
+    for (int t = wt; t < nrow; t += 64) {
+      const float* ssr = g.norm_ss + static_cast<size_t>(tok0 + t) * g.norm_ss_ld;
+      float ss = 0.f;
+      for (int j = 0; j < g.norm_ss_ld; ++j) ss += ssr[j];
+      rs[t] = rsqrtf(ss / static_cast<float>(g.K) + g.norm_eps);
+    }
+    const uint4* wsrc = static_cast<const uint4*>(g.norm_w);
+    for (int c = wt; c < g.K / 8; c += 64) reinterpret_cast<uint4*>(s_w)[c] = wsrc[c];
+    asm volatile("bar.sync 1, 64;" ::: "memory");  // the two normalizing warps only
+    const int cc = wt & 7;  // 16-byte chunk (8 columns) of the 64-column k-block this thread handles
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % C::kStages;
+      const uint32_t ph = (i / C::kStages) & 1u;
+      if (!mbar_wait(&full[s], ph)) {
+        report_error(g.err, kErrTimeoutMma);
+        break;
+      }
+      const uint4 wu = reinterpret_cast<const uint4*>(s_w)[(kb0 + i) * 8 + cc];
+      const bf16* w8 = reinterpret_cast<const bf16*>(&wu);
+      uint8_t* bt = sB + s * C::kB;
+      for (int t = wt >> 3; t < nrow; t += 8) {
+        uint4* p = reinterpret_cast<uint4*>(bt + (t >> 3) * 1024 + (t & 7) * 128 + ((cc ^ (t & 7)) << 4));
+        uint4 u = *p;
+        bf16* x8 = reinterpret_cast<bf16*>(&u);
+        const float r = rs[t];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const float xn = round_t<bf16>(__bfloat162float(x8[v]) * r);
+          x8[v] = __float2bfloat16_rn(__bfloat162float(w8[v]) * xn);
+        }
+        *p = u;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if ((wt & 31) == 0) mbar_arrive(&ready[s]);
+    }
   } else if (threadIdx.x == 32) {
     // ---------------- MMA issuer ----------------
     constexpr uint32_t idesc = umma_idesc_bf16(128, NT);
     for (int i = 0; i < nk; ++i) {
       const int s = i % C::kStages;
       const uint32_t ph = (i / C::kStages) & 1u;
-      if (!mbar_wait(&full[s], ph)) {
+      if (!mbar_wait(g.norm_x ? &ready[s] : &full[s], ph)) {
         report_error(g.err, kErrTimeoutMma);
         break;
       }
@@ -218,7 +268,7 @@ __global__ void __launch_bounds__(128, 1)
     }
     cluster_sync();  // no member leaves while another may still read its tile
   }
-  gemm_epilogue<bf16>(g, acc, NT, tok0, slab, row0, row1);
+  gemm_epilogue<bf16>(g, acc, NT, tok0, slab, row0, row1, s_epi);
 }
 
 template <int NT>

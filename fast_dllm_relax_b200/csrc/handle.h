@@ -136,7 +136,7 @@ struct fdllm_handle {
   DevBuf<uint8_t> h, xn, q, attn, act, scratch_k, scratch_v;
   DevBuf<int> tok_req, tok_pos, tok_row, tmp_ids, targets;
   DevBuf<ReqDesc> reqs;
-  DevBuf<float> attn_po, attn_pl, conf_part, tmp_maxp;
+  DevBuf<float> conf_part, tmp_maxp, ss;  // ss: per-slab row sums of squares
   DecodeState dec;
 
   // per-launch CUDA-event timing of the projection GEMM (fdllm_profile_enable / _read)

@@ -27,7 +27,7 @@ struct ReqDesc {
   int attend_rel;
 };
 
-constexpr int kMaxAttnSplits = 64;  // key splits merged by the attention combine kernel
+constexpr int kMaxAttnSplits = 8;  // key splits = attention cluster size (portable)
 constexpr int kMaxReqsPerLaunch = 48;  // keeps ReqBatch under the classic 4 KB parameter limit
 
 struct ReqBatch {
@@ -60,6 +60,9 @@ struct Epilogue {
   int ld_out;
   const void* bias;         // QkvRope: [N] in T
   void* resid;              // Residual: [M, ld_resid] in T
+  const void* resid_src;    // Residual: optional source of the residual (else resid); same layout
+  float* ss_out;            // Residual: optional [M, ss_ld] sum of squares of each new row's 128-feature
+  int ss_ld;                //   slab (the next RMSNorm's statistics, consumed by a fused-norm GEMM)
   int ld_resid;
   // QkvRope
   void* qout;               // [M, hq*hd] in T
@@ -81,6 +84,13 @@ struct GemmArgs {
   int n_tok_tiles;
   int splits;               // split-K factor = cluster size (<= 16)
   int kb_per_split;         // 64-wide k blocks per split
+  // Fused RMSNorm of the activations (tcgen05 path): when norm_x is set the B operand is
+  // rmsnorm(norm_x) * norm_w computed inside the GEMM (model/cuda.py:269-275) instead of TMA-loaded.
+  const void* norm_x;       // [M, K] in T
+  const void* norm_w;       // [K] in T
+  const float* norm_ss;     // [M, norm_ss_ld] per-128-feature sums of squares of norm_x rows
+  int norm_ss_ld;
+  float norm_eps;
   int* err;
   Epilogue epi;
 };
@@ -96,10 +106,8 @@ struct AttnArgs {
   const float* bias;        // dense path: [n_q, ld_bias] fp32 additive bias of request 0, or null
   int ld_bias;
   int causal_block;         // > 0 and bias null: implicit block-causal mask (query block >= key block)
-  int n_splits;             // key splits per (request, kv head, q tile)
-  int split_len;            // keys per split (multiple of 64)
-  float* part_o;            // [n_splits, M, hq, hd]
-  float* part_lse;          // [n_splits, M, hq]
+  int n_splits;             // key splits per (request, kv head, q tile) = cluster size
+  int split_len;            // minimum keys per split (multiple of 64)
   int m_total;              // M: activation rows of all requests
   int* err;
 };

@@ -174,12 +174,22 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
   return nt;
 }
 
-static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epilogue epi, cudaStream_t s) {
+// norm_w set (tcgen05 path only): X is the un-normalized input and the kernel applies RMSNorm
+// with weight norm_w while building its B operand.
+static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epilogue epi, cudaStream_t s,
+                    const void* norm_w = nullptr) {
   if (M <= 0) return FDLLM_OK;
   GemmArgs g{};
   const int nt = plan_gemm(h, w, M, &g);
   g.err = h->err.p;
   g.epi = epi;
+  if (norm_w != nullptr) {
+    g.norm_x = X;
+    g.norm_w = norm_w;
+    g.norm_ss = h->ss.p;
+    g.norm_ss_ld = h->cfg.hidden_size / 128;
+    g.norm_eps = h->cfg.rms_norm_eps;
+  }
   if (h->dtype == FDLLM_FLOAT32) return timed_launch(h, g, s, launch_simt_thunk, w.ptr, X, 0);
   CUtensorMap tmB;
   FDLLM_TRY(make_map(&tmB, X, M, g.K, nt));
@@ -198,8 +208,8 @@ static void plan_attention(const fdllm_handle* h, int max_q, int max_l, int nreq
   if (h->dtype == FDLLM_BFLOAT16 && !dense && base_ctas < h->num_sms) {
     const int want = std::min({(2 * h->num_sms + base_ctas - 1) / base_ctas, (max_l + 63) / 64, kMaxAttnSplits});
     if (want > 1) {
-      *split_len = static_cast<int>(round_up((max_l + want - 1) / want, 64));
-      *n_splits = (max_l + *split_len - 1) / *split_len;
+      *n_splits = want;
+      *split_len = 64;  // the kernel divides each request's own key range evenly
     }
   }
 }
@@ -221,6 +231,7 @@ static int ensure_ws(fdllm_handle* h, int M, int nreq) {
   FDLLM_TRY(h->tmp_maxp.ensure(m));
   FDLLM_TRY(h->targets.ensure(m));
   FDLLM_TRY(h->reqs.ensure(static_cast<size_t>(std::max(nreq, 1))));
+  FDLLM_TRY(h->ss.ensure(m * (c.hidden_size / 128 + 1)));
   return FDLLM_OK;
 }
 
@@ -234,10 +245,6 @@ int fdllm::reserve_workspace(fdllm_handle* h, int M, int nreq, int max_l) {
   const fdllm_config& c = h->cfg;
   int n_splits, split_len;
   plan_attention(h, M, max_l, nreq, false, &n_splits, &split_len);
-  if (n_splits > 1) {
-    FDLLM_TRY(h->attn_po.ensure(static_cast<size_t>(n_splits) * M * c.num_attention_heads * c.head_dim));
-    FDLLM_TRY(h->attn_pl.ensure(static_cast<size_t>(n_splits) * M * c.num_attention_heads));
-  }
   FDLLM_TRY(h->conf_part.ensure(static_cast<size_t>(M) * ((c.vocab_size + 127) / 128) * 4));
   return FDLLM_OK;
 }
@@ -263,10 +270,6 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
   if (max_l_hint > 0) max_l = max_l_hint;
   int n_splits, split_len;
   plan_attention(h, max_q, max_l, nreq, bias != nullptr || causal_block != 0, &n_splits, &split_len);
-  if (n_splits > 1) {
-    FDLLM_TRY(h->attn_po.ensure(static_cast<size_t>(n_splits) * M * c.num_attention_heads * c.head_dim));
-    FDLLM_TRY(h->attn_pl.ensure(static_cast<size_t>(n_splits) * M * c.num_attention_heads));
-  }
 
   Epilogue base{};
   base.hq = c.num_attention_heads;
@@ -278,17 +281,26 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
   base.rope_sin = h->rope_sin.p;
   base.max_pos = c.max_positions;
 
+  // Decode-sized calls fold each layer's input RMSNorm into the qkv projection (its CTAs normalize
+  // their B tiles in place, with row statistics left by the previous down projection); large calls
+  // normalize once in a separate kernel.
+  const bool fuse_norm = h->dtype == FDLLM_BFLOAT16 && M <= 64 && c.hidden_size <= 2560;
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const LayerW& L = h->layers[l];
-    // layer 0 reads the input embeddings and starts the residual stream h as their copy
-    CUDA_TRY(launch_rmsnorm(l == 0 ? x : h->h.p, L.ln1, h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s,
-                            l == 0 ? h->h.p : nullptr));
+    const void* layer_in = l == 0 ? x : h->h.p;
     Epilogue e = base;
     e.kind = kEpiQkvRope;
     e.layer = l;
     e.bias = L.qkv_b;
     e.qout = h->q.p;
-    FDLLM_TRY(run_gemm(h, L.qkv, h->xn.p, M, e, s));
+    if (fuse_norm && l > 0) {  // layer 0's input has no producer epilogue: normalized separately
+      FDLLM_TRY(run_gemm(h, L.qkv, layer_in, M, e, s, L.ln1));
+    } else {
+      // layer 0 reads the input embeddings and starts the residual stream h as their copy
+      CUDA_TRY(launch_rmsnorm(layer_in, L.ln1, h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s,
+                              l == 0 ? h->h.p : nullptr));
+      FDLLM_TRY(run_gemm(h, L.qkv, h->xn.p, M, e, s));
+    }
 
     AttnArgs a{};
     a.q = h->q.p;
@@ -305,8 +317,6 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     a.causal_block = causal_block;
     a.n_splits = n_splits;
     a.split_len = split_len;
-    a.part_o = h->attn_po.p;
-    a.part_lse = h->attn_pl.p;
     a.m_total = M;
     a.err = h->err.p;
     CUDA_TRY(launch_attention(a, max_q, h->dtype, s));
@@ -317,17 +327,23 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     e.ld_resid = c.hidden_size;
     FDLLM_TRY(run_gemm(h, L.o, h->attn.p, M, e, s));
 
-    CUDA_TRY(launch_rmsnorm(h->h.p, L.ln2, h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s));
     e = base;
     e.kind = kEpiSiluMul;
     e.out = h->act.p;
     e.ld_out = c.intermediate_size;
+    // gate_up streams 24 k-blocks per CTA; normalizing its B tiles in place would sit on every
+    // stage's critical path, so its RMSNorm stays a separate (small) kernel.
+    CUDA_TRY(launch_rmsnorm(h->h.p, L.ln2, h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s));
     FDLLM_TRY(run_gemm(h, L.gu, h->xn.p, M, e, s));
 
     e = base;
     e.kind = kEpiResidual;
     e.resid = h->h.p;
     e.ld_resid = c.hidden_size;
+    if (fuse_norm) {  // leave the statistics of the next layer's input RMSNorm
+      e.ss_out = h->ss.p;
+      e.ss_ld = c.hidden_size / 128;
+    }
     FDLLM_TRY(run_gemm(h, L.down, h->act.p, M, e, s));
   }
   // out == null (build_prefix_cache): the final hidden states are not needed; xn is free by now.
@@ -445,7 +461,7 @@ int fdllm_destroy(fdllm_handle* h) {
   for (auto* b : {&h->err, &h->tok_req, &h->tok_pos, &h->tok_row, &h->tmp_ids, &h->targets, &h->dec.ids,
                   &h->dec.block, &h->dec.cids, &h->dec.out})
     b->release();
-  for (auto* b : {&h->attn_po, &h->attn_pl, &h->conf_part, &h->tmp_maxp, &h->dec.cmax}) b->release();
+  for (auto* b : {&h->conf_part, &h->tmp_maxp, &h->ss, &h->dec.cmax}) b->release();
   h->reqs.release();
   if (h->dec.host) cudaFreeHost(h->dec.host);
   if (h->dec.host_params) cudaFreeHost(h->dec.host_params);
@@ -712,7 +728,7 @@ long long fdllm_workspace_bytes(fdllm_handle* h) {
   for (auto* b : {&h->h, &h->xn, &h->q, &h->attn, &h->act, &h->scratch_k, &h->scratch_v, &h->rope_cos, &h->rope_sin,
                   &h->dec.k, &h->dec.v, &h->dec.x, &h->dec.hid})
     t += static_cast<long long>(b->bytes());
-  for (auto* b : {&h->attn_po, &h->attn_pl, &h->conf_part, &h->tmp_maxp, &h->dec.cmax})
+  for (auto* b : {&h->conf_part, &h->tmp_maxp, &h->ss, &h->dec.cmax})
     t += static_cast<long long>(b->bytes());
   for (auto* b : {&h->err, &h->tok_req, &h->tok_pos, &h->tok_row, &h->tmp_ids, &h->targets, &h->dec.ids,
                   &h->dec.block, &h->dec.cids, &h->dec.out})
