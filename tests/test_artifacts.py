@@ -1,0 +1,89 @@
+"""Artifact directories and the TVM stand-in's module loading, on the CPU.
+
+The file set, the bf16-as-uint16 storage and the KV-cache manifest follow the reference's export
+and runner (fast_dllm_relax/export_utils.py:19-65, runners.py:68-76, 819-834, 925-972).
+"""
+
+import dataclasses
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from fast_dllm_relax_b200 import artifacts, install_tvm_shim
+from fast_dllm_relax_b200.config import TINY, TINY_MASK_ID, make_synthetic_params, param_names
+
+install_tvm_shim()
+import tvm  # noqa: E402
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_write_then_load_round_trip(tmp_path, dtype):
+    params = make_synthetic_params(TINY, seed=0, dtype=dtype, mask_id=TINY_MASK_ID)
+    d = artifacts.write_artifact(tmp_path / "a", TINY, params, dtype)
+    for f in (artifacts.LIBRARY, artifacts.PARAMS, artifacts.PARAM_NAMES, artifacts.DTYPE,
+              artifacts.KV_CACHE_MANIFEST, artifacts.CONFIG):
+        assert (d / f).exists(), f
+    assert (d / artifacts.PARAM_NAMES).read_text().splitlines() == param_names(TINY)
+    assert artifacts.read_dtype(d) == dtype
+    assert artifacts.read_config(d) == TINY
+    back = artifacts.load_params(d, "cpu", TINY)
+    assert len(back) == len(params)
+    for a, b in zip(params, back):
+        assert a.dtype == b.dtype and torch.equal(a, b)
+    with np.load(d / artifacts.PARAMS) as z:  # bf16 travels as its uint16 bit pattern
+        assert z["arr_0"].dtype == (np.uint16 if dtype == "bfloat16" else np.float32)
+
+
+def test_manifest_matches_reference_contract(tmp_path):
+    d = artifacts.write_artifact(tmp_path, TINY, make_synthetic_params(TINY, seed=0), "float32")
+    m = json.loads((d / artifacts.KV_CACHE_MANIFEST).read_text())
+    assert m == {"kv_cache": "inplace_bsnh_v1", "num_layers": 2, "num_kv_heads": 2, "head_dim": 64,
+                 "dtype": "float32"}
+    (d / artifacts.KV_CACHE_MANIFEST).write_text(json.dumps(dict(m, kv_cache="stacked_bhsd")))
+    with pytest.raises(RuntimeError, match="in-place KV cache"):
+        artifacts.read_kv_manifest(d)
+
+
+def test_config_inferred_without_config_file(tmp_path):
+    """A directory the reference exported has no config file: the architecture comes from the
+    parameter shapes and the manifest; eps / theta take the Qwen2.5 defaults or overrides."""
+    untied = dataclasses.replace(TINY, tie_word_embeddings=False, context_window_size=32768)
+    d = artifacts.write_artifact(tmp_path, untied, make_synthetic_params(untied, seed=0), "float32")
+    (d / artifacts.CONFIG).unlink()
+    assert artifacts.read_config(d) == untied
+    assert artifacts.read_config(d, rope_theta=1e4).rope_theta == 1e4
+
+
+def test_missing_array_and_bad_dtype_are_refused(tmp_path):
+    d = artifacts.write_artifact(tmp_path, TINY, make_synthetic_params(TINY, seed=0), "float32")
+    (d / artifacts.DTYPE).write_text("float16\n")
+    with pytest.raises(ValueError, match="not supported"):
+        artifacts.read_dtype(d)
+    (d / artifacts.DTYPE).write_text("float32\n")
+    with np.load(d / artifacts.PARAMS) as z:
+        arrs = {k: z[k] for k in z.files if k != "arr_3"}
+    np.savez(d / artifacts.PARAMS, **arrs)
+    with pytest.raises(ValueError, match="arr_3"):
+        artifacts.load_params(d, "cpu")
+
+
+def test_load_module_through_the_stand_in(tmp_path):
+    d = artifacts.write_artifact(tmp_path, TINY, make_synthetic_params(TINY, seed=0), "float32")
+    assert getattr(tvm, "IS_FDLLM_SHIM", False)
+    ex = tvm.runtime.load_module(str(d / artifacts.LIBRARY))
+    assert ex.cfg == TINY and ex.dtype == "float32"
+    # no CPU path: a VirtualMachine on the host refuses instead of falling back
+    with pytest.raises(RuntimeError, match="CUDA devices only"):
+        tvm.relax.VirtualMachine(ex, tvm.cpu(0))
+
+
+def test_runner_style_param_loading(tmp_path):
+    """runners.py:68-76: bf16 params rebuilt by empty(..., "bfloat16").copyfrom(uint16 array)."""
+    params = make_synthetic_params(TINY, seed=0, dtype="bfloat16")
+    d = artifacts.write_artifact(tmp_path, TINY, params, "bfloat16")
+    with np.load(d / artifacts.PARAMS) as z:
+        arr = z["arr_1"]
+        t = tvm.runtime.empty(arr.shape, "bfloat16", tvm.cpu(0)).copyfrom(arr)
+    assert torch.equal(t.torch, params[1])
