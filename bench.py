@@ -45,8 +45,15 @@ def _peaks() -> tuple[float, str]:
 
 
 def _traffic() -> dict | None:
-    p = REPO / "profiles" / "gemm_traffic.json"
-    return json.loads(p.read_text()) if p.exists() else None
+    """DRAM bytes per projection-GEMM launch (dram__bytes_read.sum + dram__bytes_write.sum from
+    one ncu capture), from the committed summary's `bytes_per_launch:` line."""
+    p = REPO / "profiles" / "gemm_tc_kernel_1p5b_p384.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("bytes_per_launch:"):
+            return {"bytes_per_launch": float(line.split(":", 1)[1])}
+    return None
 
 
 class ClockSampler:
@@ -101,10 +108,8 @@ class ClockSampler:
 
 
 def _dist():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    from fast_dllm_relax_b200.dp import world_info
+    return world_info()
 
 
 def make_prompt(seed: int) -> list[int]:
@@ -215,6 +220,7 @@ def main() -> None:
     import torch.distributed as dist
 
     from fast_dllm_relax_b200.config import QWEN_1_5B, QWEN_MASK_ID, make_synthetic_params
+    from fast_dllm_relax_b200 import dp
     from fast_dllm_relax_b200.engine import Engine
 
     world, rank, local = _dist()
@@ -226,7 +232,9 @@ def main() -> None:
     dev = torch.device("cuda", local)
     params = make_synthetic_params(QWEN_1_5B, seed=1, dtype="bfloat16", device=dev, mask_id=QWEN_MASK_ID)
     eng = Engine(QWEN_1_5B, params, dtype="bfloat16", device=local)
-    prompt = make_prompt(1000 + rank)
+    # batch 1 per GPU: the job is `world` requests, cut into one contiguous range per rank
+    (req,) = dp.request_range(world, world, rank)
+    prompt = make_prompt(1000 + req)
     gen_kw = dict(max_new_tokens=GEN_LEN, block_size=BLOCK, small_block_size=SUB_BLOCK, threshold=THRESHOLD,
                   use_block_cache=args.block_cache, mask_id=QWEN_MASK_ID, stop_token=None)
 
@@ -280,13 +288,9 @@ def main() -> None:
     # ms per 32-token block step (embed + forward_cached(32) + fused confidence + unmask) at P = 384
     blk = block_step_ms(eng, torch, dev)
 
-    red = torch.tensor([dec_ms, tot_ms, e2e_dec_s], dtype=torch.float64, device=dev)
-    cnt = torch.tensor([tokens, launches, e2e_tokens], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(red, op=dist.ReduceOp.MAX)
-        dist.all_reduce(cnt, op=dist.ReduceOp.SUM)
-    dec_ms, tot_ms, e2e_dec_s = red.tolist()
-    tokens, launches, e2e_tokens = cnt.tolist()
+    # off the decode path: max over ranks of the device-timed durations, sum of the work
+    (dec_ms, tot_ms, e2e_dec_s), (tokens, launches, e2e_tokens) = dp.reduce_max_sum(
+        [dec_ms, tot_ms, e2e_dec_s], [tokens, launches, e2e_tokens], device=dev)
 
     if rank == 0:
         peak, peak_kind = _peaks()
