@@ -61,6 +61,7 @@ SIGNATURES: dict[str, tuple] = {
     "fdllm_forward_cached_batch": (_I, [_P, ctypes.POINTER(FdllmRequest), _I, _P, _P, _P]),
     "fdllm_confidence": (_I, [_P, _P, _I, _P, _P, _P]),
     "fdllm_confidence_from_logits": (_I, [_P, _P, _I, _P, _P, _P]),
+    "fdllm_confidence_static": (_I, [_P, _P, _I, _P, _P, _P]),
     "fdllm_unmask": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, ctypes.c_double, _P, _P, _P, _P, _P]),
     "fdllm_token_logprob": (_I, [_P, _P, _I, _P, _P, _P]),
     "fdllm_generate": (_I, [_P, _P, _I, _I, _I, _I, ctypes.c_double, _I, _I, _I, _P, ctypes.POINTER(_I), _P, _P, _P]),

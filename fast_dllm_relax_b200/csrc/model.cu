@@ -737,3 +737,59 @@ long long fdllm_workspace_bytes(fdllm_handle* h) {
 }
 
 }  // extern "C"
+
+// ---- allocation-free confidence -------------------------------------------------------------
+// The partials of the fused lm_head confidence live in a fixed module-scope device array instead
+// of the handle's grown workspace, so the call allocates nothing.  Every (row, slab) entry the
+// combine kernel reads is written earlier in the same call, so nothing in the array has to start
+// at zero; it keeps the last call's contents.  One array per device, shared by every handle on it.
+namespace {
+constexpr size_t kStaticConfFloats = size_t(1) << 20;  // 4 MiB
+__device__ __align__(256) float g_static_conf_part[kStaticConfFloats];
+constexpr int kMaxStaticDevices = 64;
+std::mutex g_static_mu;
+float* g_static_conf_addr[kMaxStaticDevices] = {};
+}  // namespace
+
+extern "C" int fdllm_confidence_static(fdllm_handle* h, const void* hidden, int rows, int32_t* ids, float* maxp,
+                                       void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (rows <= 0 || hidden == nullptr || ids == nullptr || maxp == nullptr) return fail(FDLLM_ERR_INVALID, "bad confidence arguments");
+  const int n_slabs = (h->cfg.vocab_size + 127) / 128;
+  const size_t max_rows = kStaticConfFloats / (static_cast<size_t>(n_slabs) * 4);
+  if (static_cast<size_t>(rows) > max_rows)
+    return fail(FDLLM_ERR_INVALID, "fdllm_confidence_static: rows = " + std::to_string(rows) + " exceeds " +
+                                       std::to_string(max_rows) + ", the most the fixed 4 MiB scratch holds at vocab " +
+                                       std::to_string(h->cfg.vocab_size) + " (use fdllm_confidence)");
+  if (h->device < 0 || h->device >= kMaxStaticDevices) return fail(FDLLM_ERR_UNSUPPORTED, "device ordinal out of range");
+  float* part = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (g_static_conf_addr[h->device] == nullptr) {  // first call on this device
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_static_conf_part);
+      if (e != cudaSuccess || p == nullptr)
+        return fail(FDLLM_ERR_CUDA, std::string("cudaGetSymbolAddress(static confidence scratch): ") + cudaGetErrorString(e));
+      g_static_conf_addr[h->device] = static_cast<float*>(p);
+    }
+    part = g_static_conf_addr[h->device];
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Epilogue e{};
+  e.kind = kEpiConf;
+  e.part = part;
+  GemmArgs g{};
+  const int nt = plan_gemm(h, h->lm, rows, &g);
+  g.err = h->err.p;
+  g.epi = e;
+  if (h->dtype == FDLLM_FLOAT32) {
+    CUDA_TRY(launch_gemm_simt_f32(g, static_cast<const float*>(h->lm.ptr), static_cast<const float*>(hidden), s));
+  } else {
+    CUtensorMap tmB;
+    FDLLM_TRY(make_map(&tmB, hidden, rows, g.K, nt));
+    CUDA_TRY(launch_gemm_tc(g, h->lm.map, tmB, nt, s));
+  }
+  CUDA_TRY(launch_conf_combine(part, rows, n_slabs, ids, maxp, s));
+  return FDLLM_OK;
+}

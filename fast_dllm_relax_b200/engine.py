@@ -191,6 +191,16 @@ class Engine:
         _lib.check(self.lib.fdllm_confidence(self._h, h2.data_ptr(), n, ids.data_ptr(), maxp.data_ptr(), self._stream()))
         return ids, maxp
 
+    def confidence_static(self, hidden: torch.Tensor, ids: torch.Tensor, maxp: torch.Tensor) -> None:
+        """confidence() into caller-owned ids / maxp through fdllm_confidence_static, which
+        allocates no device memory (its scratch is a fixed 4 MiB device array per device)."""
+        h2 = self._act(hidden, "confidence_static")
+        n = h2.shape[0]
+        if ids.numel() < n or maxp.numel() < n or ids.dtype != torch.int32 or maxp.dtype != torch.float32:
+            raise ValueError("confidence_static: ids int32 and maxp float32 with at least rows elements")
+        _lib.check(self.lib.fdllm_confidence_static(self._h, h2.data_ptr(), n, ids.data_ptr(), maxp.data_ptr(),
+                                                    self._stream()))
+
     def confidence_from_logits(self, logits: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         l2 = logits.reshape(-1, self.cfg.vocab_size).to(self.device, torch.float32).contiguous()
         n = l2.shape[0]

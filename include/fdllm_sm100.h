@@ -168,6 +168,22 @@ FDLLM_API int fdllm_profile_read(fdllm_handle* h, double* out4);
 /* Bytes of device workspace the handle currently holds. */
 FDLLM_API long long fdllm_workspace_bytes(fdllm_handle* h);
 
+/* fdllm_confidence without any device allocation (no counterpart in the reference).  For callers
+ * that may not allocate device memory inside their step: an external memory pool or a fixed
+ * arena owns the device, or the step must never grow the handle's workspace.  The lm_head
+ * partials live in one fixed 4 MiB module-scope device array per device, shared by every handle
+ * on that device, so rows must satisfy rows * ceil(vocab / 128) * 16 <= 4 MiB (220 rows at vocab
+ * 151936); larger calls return FDLLM_ERR_INVALID with the limit in fdllm_last_error.
+ * - The first call on each device looks up the array's address (cudaGetSymbolAddress, which may
+ *   load the module); make that first call before any stream capture.
+ * - The array keeps the previous call's contents; nothing in it needs to start at zero, because
+ *   every entry a call reads is written earlier in that same call.
+ * - Calls whose kernels can overlap on one device (different streams, or different handles on the
+ *   same device) race on the shared array: order them on one stream or with events.
+ * Results are identical to fdllm_confidence. */
+FDLLM_API int fdllm_confidence_static(fdllm_handle* h, const void* hidden, int rows, int32_t* ids, float* maxp,
+                                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif
