@@ -365,6 +365,7 @@ int init_kernel_attributes() {
   if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (e == cudaSuccess) e = static_cast<cudaError_t>(init_gemm_tc_attributes());
+  if (e == cudaSuccess) e = static_cast<cudaError_t>(init_stack_attributes());
   return e;
 }
 

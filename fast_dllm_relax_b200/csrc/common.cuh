@@ -23,6 +23,7 @@ enum DeviceError : int {
   kErrPositionRange = 5,     // a RoPE position outside the precomputed table
   kErrCacheRange = 6,        // a KV write outside the cache capacity
   kErrTimeoutTest = 7,       // the bounded-wait self test expired (expected in that test)
+  kErrTimeoutBarrier = 8,    // the layer-stack kernel waited too long at a grid barrier or merge
 };
 
 __device__ __forceinline__ void report_error(int* err, int code) {
@@ -40,6 +41,12 @@ template <> __device__ __forceinline__ bf16 from_f<bf16>(float v) { return __flo
 
 // Round an fp32 value to the model dtype and widen it back (one op's result, in fp32 registers).
 template <typename T> __device__ __forceinline__ float round_t(float v) { return to_f<T>(from_f<T>(v)); }
+
+// Two values rounded to bf16 with one packed conversion (cvt.rn.bf16x2.f32; the scalar conversion
+// runs at a fraction of the ALU rate) and widened back: identical to two round_t<bf16> calls.
+__device__ __forceinline__ float2 round2_bf16(float a, float b) {
+  return __bfloat1622float2(__floats2bfloat162_rn(a, b));
+}
 
 // ---- time / addresses ---------------------------------------------------------------------
 __device__ __forceinline__ uint64_t global_timer_ns() {
@@ -95,6 +102,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
       if (mbar_try_wait(bar, parity)) return true;
     if (global_timer_ns() - t0 > kWaitLimitNs) return false;
   }
+}
+
+// Barrier `id` over the first `nthr` threads that reach it (a multiple of 32); id 0 with
+// nthr == blockDim.x is __syncthreads().
+__device__ __forceinline__ void named_sync(int id, int nthr) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthr) : "memory");
 }
 
 // ---- programmatic dependent launch ---------------------------------------------------------

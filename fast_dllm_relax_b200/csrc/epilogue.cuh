@@ -29,10 +29,12 @@ struct Chunk {
   };
 };
 
+// L2-only load (ld.global.cg): the persistent layer-stack kernel re-reads buffers that other CTAs
+// rewrite between its phases, so no epilogue may be served a stale line from this SM's L1.
 template <typename T>
 __device__ __forceinline__ Chunk<T> ld_chunk(const T* p) {
   Chunk<T> c;
-  c.u = *reinterpret_cast<const uint4*>(p);
+  c.u = __ldcg(reinterpret_cast<const uint4*>(p));
   return c;
 }
 
@@ -41,16 +43,31 @@ __device__ __forceinline__ void st_chunk(T* p, const Chunk<T>& c) {
   *reinterpret_cast<uint4*>(p) = c.u;
 }
 
+// Two values rounded to the model dtype and widened back (one packed conversion for bf16).
+template <typename T> __device__ __forceinline__ float2 round_pair(float a, float b);
+template <> __device__ __forceinline__ float2 round_pair<float>(float a, float b) { return make_float2(a, b); }
+template <> __device__ __forceinline__ float2 round_pair<bf16>(float a, float b) { return round2_bf16(a, b); }
+
+// dst[0], dst[1] = T(a), T(b) (one packed conversion for bf16).
+template <typename T> __device__ __forceinline__ void set_pair(T* dst, float a, float b);
+template <> __device__ __forceinline__ void set_pair<float>(float* dst, float a, float b) {
+  dst[0] = a;
+  dst[1] = b;
+}
+template <> __device__ __forceinline__ void set_pair<bf16>(bf16* dst, float a, float b) {
+  *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(a, b);
+}
+
 constexpr int kEpiBatch = 4;  // chunks in flight per thread
 
 // Rows [row0, row1) of the tile are processed (a split-K cluster member owns a share of the rows).
+// s_epi: 5120 bytes of shared scratch owned by the calling kernel.  The calling threads are
+// tid = 0..nthr-1 (a multiple of 32); they synchronise with named barrier `bar_id` (0 with
+// nthr == blockDim.x is __syncthreads()).
 template <typename T>
-// s_epi: 5120 bytes of shared scratch owned by the calling kernel.
 __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, int slab, int row0, int row1,
-                              unsigned char* s_epi) {
+                              unsigned char* s_epi, int tid, int nthr, int bar_id) {
   const Epilogue& e = g.epi;
-  const int nthr = blockDim.x;
-  const int tid = threadIdx.x;
   constexpr int V = Chunk<T>::V;
   constexpr int CPR = 128 / V;  // chunks per 128-feature row of the tile
   const int cbeg = row0 * CPR, cend = row1 * CPR;
@@ -63,7 +80,7 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
         if (tok >= g.M || F0 >= g.N) continue;
         Chunk<T> o;
 #pragma unroll
-        for (int v = 0; v < V; ++v) o.e[v] = from_f<T>(acc[t * 128 + f0 + v]);
+        for (int v = 0; v < V; v += 2) set_pair<T>(&o.e[v], acc[t * 128 + f0 + v], acc[t * 128 + f0 + v + 1]);
         st_chunk(out + (size_t)tok * e.ld_out + F0, o);
       }
       break;
@@ -74,8 +91,8 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
         const int t = c >> 5, f0 = (c & 31) * 4, tok = tok0 + t, F0 = slab * 128 + f0;
         if (tok >= g.M || F0 >= g.N) continue;
         const float* a = acc + t * 128 + f0;
-        *reinterpret_cast<float4*>(out + (size_t)tok * e.ld_out + F0) =
-            make_float4(round_t<T>(a[0]), round_t<T>(a[1]), round_t<T>(a[2]), round_t<T>(a[3]));
+        const float2 lo = round_pair<T>(a[0], a[1]), hi = round_pair<T>(a[2], a[3]);
+        *reinterpret_cast<float4*>(out + (size_t)tok * e.ld_out + F0) = make_float4(lo.x, lo.y, hi.x, hi.y);
       }
       break;
     }
@@ -100,17 +117,19 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
           Chunk<T> o;
           float ss = 0.f;
 #pragma unroll
-          for (int v = 0; v < V; ++v) {
-            o.e[v] = from_f<T>(to_f<T>(r[b].e[v]) + round_t<T>(acc[t * 128 + f0 + v]));
-            const float f = to_f<T>(o.e[v]);
-            ss = fmaf(f, f, ss);
+          for (int v = 0; v < V; v += 2) {
+            const float2 y = round_pair<T>(acc[t * 128 + f0 + v], acc[t * 128 + f0 + v + 1]);
+            const float2 z = round_pair<T>(to_f<T>(r[b].e[v]) + y.x, to_f<T>(r[b].e[v + 1]) + y.y);
+            set_pair<T>(&o.e[v], z.x, z.y);
+            ss = fmaf(z.x, z.x, ss);
+            ss = fmaf(z.y, z.y, ss);
           }
           st_chunk(h + (size_t)tok * e.ld_resid + F0, o);
           if (want_ss) s_ss[t * CPR + (c % CPR)] = ss;
         }
       }
       if (want_ss) {  // per-row sum over this slab's 128 features, in chunk order (deterministic)
-        __syncthreads();
+        named_sync(bar_id, nthr);
         for (int t = row0 + tid; t < row1; t += nthr) {
           const int tok = tok0 + t;
           if (tok >= g.M) continue;
@@ -130,11 +149,12 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
         if (tok >= g.M || j0 >= inter) continue;
         Chunk<T> o;
 #pragma unroll
-        for (int v = 0; v < V; ++v) {
-          const float gate = round_t<T>(acc[t * 128 + f0 + v]);
-          const float up = round_t<T>(acc[t * 128 + 64 + f0 + v]);
-          const float act = round_t<T>(gate * (1.0f / (1.0f + expf(-gate))));
-          o.e[v] = from_f<T>(act * up);
+        for (int v = 0; v < V; v += 2) {
+          const float2 gate = round_pair<T>(acc[t * 128 + f0 + v], acc[t * 128 + f0 + v + 1]);
+          const float2 up = round_pair<T>(acc[t * 128 + 64 + f0 + v], acc[t * 128 + 64 + f0 + v + 1]);
+          const float2 act = round_pair<T>(gate.x * (1.0f / (1.0f + expf(-gate.x))),
+                                           gate.y * (1.0f / (1.0f + expf(-gate.y))));
+          set_pair<T>(&o.e[v], act.x * up.x, act.y * up.y);
         }
         st_chunk(out + (size_t)tok * e.ld_out + j0, o);
       }
@@ -168,11 +188,15 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
         s_vb[t] = vb;
       }
       // Phase 1: projection + bias, rounded to the model dtype (the op's output tensor).
-      for (int idx = row0 * 128 + tid; idx < row1 * 128; idx += nthr) {
+      for (int idx = row0 * 128 + 2 * tid; idx < row1 * 128; idx += 2 * nthr) {  // pairs of features
         const int F = slab * 128 + (idx & 127);
-        if (F < g.N) acc[idx] = round_t<T>(acc[idx] + to_f<T>(bias[F]));
+        if (F < g.N) {
+          const float2 y = round_pair<T>(acc[idx] + to_f<T>(bias[F]), acc[idx + 1] + to_f<T>(bias[F + 1]));
+          acc[idx] = y.x;
+          acc[idx + 1] = y.y;
+        }
       }
-      __syncthreads();
+      named_sync(bar_id, nthr);
       // Phase 2: rotate q and k (partner element d +- hd/2 of the same head, inside this slab),
       // scatter q to qout and k / v to the request's cache row.
       const int hd = e.hd, half = e.hd >> 1, hq = e.hq, hkv = e.hkv;
@@ -205,10 +229,11 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
             const bool lo = d0 < half;
             const float* xp = lo ? x + half : x - half;
 #pragma unroll
-            for (int v = 0; v < V; ++v) {
-              const float rot = lo ? -xp[v] : xp[v];
-              o.e[v] = from_f<T>(round_t<T>(round_t<T>(x[v] * to_f<T>(cs[b].e[v])) +
-                                            round_t<T>(rot * to_f<T>(sn[b].e[v]))));
+            for (int v = 0; v < V; v += 2) {
+              const float r0 = lo ? -xp[v] : xp[v], r1 = lo ? -xp[v + 1] : xp[v + 1];
+              const float2 c = round_pair<T>(x[v] * to_f<T>(cs[b].e[v]), x[v + 1] * to_f<T>(cs[b].e[v + 1]));
+              const float2 sv = round_pair<T>(r0 * to_f<T>(sn[b].e[v]), r1 * to_f<T>(sn[b].e[v + 1]));
+              set_pair<T>(&o.e[v], c.x + sv.x, c.y + sv.y);  // T(round(c + s)) == T(c + s)
             }
             if (head < hq) {
               st_chunk(q + (size_t)tok * (hq * hd) + F0, o);
@@ -217,7 +242,7 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
             }
           } else if (s_vb[t] != nullptr) {
 #pragma unroll
-            for (int v = 0; v < V; ++v) o.e[v] = from_f<T>(x[v]);
+            for (int v = 0; v < V; v += 2) set_pair<T>(&o.e[v], x[v], x[v + 1]);
             st_chunk(s_vb[t] + (head - hq - hkv) * hd + d0, o);
           }
         }
@@ -232,12 +257,21 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
         if (tok >= g.M) continue;
         float best = -INFINITY;
         int best_i = 0x7fffffff;
+        float vals[4];
+        {
+          const float2 p0 = round_pair<T>(acc[t * 128 + lane], acc[t * 128 + lane + 32]);
+          const float2 p1 = round_pair<T>(acc[t * 128 + lane + 64], acc[t * 128 + lane + 96]);
+          vals[0] = p0.x;
+          vals[1] = p0.y;
+          vals[2] = p1.x;
+          vals[3] = p1.y;
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int f = lane + 32 * i;
           const int F = slab * 128 + f;
           if (F < g.N) {
-            const float v = round_t<T>(acc[t * 128 + f]);
+            const float v = vals[i];
             if (v > best || (v == best && F < best_i)) { best = v; best_i = F; }
           }
         }
@@ -251,7 +285,7 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int f = lane + 32 * i;
-          if (slab * 128 + f < g.N) sum += expf(round_t<T>(acc[t * 128 + f]) - best);
+          if (slab * 128 + f < g.N) sum += expf(vals[i] - best);
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
@@ -270,6 +304,13 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
     default:
       break;
   }
+}
+
+template <typename T>
+__device__ __forceinline__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, int slab, int row0,
+                                              int row1, unsigned char* s_epi) {
+  gemm_epilogue<T>(g, acc, nt, tok0, slab, row0, row1, s_epi, static_cast<int>(threadIdx.x),
+                   static_cast<int>(blockDim.x), 0);
 }
 
 }  // namespace fdllm

@@ -173,12 +173,13 @@ __global__ void __launch_bounds__(128, 1)
       for (int t = wt >> 3; t < nrow; t += 8) {
         uint4* p = reinterpret_cast<uint4*>(bt + (t >> 3) * 1024 + (t & 7) * 128 + ((cc ^ (t & 7)) << 4));
         uint4 u = *p;
-        bf16* x8 = reinterpret_cast<bf16*>(&u);
+        __nv_bfloat162* x2 = reinterpret_cast<__nv_bfloat162*>(&u);
         const float r = rs[t];
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          const float xn = round_t<bf16>(__bfloat162float(x8[v]) * r);
-          x8[v] = __float2bfloat16_rn(__bfloat162float(w8[v]) * xn);
+        for (int v = 0; v < 4; ++v) {
+          const float2 xf = __bfloat1622float2(x2[v]);
+          const float2 xn = round2_bf16(xf.x * r, xf.y * r);
+          x2[v] = __floats2bfloat162_rn(__bfloat162float(w8[2 * v]) * xn.x, __bfloat162float(w8[2 * v + 1]) * xn.y);
         }
         *p = u;
       }

@@ -137,6 +137,14 @@ struct fdllm_handle {
   DevBuf<int> tok_req, tok_pos, tok_row, tmp_ids, targets;
   DevBuf<ReqDesc> reqs;
   DevBuf<float> conf_part, tmp_maxp, ss;  // ss: per-slab row sums of squares
+  // persistent layer-stack kernel: weight maps and per-layer pointers (built at bind), partials,
+  // barrier / arrival counters (zeroed before every launch)
+  DevBuf<uint8_t> stack_maps, stack_layers;
+  DevBuf<float> stack_gpart, stack_apart, stack_alse;
+  DevBuf<unsigned> stack_sync;
+  bool stack_trace_on = false;            // fdllm_stack_trace_enable
+  DevBuf<unsigned long long> stack_trace; // per-CTA phase timeline of the last layer-stack launch
+  int stack_trace_grid = 0;
   DecodeState dec;
 
   // per-launch CUDA-event timing of the projection GEMM (fdllm_profile_enable / _read)
@@ -160,6 +168,10 @@ int check_handle(fdllm_handle* h);
 int forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDesc>& reqs, const float* bias, int ld_bias,
                  int causal_block, void* out, cudaStream_t s, int max_l_hint = 0);
 int reserve_workspace(fdllm_handle* h, int M, int nreq, int max_l);
+// The whole layer stack as one persistent launch when the call fits its envelope; *used is
+// FDLLM_OK when it ran, FDLLM_ERR_UNSUPPORTED when the caller must run the per-kernel loop.
+int stack_forward(fdllm_handle* h, const void* x, int M, const std::vector<ReqDesc>& reqs, int max_q, int max_l,
+                  void* out, cudaStream_t s, int* used);
 void release_step_graphs(fdllm_handle* h);
 int dense_forward(fdllm_handle* h, const void* x, const float* bias, int T, void* k, void* v, int cap, bool scratch,
                   void* out, cudaStream_t s);

@@ -240,12 +240,147 @@ static TokenMaps token_maps(fdllm_handle* h) { return TokenMaps{h->tok_req.p, h-
 // ---- the layer stack ----------------------------------------------------------------------
 // x: [M, hidden] input embeddings; reqs: host descriptors (q_tok0 / n_q filled); bias: dense fp32
 // bias of request 0 (or null), causal_block: implicit block-causal mask when bias is null.
+static int stack_reserve(fdllm_handle* h);
+
 int fdllm::reserve_workspace(fdllm_handle* h, int M, int nreq, int max_l) {
   FDLLM_TRY(ensure_ws(h, M, nreq));
+  if (M <= kStackRows) FDLLM_TRY(stack_reserve(h));
   const fdllm_config& c = h->cfg;
   int n_splits, split_len;
   plan_attention(h, M, max_l, nreq, false, &n_splits, &split_len);
   FDLLM_TRY(h->conf_part.ensure(static_cast<size_t>(M) * ((c.vocab_size + 127) / 128) * 4));
+  return FDLLM_OK;
+}
+
+// ---- persistent layer stack ------------------------------------------------------------------
+// FDLLM_STACK=1 selects the persistent layer-stack kernel for eligible calls.
+static bool stack_disabled() {
+  const char* v = std::getenv("FDLLM_STACK");
+  return v == nullptr || v[0] != '1';
+}
+
+// Tuning override "qkv,o,down,attn" of the layer-stack split factors (0 = planned value).
+static void stack_split_override(int* q, int* o, int* d, int* at) {
+  const char* v = std::getenv("FDLLM_STACK_SPLITS");
+  if (v == nullptr) return;
+  int x[4] = {0, 0, 0, 0};
+  if (std::sscanf(v, "%d,%d,%d,%d", &x[0], &x[1], &x[2], &x[3]) < 1) return;
+  if (x[0] > 0) *q = x[0];
+  if (x[1] > 0) *o = x[1];
+  if (x[2] > 0) *d = x[2];
+  if (x[3] > 0) *at = x[3];
+}
+
+// Plan of the layer-stack kernel for this call, or false when the call is outside its envelope
+// (then the per-kernel layer loop runs).
+static bool stack_plan(const fdllm_handle* h, int M, const std::vector<ReqDesc>& reqs, int max_l, StackArgs* a) {
+  const fdllm_config& c = h->cfg;
+  if (h->dtype != FDLLM_BFLOAT16 || stack_disabled() || M <= 0 || M > kStackRows) return false;
+  const int grid = h->num_sms;
+  const int H = c.hidden_size, I = c.intermediate_size, hq = c.num_attention_heads, hkv = c.num_key_value_heads;
+  const int hd = c.head_dim;
+  if ((hd != 64 && hd != 128) || hkv <= 0 || hq % hkv != 0 || hq / hkv > 6) return false;
+  const int nqkv = (hq + 2 * hkv) * hd, qd = hq * hd;
+  if (H % 128 != 0 || nqkv % 128 != 0 || qd % 64 != 0 || I % 64 != 0 || H / 8 > 384) return false;
+  const int s_qkv = nqkv / 128, s_o = H / 128, s_gu = I / 64, s_down = H / 128;
+  if (s_qkv > 64 || s_o > 64 || s_down > 64 || s_gu > grid || s_qkv > grid || s_o > grid) return false;
+  // Split-K: the fewest splits whose units fit the weight ring (prefetched whole while the
+  // previous phase runs), within the grid and the merge limit.
+  auto splits_for = [&](int slabs, int kbt) {
+    const int fit = (kbt + kStackStages - 1) / kStackStages;
+    return std::max(1, std::min({fit, grid / slabs, kStackMaxSplits, kbt}));
+  };
+  a->qkv_splits = splits_for(s_qkv, H / 64);
+  a->o_splits = splits_for(s_o, qd / 64);
+  a->down_splits = splits_for(s_down, I / 64);
+  int groups = 0;
+  for (const ReqDesc& r : reqs) groups += (r.n_q + 15) / 16 * hkv;
+  if (groups <= 0 || groups > 64) return false;
+  a->attn_groups = groups;
+  a->attn_splits = std::max(1, std::min({grid / groups, kStackMaxSplits, (std::max(max_l, 1) + 63) / 64}));
+  stack_split_override(&a->qkv_splits, &a->o_splits, &a->down_splits, &a->attn_splits);
+  auto ok_split = [&](int slabs, int kbt, int sp) { return sp >= 1 && sp <= kStackMaxSplits && sp <= kbt && slabs * sp <= grid; };
+  if (!ok_split(s_qkv, H / 64, a->qkv_splits) || !ok_split(s_o, qd / 64, a->o_splits) ||
+      !ok_split(s_down, I / 64, a->down_splits) || a->attn_splits < 1 || a->attn_splits > kStackMaxSplits ||
+      groups * a->attn_splits > grid)
+    return false;
+  auto max_nk = [](int kbt, int splits) { return (kbt + splits - 1) / splits; };
+  const int bmax = kStackBBytes / (kStackRows * 64 * 2);
+  if (max_nk(H / 64, a->qkv_splits) > bmax || max_nk(qd / 64, a->o_splits) > bmax || H / 64 > bmax ||
+      max_nk(I / 64, a->down_splits) > bmax)
+    return false;
+  return true;
+}
+
+// Partial and counter buffers at their largest sizes (units <= grid), so that no later call,
+// in particular none inside a stream capture, has to grow them.
+static int stack_reserve(fdllm_handle* h) {
+  const fdllm_config& c = h->cfg;
+  if (h->dtype != FDLLM_BFLOAT16 || c.num_key_value_heads <= 0) return FDLLM_OK;
+  const size_t grid = static_cast<size_t>(h->num_sms);
+  const size_t rows = 16 * static_cast<size_t>(c.num_attention_heads / c.num_key_value_heads);
+  FDLLM_TRY(h->stack_gpart.ensure(grid * kStackRows * 128));
+  FDLLM_TRY(h->stack_apart.ensure(grid * rows * c.head_dim));
+  FDLLM_TRY(h->stack_alse.ensure(grid * rows));
+  FDLLM_TRY(h->stack_sync.ensure(64 + static_cast<size_t>(c.num_hidden_layers) * kStackCtrPerLayer));
+  return FDLLM_OK;
+}
+
+int fdllm::stack_forward(fdllm_handle* h, const void* x, int M, const std::vector<ReqDesc>& reqs, int max_q,
+                         int max_l, void* out, cudaStream_t s, int* used) {
+  (void)max_q;
+  *used = FDLLM_ERR_UNSUPPORTED;
+  StackArgs a{};
+  if (!stack_plan(h, M, reqs, max_l, &a)) return FDLLM_OK;
+  const fdllm_config& c = h->cfg;
+  const int grid = h->num_sms;
+  FDLLM_TRY(stack_reserve(h));
+  const size_t n_sync = 64 + static_cast<size_t>(c.num_hidden_layers) * kStackCtrPerLayer;
+  CUtensorMap tm_h, tm_attn, tm_act;
+  FDLLM_TRY(make_map(&tm_h, h->h.p, M, c.hidden_size, kStackRows));
+  FDLLM_TRY(make_map(&tm_attn, h->attn.p, M, c.num_attention_heads * c.head_dim, kStackRows));
+  FDLLM_TRY(make_map(&tm_act, h->act.p, M, c.intermediate_size, kStackRows));
+  a.wmaps = reinterpret_cast<const CUtensorMap*>(h->stack_maps.p);
+  a.layers = reinterpret_cast<const StackLayer*>(h->stack_layers.p);
+  a.final_norm = h->final_norm;
+  a.x = x;
+  a.out = out ? out : h->xn.p;
+  a.h = h->h.p;
+  a.q = h->q.p;
+  a.attn = h->attn.p;
+  a.act = h->act.p;
+  a.ss = h->ss.p;
+  a.gpart = h->stack_gpart.p;
+  a.apart = h->stack_apart.p;
+  a.alse = h->stack_alse.p;
+  a.sync = h->stack_sync.p;
+  a.reqs = h->reqs.p;
+  a.n_reqs = static_cast<int>(reqs.size());
+  a.tok = token_maps(h);
+  a.rope_cos = h->rope_cos.p;
+  a.rope_sin = h->rope_sin.p;
+  a.max_pos = c.max_positions;
+  a.M = M;
+  a.H = c.hidden_size;
+  a.I = c.intermediate_size;
+  a.L = c.num_hidden_layers;
+  a.hq = c.num_attention_heads;
+  a.hkv = c.num_key_value_heads;
+  a.hd = c.head_dim;
+  a.eps = c.rms_norm_eps;
+  a.scale = 1.0f / std::sqrt(static_cast<float>(c.head_dim));
+  a.err = h->err.p;
+  a.trace = nullptr;
+  if (h->stack_trace_on) {
+    const size_t n = static_cast<size_t>(grid) * (kStackTraceHead + static_cast<size_t>(c.num_hidden_layers) * kStackTracePerLayer);
+    FDLLM_TRY(h->stack_trace.ensure(n));
+    CUDA_TRY(cudaMemsetAsync(h->stack_trace.p, 0, n * sizeof(unsigned long long), s));
+    a.trace = h->stack_trace.p;
+    h->stack_trace_grid = grid;
+  }
+  CUDA_TRY(cudaMemsetAsync(h->stack_sync.p, 0, n_sync * sizeof(unsigned), s));
+  CUDA_TRY(launch_stack(a, tm_h, tm_attn, tm_act, grid, s));
+  *used = FDLLM_OK;
   return FDLLM_OK;
 }
 
@@ -270,6 +405,12 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
   if (max_l_hint > 0) max_l = max_l_hint;
   int n_splits, split_len;
   plan_attention(h, max_q, max_l, nreq, bias != nullptr || causal_block != 0, &n_splits, &split_len);
+
+  if (bias == nullptr && causal_block == 0) {
+    int rc = FDLLM_ERR_UNSUPPORTED;
+    FDLLM_TRY(stack_forward(h, x, M, reqs, max_q, max_l, out, s, &rc));
+    if (rc == FDLLM_OK) return FDLLM_OK;  // else: not eligible, run the per-kernel layer loop
+  }
 
   Epilogue base{};
   base.hq = c.num_attention_heads;
@@ -461,7 +602,12 @@ int fdllm_destroy(fdllm_handle* h) {
   for (auto* b : {&h->err, &h->tok_req, &h->tok_pos, &h->tok_row, &h->tmp_ids, &h->targets, &h->dec.ids,
                   &h->dec.block, &h->dec.cids, &h->dec.out})
     b->release();
-  for (auto* b : {&h->conf_part, &h->tmp_maxp, &h->ss, &h->dec.cmax}) b->release();
+  for (auto* b : {&h->conf_part, &h->tmp_maxp, &h->ss, &h->dec.cmax, &h->stack_gpart, &h->stack_apart, &h->stack_alse})
+    b->release();
+  h->stack_maps.release();
+  h->stack_layers.release();
+  h->stack_sync.release();
+  h->stack_trace.release();
   h->reqs.release();
   if (h->dec.host) cudaFreeHost(h->dec.host);
   if (h->dec.host_params) cudaFreeHost(h->dec.host_params);
@@ -509,6 +655,21 @@ int fdllm_bind_params(fdllm_handle* h, const void* const* ptrs, int n) {
       FDLLM_TRY(make_map(&L.down.map, L.down.ptr, L.down.rows, L.down.cols, 128));
     }
     FDLLM_TRY(make_map(&h->lm.map, h->lm.ptr, h->lm.rows, h->lm.cols, 128));
+    // the layer-stack kernel reads every layer's weight maps and small pointers from device memory
+    std::vector<CUtensorMap> maps(static_cast<size_t>(c.num_hidden_layers) * 4);
+    std::vector<StackLayer> sl(c.num_hidden_layers);
+    for (int l = 0; l < c.num_hidden_layers; ++l) {
+      const LayerW& L = h->layers[l];
+      maps[l * 4 + 0] = L.qkv.map;
+      maps[l * 4 + 1] = L.o.map;
+      maps[l * 4 + 2] = L.gu.map;
+      maps[l * 4 + 3] = L.down.map;
+      sl[l] = StackLayer{L.qkv_b, L.ln1, L.ln2};
+    }
+    FDLLM_TRY(h->stack_maps.ensure(maps.size() * sizeof(CUtensorMap)));
+    FDLLM_TRY(h->stack_layers.ensure(sl.size() * sizeof(StackLayer)));
+    CUDA_TRY(cudaMemcpy(h->stack_maps.p, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(h->stack_layers.p, sl.data(), sl.size() * sizeof(StackLayer), cudaMemcpyHostToDevice));
   }
   h->bound = true;
   return FDLLM_OK;
@@ -719,6 +880,28 @@ int fdllm_profile_read(fdllm_handle* h, double* out4) {
   h->prof_used = 0;
   h->prof_bytes = h->prof_flops = h->prof_ms_extra = 0.0;
   h->prof_launch_extra = 0;
+  return FDLLM_OK;
+}
+
+int fdllm_stack_trace_enable(fdllm_handle* h, int enable) {
+  if (h == nullptr) return fail(FDLLM_ERR_INVALID, "null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  h->stack_trace_on = enable != 0;
+  return FDLLM_OK;
+}
+
+int fdllm_stack_trace_read(fdllm_handle* h, uint64_t* out, long long cap, int32_t* n_cta, int32_t* per_cta) {
+  if (h == nullptr || n_cta == nullptr || per_cta == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
+  std::lock_guard<std::mutex> lock(h->mu);
+  const int per = kStackTraceHead + h->cfg.num_hidden_layers * kStackTracePerLayer;
+  *n_cta = h->stack_trace_grid;
+  *per_cta = per;
+  const long long n = static_cast<long long>(h->stack_trace_grid) * per;
+  if (out == nullptr || n == 0) return FDLLM_OK;
+  if (cap < n) return fail(FDLLM_ERR_INVALID, "trace buffer too small");
+  CUDA_TRY(cudaSetDevice(h->device));
+  CUDA_TRY(cudaDeviceSynchronize());
+  CUDA_TRY(cudaMemcpy(out, h->stack_trace.p, static_cast<size_t>(n) * sizeof(uint64_t), cudaMemcpyDeviceToHost));
   return FDLLM_OK;
 }
 

@@ -168,6 +168,19 @@ FDLLM_API int fdllm_profile_read(fdllm_handle* h, double* out4);
 /* Bytes of device workspace the handle currently holds. */
 FDLLM_API long long fdllm_workspace_bytes(fdllm_handle* h);
 
+/* Diagnostics of the persistent layer-stack kernel (no counterpart in the reference; the
+ * reference profiles per compiled function, docs/notebooks/07_profiling.ipynb).  While enabled,
+ * every layer-stack launch issued afterwards records %globaltimer stamps (ns) per CTA;
+ * fdllm_stack_trace_read copies the last record (synchronises): out[cta * per_cta + slot] with
+ * slots 0 start, 1 layer-0 statistics done, 2 first grid barrier passed, 3 end, and per layer l
+ * at 4 + 32*l: qkv 0-4 (start, B landed, B ready, accumulator ready, epilogue done), 5 barrier;
+ * attention 6 start, 7 done, 8 barrier; o 9-13, 14 barrier; gate_up 15-19, 20 barrier;
+ * down 21-25, 26 barrier.  0 = not reached (a CTA without a unit in that phase).  With
+ * out == NULL only *n_cta and *per_cta are written.  A CUDA graph captured while disabled keeps
+ * recording nothing. */
+FDLLM_API int fdllm_stack_trace_enable(fdllm_handle* h, int enable);
+FDLLM_API int fdllm_stack_trace_read(fdllm_handle* h, uint64_t* out, long long cap, int32_t* n_cta, int32_t* per_cta);
+
 /* fdllm_confidence without any device allocation (no counterpart in the reference).  For callers
  * that may not allocate device memory inside their step: an external memory pool or a fixed
  * arena owns the device, or the step must never grow the handle's workspace.  The lm_head
