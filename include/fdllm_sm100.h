@@ -173,9 +173,11 @@ FDLLM_API long long fdllm_workspace_bytes(fdllm_handle* h);
  * every layer-stack launch issued afterwards records %globaltimer stamps (ns) per CTA;
  * fdllm_stack_trace_read copies the last record (synchronises): out[cta * per_cta + slot] with
  * slots 0 start, 1 layer-0 statistics done, 2 first grid barrier passed, 3 end, and per layer l
- * at 4 + 32*l: qkv 0-4 (start, B landed, B ready, accumulator ready, epilogue done), 5 barrier;
- * attention 6 start, 7 done, 8 barrier; o 9-13, 14 barrier; gate_up 15-19, 20 barrier;
- * down 21-25, 26 barrier.  0 = not reached (a CTA without a unit in that phase).  With
+ * at 4 + 40*l: qkv 0-4 (start, first B group landed, B released, accumulator ready, epilogue
+ * done), 5 barrier; attention 6 start, 7 done, 8 barrier; o 9-13, 14 barrier; gate_up 15-19,
+ * 20 barrier; down 21-25, 26 barrier; attention detail 27 first K/V tile, 28 partial written,
+ * 29 splits gathered; qkv split-K 30 partial published, 31 splits gathered.  0 = not reached
+ * (a CTA without a unit in that phase).  With
  * out == NULL only *n_cta and *per_cta are written.  A CUDA graph captured while disabled keeps
  * recording nothing. */
 FDLLM_API int fdllm_stack_trace_enable(fdllm_handle* h, int enable);
