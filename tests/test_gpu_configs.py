@@ -1,0 +1,134 @@
+"""Parity at the shapes of BASELINE configs[2..4] on the GPU (the 1.5B layer shapes; 2 layers and a
+4096-token vocabulary keep the CPU oracle fast):
+
+* a long prefix (here 1024 rows; 4096 through the size-independent cached == dense
+  invariant) and batch 8;
+* 32 requests in one batched forward (1024 token rows: the large-tile GEMM path);
+* masked-continuation scoring, 512-token contexts and 16-token continuations, batch 4,
+  with the device log-softmax gather (runners.py:877-881).
+"""
+
+import pytest
+import torch
+
+from fast_dllm_relax_b200.config import ModelConfig, make_synthetic_params
+from oracle.model import build_block_bias
+from tests._oracle_util import make_oracle
+
+pytestmark = pytest.mark.gpu
+
+MID = ModelConfig(vocab_size=4096, hidden_size=1536, intermediate_size=8960, num_hidden_layers=2,
+                  num_attention_heads=12, num_key_value_heads=2, head_dim=128, context_window_size=8192)
+TOL = dict(rtol=2e-2, atol=2e-2)
+MASK = 4095
+
+
+def _dev():
+    return torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module")
+def mid():
+    from fast_dllm_relax_b200.engine import Engine
+    params = make_synthetic_params(MID, seed=7, dtype="bfloat16", mask_id=MASK)
+    eng = Engine(MID, [p.to(_dev()) for p in params], dtype="bfloat16")
+    return eng, make_oracle(MID, params, "bfloat16")
+
+
+def _act(n, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn((1, n, MID.hidden_size), generator=g).to(torch.bfloat16)
+
+
+def _close(a, b, label=""):
+    torch.testing.assert_close(a.float().cpu(), b.float().cpu(), msg=lambda m: f"{label}: {m}", **TOL)
+
+
+def test_long_prefix_matches_oracle(mid):
+    eng, orc = mid
+    P = 1024
+    prefix, block = _act(P, 1), _act(32, 2)
+    k, v = eng.new_cache(P + 32)
+    eng.build_prefix_cache(prefix.to(_dev()), None, k, v)
+    kr, vr = torch.zeros(k.shape, dtype=k.dtype), torch.zeros(v.shape, dtype=v.dtype)
+    orc.build_prefix_cache(prefix, build_block_bias(0, P, 32), kr, vr)
+    _close(k[:, :, :P], kr[:, :, :P], "prefix k")
+    h = eng.forward_cached(block.to(_dev()), k, v, P, P)
+    _close(h, orc.forward_cached(block, kr, vr, P, P), "forward_cached at P=1024")
+    for rp in (8, 24):
+        x8 = _act(8, 10 + rp)
+        hp = eng.forward_block_partial(x8.to(_dev()), k, v, P + rp, P, rp)
+        _close(hp, orc.forward_block_partial(x8, kr, vr, P + rp, P, rp), f"rp{rp} at P=1024")
+
+
+def test_cached_equals_dense_at_4096(mid):
+    """configs[3]'s prefix length through the size-independent invariant (no oracle)."""
+    eng, _ = mid
+    P = 4096
+    seq = _act(P + 32, 3).to(_dev())
+    dense = eng.forward_hidden(seq, None)[:, P:]  # implicit block-causal mask
+    k, v = eng.new_cache(P + 32)
+    eng.build_prefix_cache(seq[:, :P].contiguous(), None, k, v)
+    cached = eng.forward_cached(seq[:, P:].contiguous(), k, v, P, P)
+    _close(cached, dense, "cached vs dense at P=4096")
+    assert eng.device_error() == 0
+
+
+@pytest.mark.parametrize("n_req,prefix", [(8, 1024), (32, 96)])
+def test_batched_requests_match_single(mid, n_req, prefix):
+    """configs[3] (batch 8, long prefixes) and configs[2] (32 requests = 1024 rows)."""
+    eng, orc = mid
+    reqs, xs, singles = [], [], []
+    g = torch.Generator().manual_seed(n_req)
+    for i in range(n_req):
+        P = prefix + 32 * int(torch.randint(0, 3, (1,), generator=g))
+        k, v = eng.new_cache(P + 32)
+        eng.build_prefix_cache(_act(P, 100 + i).to(_dev()), None, k, v)
+        x = _act(32, 200 + i).to(_dev())
+        ks, vs = k.clone(), v.clone()
+        singles.append((eng.forward_cached(x, ks, vs, P, P)[0], ks, vs))
+        xs.append(x[0])
+        reqs.append(dict(k=k, v=v, rows=32, prefix_len=P))
+    out = eng.forward_cached_batch(torch.cat(xs), reqs)
+    # 32- and 1024-row calls use different token tiles and split-K plans, so their fp32 sums run in
+    # a different order and an occasional bf16 rounding flips, then propagates through the next
+    # layer: nearly all elements agree within the bf16 tolerance, the rest within two ulps.
+    for i, (r, (hs, ks, vs)) in enumerate(zip(reqs, singles)):
+        a, b = out[32 * i:32 * (i + 1)].float().cpu(), hs.float().cpu()
+        torch.testing.assert_close(a, b, rtol=2e-2, atol=4e-2, msg=lambda m: f"request {i}: {m}")
+        assert ((a - b).abs() > 2e-2 + 2e-2 * b.abs()).float().mean() < 1e-3, f"request {i}"
+        _close(r["k"], ks, f"request {i} k")
+    assert eng.device_error() == 0
+
+
+def test_masked_continuation_scoring(mid):
+    """context 512, continuation 16 in a masked 32-row block (eos at row 16, pad
+    masks after), log-softmax gathered on the device, batch 4."""
+    eng, orc = mid
+    B, C, N = 4, 512, 16
+    g = torch.Generator().manual_seed(5)
+    reqs, xs, targets, refs = [], [], [], []
+    for i in range(B):
+        ctx = torch.randint(0, MASK, (C,), generator=g)
+        cont = torch.randint(0, MASK, (N,), generator=g)
+        block = torch.full((32,), MASK, dtype=torch.int64)
+        block[N] = 4094  # eos after the masked continuation, pad masks behind it
+        k, v = eng.new_cache(C + 32)
+        eng.build_prefix_cache(eng.embed(ctx.to(_dev()))[None], None, k, v)
+        xs.append(eng.embed(block.to(_dev())))
+        reqs.append(dict(k=k, v=v, rows=32, prefix_len=C))
+        t = torch.zeros(32, dtype=torch.int32)
+        t[:N] = cont.to(torch.int32)
+        targets.append(t)
+        # oracle: the same forward and log_softmax(logits)[target]
+        kr, vr = torch.zeros(k.shape, dtype=k.dtype), torch.zeros(v.shape, dtype=v.dtype)
+        orc.build_prefix_cache(orc.embed(ctx.to(torch.int32))[None], build_block_bias(0, C, 32), kr, vr)
+        hr = orc.forward_cached(orc.embed(block.to(torch.int32))[None], kr, vr, C, C)
+        lp = torch.log_softmax(orc.get_logits(hr)[0].float(), dim=-1)
+        refs.append(lp.gather(-1, t.long()[:, None])[:N, 0])
+    hidden = eng.forward_cached_batch(torch.cat(xs), reqs)
+    logprob = eng.token_logprob(hidden, torch.cat(targets).to(_dev())).cpu()
+    for i in range(B):
+        got = logprob[32 * i:32 * i + N]
+        torch.testing.assert_close(got, refs[i], rtol=2e-2, atol=5e-2, msg=f"sequence {i}")
+        assert abs(float(got.sum()) - float(refs[i].sum())) < 0.05 * N
