@@ -270,6 +270,75 @@ __global__ void __launch_bounds__(128, 1)
     cluster_sync();  // no member leaves while another may still read its tile
   }
   gemm_epilogue<bf16>(g, acc, NT, tok0, slab, row0, row1, s_epi);
+
+  // ---------------- post-norm: the next RMSNorm, by the last CTA of each token-row group ----------
+  // Every slab's cluster member of rank r owns the same rows [row0, row1) of this token tile, so
+  // the n_slabs CTAs of one (tile, rank) together complete those rows; the last to arrive
+  // normalises them (model/cuda.py:269-275) with the row statistics the residual epilogues left.
+  if (g.post_out != nullptr) {
+    __shared__ int s_last;
+    const int rank = g.splits > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+    __syncthreads();  // this CTA's residual and statistics stores are issued
+    if (threadIdx.x == 0) {
+      __threadfence();
+      unsigned* ctr = g.post_ctr + tile * 16 + rank;
+      const unsigned old = atomicAdd(ctr, 1u);
+      s_last = (old == static_cast<unsigned>(g.n_slabs) - 1u) ? 1 : 0;
+      if (s_last) {
+        __threadfence();
+        *ctr = 0u;  // the last arrival: nobody else touches this counter in this launch
+      }
+    }
+    __syncthreads();
+    if (s_last) {
+      const int H = g.N;
+      const int n_ss = g.epi.ss_ld;
+      const bf16* hsrc = static_cast<const bf16*>(g.epi.resid);
+      const bf16* w = static_cast<const bf16*>(g.post_w);
+      bf16* out = static_cast<bf16*>(g.post_out);
+      float* rs = reinterpret_cast<float*>(s_epi);  // rows of this group
+      for (int t = row0 + threadIdx.x; t < row1; t += blockDim.x) {
+        const int tok = tok0 + t;
+        float ss = 0.f;
+        if (tok < g.M)
+          for (int j = 0; j < n_ss; ++j) ss += __ldcg(g.epi.ss_out + static_cast<size_t>(tok) * n_ss + j);
+        rs[t - row0] = rsqrtf(ss / static_cast<float>(H) + g.norm_eps);
+      }
+      __syncthreads();
+      const int cpr = H / 8;
+      for (int c0 = threadIdx.x; c0 < (row1 - row0) * cpr; c0 += blockDim.x * 4) {
+        uint4 xv[4], wv[4];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {  // loads first
+          const int c = c0 + b * blockDim.x;
+          const int t = row0 + c / cpr, col = (c % cpr) * 8;
+          if (c < (row1 - row0) * cpr && tok0 + t < g.M) {
+            xv[b] = __ldcg(reinterpret_cast<const uint4*>(hsrc + static_cast<size_t>(tok0 + t) * H + col));
+            wv[b] = *reinterpret_cast<const uint4*>(w + col);
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int c = c0 + b * blockDim.x;
+          const int t = row0 + c / cpr, col = (c % cpr) * 8;
+          if (c >= (row1 - row0) * cpr || tok0 + t >= g.M) continue;
+          const float r = rs[t - row0];
+          const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv[b]);
+          const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv[b]);
+          uint4 o;
+          __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const float2 xf = __bfloat1622float2(x2[v]);
+            const float2 wf = __bfloat1622float2(w2[v]);
+            const float2 xn = round2_bf16(xf.x * r, xf.y * r);
+            o2[v] = __floats2bfloat162_rn(wf.x * xn.x, wf.y * xn.y);
+          }
+          *reinterpret_cast<uint4*>(out + static_cast<size_t>(tok0 + t) * H + col) = o;
+        }
+      }
+    }
+  }
 }
 
 template <int NT>

@@ -137,6 +137,7 @@ struct fdllm_handle {
   DevBuf<int> tok_req, tok_pos, tok_row, tmp_ids, targets;
   DevBuf<ReqDesc> reqs;
   DevBuf<float> conf_part, tmp_maxp, ss;  // ss: per-slab row sums of squares
+  DevBuf<unsigned> post_ctr;                // post-norm arrival counters (zero between launches)
   // persistent layer-stack kernel: weight maps and per-layer pointers (built at bind), partials,
   // barrier / arrival counters (zeroed before every launch)
   DevBuf<uint8_t> stack_maps, stack_layers;

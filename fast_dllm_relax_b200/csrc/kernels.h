@@ -91,6 +91,13 @@ struct GemmArgs {
   const float* norm_ss;     // [M, norm_ss_ld] per-128-feature sums of squares of norm_x rows
   int norm_ss_ld;
   float norm_eps;
+  // Post-norm (residual epilogue with ss_out, N = hidden): once every slab has written its part of a
+  // token row, the last CTA to finish those rows writes post_out = rmsnorm(row) * post_w, the next
+  // projection's normalised input.  post_ctr: [token tiles][16] arrival counters, zero between
+  // launches (the last arrival resets its counter).
+  const void* post_w;
+  void* post_out;
+  unsigned* post_ctr;
   int* err;
   Epilogue epi;
 };

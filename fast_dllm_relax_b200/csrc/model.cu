@@ -177,12 +177,18 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
 // norm_w set (tcgen05 path only): X is the un-normalized input and the kernel applies RMSNorm
 // with weight norm_w while building its B operand.
 static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epilogue epi, cudaStream_t s,
-                    const void* norm_w = nullptr) {
+                    const void* norm_w = nullptr, const void* post_w = nullptr, void* post_out = nullptr) {
   if (M <= 0) return FDLLM_OK;
   GemmArgs g{};
   const int nt = plan_gemm(h, w, M, &g);
   g.err = h->err.p;
   g.epi = epi;
+  if (post_out != nullptr) {  // residual epilogue (with row statistics) followed by the next RMSNorm
+    g.post_w = post_w;
+    g.post_out = post_out;
+    g.post_ctr = h->post_ctr.p;
+    g.norm_eps = h->cfg.rms_norm_eps;
+  }
   if (norm_w != nullptr) {
     g.norm_x = X;
     g.norm_w = norm_w;
@@ -206,7 +212,9 @@ static void plan_attention(const fdllm_handle* h, int max_q, int max_l, int nreq
   *n_splits = 1;
   *split_len = std::max(64, static_cast<int>(round_up(std::max(max_l, 1), 64)));
   if (h->dtype == FDLLM_BFLOAT16 && !dense && base_ctas < h->num_sms) {
-    const int want = std::min({(2 * h->num_sms + base_ctas - 1) / base_ctas, (max_l + 63) / 64, kMaxAttnSplits});
+    int want = std::min({(2 * h->num_sms + base_ctas - 1) / base_ctas, (max_l + 63) / 64, kMaxAttnSplits});
+    const char* ev = std::getenv("FDLLM_ATTN_SPLITS");  // tuning override
+    if (ev != nullptr && std::atoi(ev) > 0) want = std::min(std::atoi(ev), kMaxAttnSplits);
     if (want > 1) {
       *n_splits = want;
       *split_len = 64;  // the kernel divides each request's own key range evenly
@@ -219,6 +227,7 @@ static int ensure_ws(fdllm_handle* h, int M, int nreq) {
   const fdllm_config& c = h->cfg;
   const size_t m = round_up(static_cast<size_t>(std::max(M, 1)), 64);
   const size_t qd = static_cast<size_t>(c.num_attention_heads) * c.head_dim;
+  FDLLM_TRY(h->post_ctr.ensure(4 * 16, true));  // zeroed once; every launch leaves it zero
   FDLLM_TRY(h->h.ensure(m * c.hidden_size * h->esz));
   FDLLM_TRY(h->xn.ensure(m * std::max<size_t>(c.hidden_size, c.intermediate_size) * h->esz));
   FDLLM_TRY(h->q.ensure(m * qd * h->esz));
@@ -426,6 +435,19 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
   // their B tiles in place, with row statistics left by the previous down projection); large calls
   // normalize once in a separate kernel.
   const bool fuse_norm = h->dtype == FDLLM_BFLOAT16 && M <= 64 && c.hidden_size <= 2560;
+  // The post-attention RMSNorm folds into gate_up for 8/16-row calls (partial steps); at 32 rows its
+  // per-stage normalisation outlasts the weight tile it waits for, so a separate kernel runs it.
+  // FDLLM_FUSE_GU_NORM=0/1 overrides.
+  // post-attention RMSNorm: "post" = the o projection's last CTAs normalise each finished row
+  // group (no separate kernel, gate_up reads the result); "fused" = gate_up normalises its B tiles
+  // (fastest for <= 16 rows, where a stage's normalisation is short); "kernel" = a separate rmsnorm
+  // kernel.  FDLLM_GU_NORM overrides the choice.
+  const char* gn = std::getenv("FDLLM_GU_NORM");
+  const std::string gu_norm =
+      gn != nullptr ? std::string(gn) : std::string(!fuse_norm ? "kernel" : (M <= 16 ? "fused" : "post"));
+  const bool fuse_norm_gu = fuse_norm && gu_norm == "fused";
+  const bool post_norm_gu = fuse_norm && gu_norm == "post" && M <= 64;
+
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const LayerW& L = h->layers[l];
     const void* layer_in = l == 0 ? x : h->h.p;
@@ -466,16 +488,28 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     e.kind = kEpiResidual;
     e.resid = h->h.p;
     e.ld_resid = c.hidden_size;
-    FDLLM_TRY(run_gemm(h, L.o, h->attn.p, M, e, s));
+    if (fuse_norm_gu || post_norm_gu) {  // leave the statistics of the post-attention RMSNorm
+      e.ss_out = h->ss.p;
+      e.ss_ld = c.hidden_size / 128;
+    }
+    if (post_norm_gu) {
+      FDLLM_TRY(run_gemm(h, L.o, h->attn.p, M, e, s, nullptr, L.ln2, h->xn.p));
+    } else {
+      FDLLM_TRY(run_gemm(h, L.o, h->attn.p, M, e, s));
+    }
 
     e = base;
     e.kind = kEpiSiluMul;
     e.out = h->act.p;
     e.ld_out = c.intermediate_size;
-    // gate_up streams 24 k-blocks per CTA; normalizing its B tiles in place would sit on every
-    // stage's critical path, so its RMSNorm stays a separate (small) kernel.
-    CUDA_TRY(launch_rmsnorm(h->h.p, L.ln2, h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s));
-    FDLLM_TRY(run_gemm(h, L.gu, h->xn.p, M, e, s));
+    if (post_norm_gu) {
+      FDLLM_TRY(run_gemm(h, L.gu, h->xn.p, M, e, s));
+    } else if (fuse_norm_gu) {
+      FDLLM_TRY(run_gemm(h, L.gu, h->h.p, M, e, s, L.ln2));
+    } else {
+      CUDA_TRY(launch_rmsnorm(h->h.p, L.ln2, h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s));
+      FDLLM_TRY(run_gemm(h, L.gu, h->xn.p, M, e, s));
+    }
 
     e = base;
     e.kind = kEpiResidual;
@@ -607,6 +641,7 @@ int fdllm_destroy(fdllm_handle* h) {
   h->stack_maps.release();
   h->stack_layers.release();
   h->stack_sync.release();
+  h->post_ctr.release();
   h->stack_trace.release();
   h->reqs.release();
   if (h->dec.host) cudaFreeHost(h->dec.host);
