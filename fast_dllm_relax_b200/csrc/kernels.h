@@ -163,6 +163,7 @@ struct StackArgs {
   int* err;
   // optional per-CTA timeline (globaltimer ns): [cta][kStackTraceHead + l * kStackTracePerLayer + event]
   unsigned long long* trace;
+  int b_lsu;  // stage the B operand with cp.async by the compute warps instead of TMA
 };
 constexpr int kStackTraceHead = 4;
 constexpr int kStackTracePerLayer = 40;

@@ -380,6 +380,8 @@ int fdllm::stack_forward(fdllm_handle* h, const void* x, int M, const std::vecto
   a.scale = 1.0f / std::sqrt(static_cast<float>(c.head_dim));
   a.err = h->err.p;
   a.trace = nullptr;
+  const char* bl = std::getenv("FDLLM_STACK_BLSU");
+  a.b_lsu = (bl != nullptr && bl[0] == '1') ? 1 : 0;
   if (h->stack_trace_on) {
     const size_t n = static_cast<size_t>(grid) * (kStackTraceHead + static_cast<size_t>(c.num_hidden_layers) * kStackTracePerLayer);
     FDLLM_TRY(h->stack_trace.ensure(n));

@@ -719,7 +719,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       // released to the MMA issuer as soon as it is ready, so the MMAs start on the first group.
       // Always kBGroups groups (an empty group completes with 0 bytes), so every group barrier
       // completes exactly once per unit; CTAs visit the groups in rotated order.
-      if (tid == 0) {
+      if (a.b_lsu) {
+        // the same tiles through the load/store path (16-byte cp.async.cg), one commit group per
+        // B group; rows >= M are zero-filled
+        const bf16* src = static_cast<const bf16*>(p == 1 ? a.attn : (p == 3 ? a.act : a.h));
+        const int ld = p == 1 ? a.hq * a.hd : (p == 3 ? a.I : a.H);
+        for (int gi = 0; gi < kBGroups; ++gi) {
+          const int g = (gi + cta) % kBGroups;
+          const int c0 = g * nk / kBGroups, c1 = (g + 1) * nk / kBGroups;
+          for (int idx = tid; idx < (c1 - c0) * kStackRows * 8; idx += kCompute) {
+            const int c = c0 + idx / (kStackRows * 8), t = (idx >> 3) % kStackRows, cc = idx & 7;
+            const bool valid = t < a.M;
+            const bf16* sp = src + static_cast<size_t>(valid ? t : 0) * ld + (u.kb0 + c) * 64 + cc * 8;
+            cp_async_16(breg + c * kBChunk + sw128_off(t, cc), sp, valid);
+          }
+          cp_async_commit();
+        }
+      } else if (tid == 0) {
         fence_proxy_async_global();
         for (int gi = 0; gi < kBGroups; ++gi) {
           const int g = (gi + cta) % kBGroups;
@@ -737,7 +753,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int gi = 0; gi < kBGroups; ++gi) {
         const int g = (gi + cta) % kBGroups;
-        if (!wait_bar(a, &b_tma[g], btcnt & 1u)) {
+        if (a.b_lsu) {
+          switch (kBGroups - 1 - gi) {  // this thread's copies of groups 0..gi have landed
+            case 3: cp_async_wait<3>(); break;
+            case 2: cp_async_wait<2>(); break;
+            case 1: cp_async_wait<1>(); break;
+            default: cp_async_wait<0>(); break;
+          }
+          fence_proxy_async_smem();
+          named_sync(kComputeBar, kCompute);  // everyone's copies of the group have landed
+        } else if (!wait_bar(a, &b_tma[g], btcnt & 1u)) {
           if (tid == 0 && !aborted(a.sync)) raise_abort(a, kErrTimeoutEpilogue);
           return false;
         }
