@@ -32,9 +32,12 @@ struct TcCfg {
   static constexpr int kStage = kA + kB;
   // Ring depth: for NT <= 128 the CTA stays under ~110 KB of shared memory, so a CTA of the next
   // projection (launched early, prefetching its weights) can sit beside a draining one on each SM.
-  static constexpr int kStages = NT <= 32 ? 5 : (NT <= 64 ? 4 : (NT <= 128 ? 3 : 4));
+  // NT = 256 keeps 2 stages so that two CTAs share an SM: one's epilogue overlaps the other's
+  // mainloop (their TMEM accumulators, 256 columns each, fill the SM's 512).
+  static constexpr int kStages = NT <= 32 ? 5 : (NT <= 64 ? 4 : (NT <= 128 ? 3 : 2));
   static constexpr int kTmemCols = NT < 32 ? 32 : NT;
-  static constexpr int kAcc = NT * 128 * 4;  // fp32 epilogue tile (reuses the ring)
+  static constexpr int kChunk = NT < 64 ? NT : 64;  // token columns drained and finished at a time
+  static constexpr int kAcc = kChunk * 128 * 4;     // fp32 epilogue chunk (reuses the ring)
   static constexpr int kPipe = kStages * kStage;
   static constexpr int kRegion = kPipe > kAcc ? kPipe : kAcc;
   static constexpr int kBarBytes = 512;  // barriers, TMEM slot, fused-norm row scales (NT <= 64)
@@ -215,61 +218,82 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_after_sync();
   __syncthreads();  // the producer's drain is complete before the ring is overwritten
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-#pragma unroll
-  for (int c0 = 0; c0 < NT; c0 += 32) {
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(tmem + lane_base + static_cast<uint32_t>(c0), r);
-    tmem_ld_wait();
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (c0 + j < NT) acc[(c0 + j) * 128 + warp * 32 + lane] = __uint_as_float(r[j]);
-  }
-  if (nk == 0) {  // empty K range: the accumulator was never written
-    for (int idx = threadIdx.x; idx < NT * 128; idx += blockDim.x) acc[idx] = 0.f;
-  }
-  tc_fence_before_sync();
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after_sync();
-    tmem_dealloc(tmem, C::kTmemCols);
-  }
-
-  // ---------------- split-K: reduction across the thread-block cluster ----------------
-  // The g.splits CTAs of one (slab, token tile) form one cluster.  Each keeps its fp32 partial tile
-  // in shared memory; member r then sums token rows [r*NT/S, (r+1)*NT/S) over all members' tiles,
-  // read through distributed shared memory in rank (= split) order -- deterministic, no global
-  // round trip -- and runs the epilogue for those rows only.
-  int row0 = 0, row1 = NT;
-  if (g.splits > 1) {
-    constexpr int kMaxS = 16;
-    const uint32_t S = static_cast<uint32_t>(g.splits);
-    const uint32_t rank = cluster_ctarank();
-    row0 = static_cast<int>(rank * NT / S);
-    row1 = static_cast<int>((rank + 1) * NT / S);
-    cluster_sync();  // every member's partial tile is complete
-    const uint32_t acc_addr = smem_addr(acc);
-    float4* acc4 = reinterpret_cast<float4*>(acc);
-    for (int c = row0 * 32 + threadIdx.x; c < row1 * 32; c += blockDim.x) {
-      float4 v[kMaxS];
-#pragma unroll
-      for (int m = 0; m < kMaxS; ++m)
-        v[m] = (static_cast<uint32_t>(m) < S) ? ld_dsmem_f4(map_shared_rank(acc_addr + c * 16, m))
-                                              : make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int m = 0; m < kMaxS; ++m) {
-        if (static_cast<uint32_t>(m) < S) {
-          sum.x += v[m].x;
-          sum.y += v[m].y;
-          sum.z += v[m].z;
-          sum.w += v[m].w;
-        }
+  // The accumulator is finished kChunk token columns at a time (the shared fp32 chunk reuses the
+  // ring).  Split-K: the g.splits CTAs of one (slab, token tile) form one cluster; each keeps its
+  // fp32 partial chunk in shared memory, member r sums rows [r*kChunk/S, (r+1)*kChunk/S) of the
+  // chunk over all members through distributed shared memory in rank (= split) order --
+  // deterministic, no global round trip -- and runs the epilogue for those rows only.
+  const uint32_t S = static_cast<uint32_t>(g.splits > 1 ? g.splits : 1);
+  const uint32_t rank = g.splits > 1 ? cluster_ctarank() : 0u;
+  const int lr0 = static_cast<int>(rank * C::kChunk / S), lr1 = static_cast<int>((rank + 1) * C::kChunk / S);
+  int row0 = lr0, row1 = lr1;  // rows of the last chunk this CTA finished (the only chunk when NT <= 64)
+  for (int ch = 0; ch < NT / C::kChunk; ++ch) {
+    const int cb = ch * C::kChunk;
+    if (ch > 0) {  // the previous chunk is consumed (its epilogue, and the peers' reads of it)
+      if (S > 1) {
+        cluster_sync();
+      } else {
+        __syncthreads();
       }
-      acc4[c] = sum;  // only this member reads or writes these rows from here on
     }
-    cluster_sync();  // no member leaves while another may still read its tile
+#pragma unroll
+    for (int c0 = 0; c0 < C::kChunk; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tmem + lane_base + static_cast<uint32_t>(cb + c0), r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (c0 + j < C::kChunk) acc[(c0 + j) * 128 + warp * 32 + lane] = __uint_as_float(r[j]);
+    }
+    if (nk == 0) {  // empty K range: the accumulator was never written
+      for (int idx = threadIdx.x; idx < C::kChunk * 128; idx += blockDim.x) acc[idx] = 0.f;
+    }
+    if (ch == NT / C::kChunk - 1) {  // every column drained: free TMEM
+      tc_fence_before_sync();
+      __syncthreads();
+      if (warp == 0) {
+        tc_fence_after_sync();
+        tmem_dealloc(tmem, C::kTmemCols);
+      }
+    } else {
+      __syncthreads();
+    }
+    if (S > 1) {
+      constexpr int kMaxS = 16;
+      cluster_sync();  // every member's partial chunk is complete
+      const uint32_t acc_addr = smem_addr(acc);
+      float4* acc4 = reinterpret_cast<float4*>(acc);
+      for (int c = lr0 * 32 + threadIdx.x; c < lr1 * 32; c += blockDim.x) {
+        float4 v[kMaxS];
+#pragma unroll
+        for (int m = 0; m < kMaxS; ++m)
+          v[m] = (static_cast<uint32_t>(m) < S) ? ld_dsmem_f4(map_shared_rank(acc_addr + c * 16, m))
+                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int m = 0; m < kMaxS; ++m) {
+          if (static_cast<uint32_t>(m) < S) {
+            sum.x += v[m].x;
+            sum.y += v[m].y;
+            sum.z += v[m].z;
+            sum.w += v[m].w;
+          }
+        }
+        acc4[c] = sum;  // only this member reads or writes its own rows from here on
+      }
+      __syncthreads();
+    }
+    row0 = cb + lr0;
+    row1 = cb + lr1;
+    // acc holds token columns [cb, cb + kChunk); the epilogue indexes it as the whole tile
+    gemm_epilogue<bf16>(g, acc - static_cast<size_t>(cb) * 128, NT, tok0, slab, S > 1 ? row0 : cb,
+                        S > 1 ? row1 : cb + C::kChunk, s_epi);
   }
-  gemm_epilogue<bf16>(g, acc, NT, tok0, slab, row0, row1, s_epi);
+  if (S > 1) cluster_sync();  // no member leaves while another may still read its shared memory
+  if (S == 1) {
+    row0 = 0;
+    row1 = NT;
+  }
 
   // ---------------- post-norm: the next RMSNorm, by the last CTA of each token-row group ----------
   // Every slab's cluster member of rank r owns the same rows [row0, row1) of this token tile, so
