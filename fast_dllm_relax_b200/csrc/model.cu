@@ -72,10 +72,15 @@ size_t fdllm::round_up(size_t x, size_t m) { return (x + m - 1) / m * m; }
 
 // ---- GEMM dispatch -------------------------------------------------------------------------
 static int pick_nt(int M) {
+  static const int nt_max = [] {  // tuning override of the largest token tile
+    const char* v = std::getenv("FDLLM_NT_MAX");
+    const int x = v ? std::atoi(v) : 256;
+    return (x == 64 || x == 128 || x == 256) ? x : 256;
+  }();
   if (M <= 16) return 16;
   if (M <= 32) return 32;
-  if (M <= 64) return 64;
-  if (M <= 128) return 128;
+  if (M <= 64 || nt_max == 64) return 64;
+  if (M <= 128 || nt_max == 128) return 128;
   return 256;
 }
 
@@ -164,8 +169,13 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
   const int kblocks = g->K / 64;
   const int tiles = g->n_slabs * g->n_tok_tiles;
   int splits = 1;
-  if (tiles < h->num_sms) {  // split K over a cluster of at most 16 CTAs
-    splits = std::max(1, std::min({kblocks, h->num_sms / tiles, 16}));
+  static const int target = [] {  // tuning override: CTAs per SM the split-K plan aims for
+    const char* v = std::getenv("FDLLM_SPLIT_TARGET");
+    const int x = v ? std::atoi(v) : 1;
+    return x >= 1 && x <= 4 ? x : 1;
+  }();
+  if (tiles < target * h->num_sms) {  // split K over a cluster of at most 16 CTAs
+    splits = std::max(1, std::min({kblocks, target * h->num_sms / tiles, 16}));
     const int kpb = (kblocks + splits - 1) / splits;
     splits = (kblocks + kpb - 1) / kpb;
   }
@@ -449,6 +459,11 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
       gn != nullptr ? std::string(gn) : std::string(!fuse_norm ? "kernel" : (M <= 16 ? "fused" : "post"));
   const bool fuse_norm_gu = fuse_norm && gu_norm == "fused";
   const bool post_norm_gu = fuse_norm && gu_norm == "post" && M <= 64;
+  // The next layer's input RMSNorm (and the final norm): "fused" = the qkv projection normalises
+  // its B tiles with the statistics the down projection left; "post" = the down projection's last
+  // CTAs write the normalised rows (FDLLM_QKV_NORM overrides).
+  const char* qn = std::getenv("FDLLM_QKV_NORM");
+  const bool post_norm_qkv = fuse_norm && M <= 64 && qn != nullptr && std::string(qn) == "post";
 
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const LayerW& L = h->layers[l];
@@ -458,7 +473,9 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     e.layer = l;
     e.bias = L.qkv_b;
     e.qout = h->q.p;
-    if (fuse_norm && l > 0) {  // layer 0's input has no producer epilogue: normalized separately
+    if (post_norm_qkv && l > 0) {  // the previous down projection wrote the normalised input
+      FDLLM_TRY(run_gemm(h, L.qkv, h->xn.p, M, e, s));
+    } else if (fuse_norm && l > 0) {  // layer 0's input has no producer epilogue: normalized separately
       FDLLM_TRY(run_gemm(h, L.qkv, layer_in, M, e, s, L.ln1));
     } else {
       // layer 0 reads the input embeddings and starts the residual stream h as their copy
@@ -521,8 +538,15 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
       e.ss_out = h->ss.p;
       e.ss_ld = c.hidden_size / 128;
     }
-    FDLLM_TRY(run_gemm(h, L.down, h->act.p, M, e, s));
+    if (post_norm_qkv) {
+      const bool last = l + 1 == c.num_hidden_layers;
+      FDLLM_TRY(run_gemm(h, L.down, h->act.p, M, e, s, nullptr, last ? h->final_norm : h->layers[l + 1].ln1,
+                         last ? (out ? out : h->xn.p) : h->xn.p));
+    } else {
+      FDLLM_TRY(run_gemm(h, L.down, h->act.p, M, e, s));
+    }
   }
+  if (post_norm_qkv) return FDLLM_OK;  // the last down projection wrote the final norm
   // out == null (build_prefix_cache): the final hidden states are not needed; xn is free by now.
   CUDA_TRY(launch_rmsnorm(h->h.p, h->final_norm, out ? out : h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s));
   return FDLLM_OK;
