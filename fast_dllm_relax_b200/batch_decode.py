@@ -1,0 +1,253 @@
+"""Batched block-diffusion decoding: many requests served together on one GPU.
+
+Each request follows the greedy decode loop of the reference's runtime
+(fast_dllm_relax/runtime.py:591-880, `relax_greedy_generate`) exactly: the block-aligned
+prompt fast path (:679-708), the prefix-cache rebuild rule (:718-739), the sub-block refinement
+loop with the full / partial step choice (:748-805), the stateless first block of short prompts
+(:806-837, 862-873), the length and stop checks (:655-669, 839-849) and block-append
+(:851-878).  The loop of each request is written as a generator that yields the model work it
+needs next; the scheduler gathers the pending work of all requests and runs it together:
+
+* every cached step of every request that needs one (full 32-row refinements, 8-row partial
+  refinements, block appends, in any mix) is ONE batched forward (fdllm_forward_cached_batch)
+  plus ONE fused lm_head + confidence launch over all rows;
+* prefix-cache builds run per request (the implicit block-causal mask, no O(P^2) bias);
+* the unmask decision (runtime.py:158-181 shift, 794-805 rule) runs on the host from the
+  per-row (argmax, max-probability) pairs, 8 bytes per row read back per step.
+
+Requests are independent: batching changes which kernels run together, not what any request
+computes, up to the bf16 rounding of the larger token tiles.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+from typing import Generator, Sequence
+
+import numpy as np
+import torch
+
+from .engine import Engine
+
+
+@dataclasses.dataclass
+class _Cache:
+    k: torch.Tensor
+    v: torch.Tensor
+    prefix_len: int = 0
+
+    @property
+    def capacity(self) -> int:
+        return int(self.k.shape[2])
+
+
+# Work items a request program yields (and what it receives back):
+#   ("prefill", cache, ids)                      -> None; rows [0, len(ids)) of `cache` written
+#   ("step", cache, ids, write_rel, attend_rel)  -> (ids int64[rows], maxp float32[rows]), unshifted
+#   ("dense", seq_ids)                           -> float32 logits [len(seq_ids), vocab] (stateless path)
+
+def _shift(ids: np.ndarray, maxp: np.ndarray):
+    """runtime.py:169-174: row i takes row i-1's prediction, row 0 its own."""
+    return np.concatenate([ids[:1], ids[:-1]]), np.concatenate([maxp[:1], maxp[:-1]])
+
+
+def _unmask_rows(masked: list[int], prob: np.ndarray, threshold: float) -> list[int]:
+    """runtime.py:796-805: masked rows above the threshold, else the first most confident one."""
+    rows = [r for r in masked if float(prob[r]) > threshold]
+    if not rows:
+        rows = [masked[int(np.argmax([float(prob[r]) for r in masked]))]]
+    return rows
+
+
+def request_program(engine: Engine, prompt_ids: Sequence[int], *, max_new_tokens: int, block_size: int,
+                    small_block_size: int, threshold: float, use_block_cache: bool, mask_id: int,
+                    stop_token: int | None, stats: dict) -> Generator:
+    """One request's decode loop (runtime.py:591-880, greedy); returns its continuation."""
+    if max_new_tokens < 0:
+        raise ValueError("max_new_tokens must be non-negative.")
+    bs = block_size
+    gen = [int(t) for t in prompt_ids]
+    n0 = len(gen)
+    cap = -(-(n0 + max_new_tokens) // bs) * bs + bs
+    cache: _Cache | None = None
+    kv_valid = False
+
+    def new_cache() -> _Cache:
+        k, v = engine.new_cache(cap)
+        return _Cache(k, v, 0)
+
+    def done_stop(seq, plen):
+        if stop_token is None:
+            return False
+        suf = seq[plen:]
+        if stop_token not in suf:
+            return False
+        return mask_id not in suf[:suf.index(stop_token)]
+
+    def continuation(toks):
+        raw = toks[n0:n0 + max_new_tokens]
+        fm = next((i for i, t in enumerate(raw) if t == mask_id), len(raw))
+        return raw[:fm]
+
+    if n0 % bs == 0 and n0 > 0 and max_new_tokens > 0:  # block-aligned prompt: commit its last block
+        lb = n0 - bs
+        cache = new_cache()
+        if lb > 0:
+            yield ("prefill", cache, gen[:lb])
+            cache.prefix_len = lb
+        ids, _ = yield ("step", cache, gen[lb:], 0, bs)
+        cache.prefix_len += bs
+        stats["block_recomputes"] += 1
+        stats["block_appends"] += 1
+        nxt = int(ids[-1])
+        gen.append(nxt)
+        if stop_token is not None and nxt == int(stop_token):
+            return continuation(gen)
+
+    while len(gen) - n0 < max_new_tokens:
+        plen = len(gen)
+        x = gen + [mask_id] * (bs - plen % bs)
+        a0 = len(x) - bs
+        use_cache = a0 != 0
+        if use_cache and (cache is None or cache.prefix_len != a0):  # (re)build the prefix cache
+            cache = new_cache()
+            yield ("prefill", cache, x[:a0])
+            cache.prefix_len = a0
+            kv_valid = False
+        for s0 in range(0, bs, small_block_size):
+            s1 = min(bs, s0 + small_block_size)
+            while True:
+                masked = [i for i, t in enumerate(x[a0 + s0:a0 + s1]) if t == mask_id]
+                if not masked:
+                    break
+                if done_stop(x, plen):
+                    return continuation(x)
+                if use_cache:
+                    partial = use_block_cache and kv_valid and x[a0 + s0] != mask_id
+                    if partial:
+                        ids, maxp = yield ("step", cache, x[a0 + s0:a0 + s1], s0, bs)
+                        tok, prob = _shift(ids, maxp)
+                    else:
+                        ids, maxp = yield ("step", cache, x[a0:], 0, bs)
+                        tok, prob = _shift(ids, maxp)
+                        tok, prob = tok[s0:s1], prob[s0:s1]
+                        kv_valid = use_block_cache
+                    stats["block_recomputes"] += 1
+                    stats["partial_recomputes"] += int(partial)
+                    rows = _unmask_rows(masked, prob, threshold)
+                    for r in rows:
+                        x[a0 + s0 + r] = int(tok[r])
+                    stats["unmask_updates"] += len(rows)
+                else:  # stateless first block (runtime.py:806-837): dense forward over the sequence
+                    logits = yield ("dense", x)
+                    stats["block_recomputes"] += 1
+                    act = logits[-bs:]
+                    sh = np.concatenate([act[:1], act[:-1]], axis=0)  # model/cuda.py:180-204
+                    small = sh[s0:s1].astype(np.float64)
+                    chosen = small.argmax(axis=-1)
+                    e = np.exp(small - small.max(axis=-1, keepdims=True))
+                    probs = e[np.arange(len(chosen)), chosen] / e.sum(axis=-1)
+                    gated = np.full_like(probs, -np.inf)
+                    gated[masked] = probs[masked]
+                    rows = [r for r in masked if gated[r] > threshold] or [int(np.argmax(gated))]
+                    for r in rows:
+                        x[a0 + s0 + r] = int(chosen[r])
+                    stats["unmask_updates"] += len(rows)
+                if len(x) - n0 >= max_new_tokens:
+                    break
+            if len(x) - n0 >= max_new_tokens:
+                break
+        gen = x
+        if len(gen) - n0 >= max_new_tokens or done_stop(gen, n0):
+            break
+        if use_cache:  # block-append: the committing forward
+            ids, _ = yield ("step", cache, gen[a0:], 0, bs)
+            cache.prefix_len += bs
+            kv_valid = False
+            nxt = int(ids[-1])
+        else:
+            logits = yield ("dense", gen)
+            nxt = int(np.argmax(logits[-1]))
+        stats["block_recomputes"] += 1
+        stats["block_appends"] += 1
+        gen.append(nxt)
+        if stop_token is not None and nxt == int(stop_token):
+            break
+    return continuation(gen)
+
+
+def generate_batch(engine: Engine, prompts: Sequence[Sequence[int]], *, max_new_tokens: int,
+                   block_size: int = 32, small_block_size: int = 8, threshold: float = 0.9,
+                   use_block_cache: bool = False, mask_id: int, stop_token: int | None = None,
+                   timing: dict | None = None) -> tuple[list[list[int]], list[dict]]:
+    """Decode every prompt; returns (continuations, per-request statistics).  `timing`, when a
+    dict, receives total_ms and prefill_ms (the prefix-cache builds), measured with CUDA events."""
+    if block_size != engine.cfg.bd_size:
+        raise ValueError("block_size must equal the model's bd_size")
+    dev = engine.device
+    stats = [dict(unmask_updates=0, block_recomputes=0, partial_recomputes=0, block_appends=0) for _ in prompts]
+    progs = [request_program(engine, p, max_new_tokens=max_new_tokens, block_size=block_size,
+                             small_block_size=small_block_size, threshold=threshold,
+                             use_block_cache=use_block_cache, mask_id=mask_id, stop_token=stop_token,
+                             stats=st) for p, st in zip(prompts, stats)]
+    results: list[list[int] | None] = [None] * len(progs)
+    pending: dict[int, tuple] = {}
+
+    def advance(i, value):
+        try:
+            pending[i] = progs[i].send(value)
+        except StopIteration as stop:
+            results[i] = list(stop.value)
+            pending.pop(i, None)
+
+    ev = []  # (start, end) CUDA event pairs around prefix-cache builds
+    t0 = torch.cuda.Event(enable_timing=True) if timing is not None else None
+    if t0 is not None:
+        t0.record()
+    for i in range(len(progs)):
+        advance(i, None)
+    while pending:
+        # prefix-cache builds and stateless dense forwards: one request at a time
+        for i in [i for i, op in pending.items() if op[0] != "step"]:
+            op = pending[i]
+            if op[0] == "prefill":
+                _, cache, ids = op
+                if timing is not None:
+                    ev.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+                    ev[-1][0].record()
+                x = engine.embed(torch.tensor(ids, dtype=torch.int32, device=dev))[None]
+                engine.build_prefix_cache(x, None, cache.k, cache.v)
+                if timing is not None:
+                    ev[-1][1].record()
+                advance(i, None)
+            else:
+                _, seq = op
+                x = engine.embed(torch.tensor(seq, dtype=torch.int32, device=dev))[None]
+                hidden = engine.forward_hidden(x, None)
+                advance(i, engine.get_logits(hidden)[0].float().cpu().numpy())
+        steps = [(i, op) for i, op in pending.items() if op[0] == "step"]
+        if not steps:
+            continue
+        # every pending cached step in one batched forward + one fused confidence launch
+        ids_all = torch.tensor([t for _, op in steps for t in op[2]], dtype=torch.int32, device=dev)
+        x = engine.embed(ids_all)
+        reqs = []
+        for _, (_, cache, ids, write_rel, attend_rel) in steps:
+            rows = len(ids)
+            reqs.append(dict(k=cache.k, v=cache.v, rows=rows, prefix_len=cache.prefix_len, write_rel=write_rel,
+                             attend_rel=attend_rel))
+        hidden = engine.forward_cached_batch(x, reqs)
+        cid, cmax = engine.confidence(hidden)
+        cid, cmax = cid.cpu().numpy().astype(np.int64), cmax.cpu().numpy()
+        o = 0
+        for i, op in steps:
+            rows = len(op[2])
+            advance(i, (cid[o:o + rows], cmax[o:o + rows]))
+            o += rows
+    if timing is not None:
+        t1 = torch.cuda.Event(enable_timing=True)
+        t1.record()
+        t1.synchronize()
+        timing["total_ms"] = t0.elapsed_time(t1)
+        timing["prefill_ms"] = sum(a.elapsed_time(b) for a, b in ev)
+    return results, stats
