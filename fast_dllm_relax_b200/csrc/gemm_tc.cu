@@ -365,6 +365,170 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
+// ---- persistent variant for large token counts (M >= 256 rows, no split-K) ------------------------
+// One CTA per SM walks its tiles (slab-major: neighbouring CTAs share a weight slab in L2) with
+// three roles: warp 0 issues TMA for every tile's k blocks through a 4-stage ring, warp 1 issues
+// tcgen05.mma into one of two TMEM accumulators (2 x 256 columns: the whole TMEM), warps 2-9 drain
+// the other accumulator 32 token columns at a time through shared memory into the fused epilogue
+// (two warps per TMEM lane quarter, 16 columns each).
+// The epilogue of tile i therefore overlaps the mainloop of tile i + 1.
+constexpr int kPNT = 256;
+constexpr int kPStages = 4;
+constexpr int kPStage = 128 * 64 * 2 + kPNT * 64 * 2;  // 48 KB
+constexpr int kPChunk = 32;
+constexpr int kPSmem = 1024 + kPStages * kPStage + kPChunk * 128 * 4 + 256;
+static_assert(kPSmem <= 227 * 1024 - 5120, "shared memory budget");
+
+constexpr int kPEpi = 256;  // epilogue threads (warps 2-9)
+
+__global__ void __launch_bounds__(64 + kPEpi, 1)
+    gemm_tc_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const GemmArgs g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = base;  // stage s: A at s * kPStage, B at s * kPStage + 16 KB
+  float* acc = reinterpret_cast<float*>(base + kPStages * kPStage);
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + kPStages * kPStage + kPChunk * 128 * 4);
+  uint64_t* empty = full + kPStages;
+  uint64_t* tfull = empty + kPStages;  // [2] accumulator complete
+  uint64_t* tempty = tfull + 2;        // [2] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  __shared__ __align__(16) unsigned char s_epi[5120];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = g.n_slabs * g.n_tok_tiles;
+  const int nk = g.K / 64;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 1);
+    }
+    mbar_fence_init();
+    tma_prefetch_map(&tmA);
+    tma_prefetch_map(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * kPNT);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      pdl_wait();
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+        const int slab = t / g.n_tok_tiles, tok0 = (t % g.n_tok_tiles) * kPNT;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kPStages;
+          if (!mbar_wait(&empty[s], ((it / kPStages) & 1u) ^ 1u)) {
+            report_error(g.err, kErrTimeoutProducer);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], kPStage);
+          uint8_t* a = ring + s * kPStage;
+          if (g.paired) {
+            tma_load_2d(a, &tmA, &full[s], kb * 64, slab * 64, pol_w);
+            tma_load_2d(a + 8192, &tmA, &full[s], kb * 64, g.N / 2 + slab * 64, pol_w);
+          } else {
+            tma_load_2d(a, &tmA, &full[s], kb * 64, slab * 128, pol_w);
+          }
+          tma_load_2d(a + 16384, &tmB, &full[s], kb * 64, tok0, pol_x);
+        }
+      }
+      for (uint32_t i = it > static_cast<uint32_t>(kPStages) ? it - kPStages : 0u; i < it; ++i)
+        if (!mbar_wait(&full[i % kPStages], (i / kPStages) & 1u)) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = umma_idesc_bf16(128, kPNT);
+      uint32_t it = 0, ti = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++ti) {
+        const uint32_t buf = ti & 1u;
+        if (!mbar_wait(&tempty[buf], ((ti >> 1) & 1u) ^ 1u)) {  // the epilogue released this accumulator
+          report_error(g.err, kErrTimeoutMma);
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t d = tmem + buf * kPNT;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % kPStages;
+          if (!mbar_wait(&full[s], (it / kPStages) & 1u)) {
+            report_error(g.err, kErrTimeoutMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint64_t ad = umma_desc_sw128(ring + s * kPStage);
+          const uint64_t bd = umma_desc_sw128(ring + s * kPStage + 16384);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) tc_mma_bf16(d, ad + 2 * kk, bd + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&empty[s]);
+        }
+        if (ok) tc_commit(&tfull[buf]);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2-9 ----------------
+    const int tid = threadIdx.x - 64;
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;   // which 16 of the chunk's 32 columns it drains
+    pdl_wait();
+    uint32_t ti = 0;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++ti) {
+      const int slab = t / g.n_tok_tiles, tok0 = (t % g.n_tok_tiles) * kPNT;
+      const uint32_t buf = ti & 1u;
+      if (!mbar_wait(&tfull[buf], (ti >> 1) & 1u)) {
+        report_error(g.err, kErrTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after_sync();
+      for (int cb = 0; cb < kPNT && tok0 + cb < g.M; cb += kPChunk) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tmem + buf * kPNT + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(cb + half * 16),
+                           r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[(half * 16 + j) * 128 + q * 32 + lane] = __uint_as_float(r[j]);
+        named_sync(1, kPEpi);
+        gemm_epilogue<bf16>(g, acc - static_cast<size_t>(cb) * 128, kPNT, tok0, slab, cb, cb + kPChunk, s_epi, tid,
+                            kPEpi, 1);
+        named_sync(1, kPEpi);
+      }
+      tc_fence_before_sync();
+      named_sync(1, kPEpi);
+      if (tid == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+  __syncwarp();
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, 2 * kPNT);
+  }
+}
+
+int launch_gemm_tc_persist(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int grid,
+                           cudaStream_t s) {
+  return launch_k(gemm_tc_persist_kernel, dim3(grid), dim3(64 + kPEpi), kPSmem, s, tmA, tmB, a);
+}
+
 template <int NT>
 static int launch_nt(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, cudaStream_t s) {
   using C = TcCfg<NT>;
@@ -381,7 +545,8 @@ static cudaError_t set_attr() {
 }
 
 int init_gemm_tc_attributes() {
-  cudaError_t e = set_attr<16>();
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
+  if (e == cudaSuccess) e = set_attr<16>();
   if (e == cudaSuccess) e = set_attr<32>();
   if (e == cudaSuccess) e = set_attr<64>();
   if (e == cudaSuccess) e = set_attr<128>();

@@ -146,6 +146,19 @@ static int launch_tc_thunk(const GemmArgs& g, const void* a, const void* b, int 
   return launch_gemm_tc(g, *static_cast<const CUtensorMap*>(a), *static_cast<const CUtensorMap*>(b), nt, s);
 }
 
+static int launch_persist_thunk(const GemmArgs& g, const void* a, const void* b, int grid, cudaStream_t s) {
+  return launch_gemm_tc_persist(g, *static_cast<const CUtensorMap*>(a), *static_cast<const CUtensorMap*>(b), grid, s);
+}
+
+// The persistent large-tile GEMM for >= 256 token rows (FDLLM_PERSIST=0 turns it off).
+static bool use_persist(const fdllm_handle* h, int M) {
+  static const bool on = [] {
+    const char* v = std::getenv("FDLLM_PERSIST");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on && h->dtype == FDLLM_BFLOAT16 && M >= 256;
+}
+
 static int launch_simt_thunk(const GemmArgs& g, const void* w, const void* x, int, cudaStream_t s) {
   return launch_gemm_simt_f32(g, static_cast<const float*>(w), static_cast<const float*>(x), s);
 }
@@ -207,6 +220,16 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
     g.norm_eps = h->cfg.rms_norm_eps;
   }
   if (h->dtype == FDLLM_FLOAT32) return timed_launch(h, g, s, launch_simt_thunk, w.ptr, X, 0);
+  if (norm_w == nullptr && post_out == nullptr && use_persist(h, M)) {
+    g.n_slabs = w.paired ? (g.N / 2) / 64 : g.N / 128;
+    g.n_tok_tiles = (M + 255) / 256;
+    g.splits = 1;
+    g.kb_per_split = g.K / 64;
+    const int grid = std::min(h->num_sms, g.n_slabs * g.n_tok_tiles);
+    CUtensorMap tmB;
+    FDLLM_TRY(make_map(&tmB, X, M, g.K, 256));
+    return timed_launch(h, g, s, launch_persist_thunk, &w.map, &tmB, grid);
+  }
   CUtensorMap tmB;
   FDLLM_TRY(make_map(&tmB, X, M, g.K, nt));
   return timed_launch(h, g, s, launch_tc_thunk, &w.map, &tmB, nt);
