@@ -372,18 +372,24 @@ __global__ void __launch_bounds__(128, 1)
 // the other accumulator 32 token columns at a time through shared memory into the fused epilogue
 // (two warps per TMEM lane quarter, 16 columns each).
 // The epilogue of tile i therefore overlaps the mainloop of tile i + 1.
-constexpr int kPNT = 256;
-constexpr int kPStages = 4;
-constexpr int kPStage = 128 * 64 * 2 + kPNT * 64 * 2;  // 48 KB
-constexpr int kPChunk = 32;
-constexpr int kPSmem = 1024 + kPStages * kPStage + kPChunk * 128 * 4 + 256;
-static_assert(kPSmem <= 227 * 1024 - 5120, "shared memory budget");
-
+template <int NT>
+struct PCfg {
+  static constexpr int kStages = NT == 256 ? 4 : 6;
+  static constexpr int kStage = 128 * 64 * 2 + NT * 64 * 2;  // A + B of one k block
+  static constexpr int kChunk = 32;
+  static constexpr int kSmem = 1024 + kStages * kStage + kChunk * 128 * 4 + 256;
+  static_assert(kSmem <= 227 * 1024 - 5120, "shared memory budget");
+};
 constexpr int kPEpi = 256;  // epilogue threads (warps 2-9)
 
+template <int NT>
 __global__ void __launch_bounds__(64 + kPEpi, 1)
     gemm_tc_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const GemmArgs g) {
+  constexpr int kPNT = NT;
+  constexpr int kPStages = PCfg<NT>::kStages;
+  constexpr int kPStage = PCfg<NT>::kStage;
+  constexpr int kPChunk = PCfg<NT>::kChunk;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = base;  // stage s: A at s * kPStage, B at s * kPStage + 16 KB
@@ -446,7 +452,7 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
           } else {
             tma_load_2d(a, &tmA, &full[s], kb * 64, slab * 128, pol_w);
           }
-          tma_load_2d(a + 16384, &tmB, &full[s], kb * 64, tok0, pol_x);
+          tma_load_2d(a + 16384, &tmB, &full[s], kb * 64, tok0, pol_x);  // NT token rows
         }
       }
       for (uint32_t i = it > static_cast<uint32_t>(kPStages) ? it - kPStages : 0u; i < it; ++i)
@@ -524,9 +530,13 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
   }
 }
 
-int launch_gemm_tc_persist(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int grid,
+int launch_gemm_tc_persist(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int nt, int grid,
                            cudaStream_t s) {
-  return launch_k(gemm_tc_persist_kernel, dim3(grid), dim3(64 + kPEpi), kPSmem, s, tmA, tmB, a);
+  if (nt == 256)
+    return launch_k(gemm_tc_persist_kernel<256>, dim3(grid), dim3(64 + kPEpi), PCfg<256>::kSmem, s, tmA, tmB, a);
+  if (nt == 128)
+    return launch_k(gemm_tc_persist_kernel<128>, dim3(grid), dim3(64 + kPEpi), PCfg<128>::kSmem, s, tmA, tmB, a);
+  return cudaErrorInvalidValue;
 }
 
 template <int NT>
@@ -545,7 +555,10 @@ static cudaError_t set_attr() {
 }
 
 int init_gemm_tc_attributes() {
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem);
+  cudaError_t e =
+      cudaFuncSetAttribute(gemm_tc_persist_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<256>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc_persist_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<128>::kSmem);
   if (e == cudaSuccess) e = set_attr<16>();
   if (e == cudaSuccess) e = set_attr<32>();
   if (e == cudaSuccess) e = set_attr<64>();

@@ -222,7 +222,7 @@ cudaError_t launch_kc(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
 // ---- launchers (return a cudaError_t) --------------------------------------------------------
 int launch_gemm_tc(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int nt, cudaStream_t s);
 // Persistent 256-token-tile variant (grid CTAs walk all slab x token tiles; no split-K).
-int launch_gemm_tc_persist(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int grid,
+int launch_gemm_tc_persist(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int nt, int grid,
                            cudaStream_t s);
 int launch_gemm_simt_f32(const GemmArgs& a, const float* W, const float* X, cudaStream_t s);
 int gemm_tc_smem_bytes(int nt);

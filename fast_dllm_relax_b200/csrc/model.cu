@@ -147,7 +147,9 @@ static int launch_tc_thunk(const GemmArgs& g, const void* a, const void* b, int 
 }
 
 static int launch_persist_thunk(const GemmArgs& g, const void* a, const void* b, int grid, cudaStream_t s) {
-  return launch_gemm_tc_persist(g, *static_cast<const CUtensorMap*>(a), *static_cast<const CUtensorMap*>(b), grid, s);
+  const int nt = g.n_tok_tiles * 256 >= g.M + 256 ? 128 : 256;  // recover the tile from the plan
+  return launch_gemm_tc_persist(g, *static_cast<const CUtensorMap*>(a), *static_cast<const CUtensorMap*>(b), nt, grid,
+                                s);
 }
 
 // The persistent large-tile GEMM for >= 256 token rows (FDLLM_PERSIST=0 turns it off).
@@ -222,12 +224,14 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
   if (h->dtype == FDLLM_FLOAT32) return timed_launch(h, g, s, launch_simt_thunk, w.ptr, X, 0);
   if (norm_w == nullptr && post_out == nullptr && use_persist(h, M)) {
     g.n_slabs = w.paired ? (g.N / 2) / 64 : g.N / 128;
-    g.n_tok_tiles = (M + 255) / 256;
+    // 256-token tiles when they cover half the SMs, else 128 (twice the tiles for few-slab weights)
+    const int pnt = 2 * g.n_slabs * ((M + 255) / 256) >= h->num_sms ? 256 : 128;
+    g.n_tok_tiles = (M + pnt - 1) / pnt;
     g.splits = 1;
     g.kb_per_split = g.K / 64;
     const int grid = std::min(h->num_sms, g.n_slabs * g.n_tok_tiles);
     CUtensorMap tmB;
-    FDLLM_TRY(make_map(&tmB, X, M, g.K, 256));
+    FDLLM_TRY(make_map(&tmB, X, M, g.K, pnt));
     return timed_launch(h, g, s, launch_persist_thunk, &w.map, &tmB, grid);
   }
   CUtensorMap tmB;
