@@ -55,8 +55,10 @@ __device__ __forceinline__ uint32_t tile_off(int key, int c) {
   return static_cast<uint32_t>(key * (HD * 2) + ((c ^ (key & 7)) << 4));
 }
 
-template <int HD>
-__global__ void attn_mma_kernel(const AttnArgs a) {
+// At most 6 query heads per KV head (192 threads).  MINB = 2 (two CTAs per SM, <= 170 registers)
+// for launches with more CTAs than SMs; MINB = 1 keeps every accumulator in registers.
+template <int HD, int MINB>
+__global__ void __launch_bounds__(192, MINB) attn_mma_kernel(const AttnArgs a) {
   pdl_trigger();
   pdl_wait();
   constexpr int kChunks = HD / 8;          // 16-byte chunks per key row
@@ -352,18 +354,30 @@ static int launch_mma(const AttnArgs& a, int max_q, cudaStream_t s) {
   constexpr int smem = 4 * kKT * HD * 2;
   cudaError_t e;
   dim3 grid((max_q + kQT - 1) / kQT, a.hkv, a.n_reqs * a.n_splits);
-  e = launch_kc(attn_mma_kernel<HD>, grid, dim3(G * 32), smem, s, a.n_splits, a);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (static_cast<long long>(grid.x) * grid.y * grid.z > sms)
+    e = launch_kc(attn_mma_kernel<HD, 2>, grid, dim3(G * 32), smem, s, a.n_splits, a);
+  else
+    e = launch_kc(attn_mma_kernel<HD, 1>, grid, dim3(G * 32), smem, s, a.n_splits, a);
   return e;
 }
 
 int init_gemm_tc_attributes();
 
+template <int HD, int MINB>
+static cudaError_t attn_attrs() {
+  cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<HD, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * kKT * HD * 2);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_mma_kernel<HD, MINB>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
+}
+
 int init_kernel_attributes() {
-  cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * kKT * 128 * 2);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * kKT * 64 * 2);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_mma_kernel<128>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_mma_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t e = attn_attrs<128, 1>();
+  if (e == cudaSuccess) e = attn_attrs<128, 2>();
+  if (e == cudaSuccess) e = attn_attrs<64, 1>();
+  if (e == cudaSuccess) e = attn_attrs<64, 2>();
   if (e == cudaSuccess) e = static_cast<cudaError_t>(init_gemm_tc_attributes());
   if (e == cudaSuccess) e = static_cast<cudaError_t>(init_stack_attributes());
   return e;
@@ -372,7 +386,7 @@ int init_kernel_attributes() {
 int launch_attention(const AttnArgs& a, int max_q, int dtype, cudaStream_t s) {
   if (a.hq % a.hkv != 0 || a.hd % 32 != 0 || a.hd > 128) return cudaErrorInvalidValue;
   const int G = a.hq / a.hkv;
-  if (dtype == 1 && (a.hd == 128 || a.hd == 64) && G <= 32) {
+  if (dtype == 1 && (a.hd == 128 || a.hd == 64) && G <= 6) {
     return a.hd == 128 ? launch_mma<128>(a, max_q, s) : launch_mma<64>(a, max_q, s);
   }
   AttnArgs b = a;
