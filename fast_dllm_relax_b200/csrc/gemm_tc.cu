@@ -404,6 +404,13 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tiles = g.n_slabs * g.n_tok_tiles;
   const int nk = g.K / 64;
+  const int S = g.splits > 1 ? g.splits : 1;  // split-K: unit = (tile, split), neighbours split one tile
+  const int n_units = n_tiles * S;
+  auto kb_range = [&](int u, int* kb0, int* kb1) {
+    const int sp = u % S;
+    *kb0 = sp * g.kb_per_split;
+    *kb1 = min(nk, *kb0 + g.kb_per_split);
+  };
   if (threadIdx.x == 0) {
     for (int i = 0; i < kPStages; ++i) {
       mbar_init(&full[i], 1);
@@ -435,9 +442,12 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
       pdl_wait();
       uint32_t it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        const int t = u / S;
         const int slab = t / g.n_tok_tiles, tok0 = (t % g.n_tok_tiles) * kPNT;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        int kb0, kb1;
+        kb_range(u, &kb0, &kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kPStages;
           if (!mbar_wait(&empty[s], ((it / kPStages) & 1u) ^ 1u)) {
             report_error(g.err, kErrTimeoutProducer);
@@ -464,15 +474,17 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
       constexpr uint32_t idesc = umma_idesc_bf16(128, kPNT);
       uint32_t it = 0, ti = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++ti) {
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++ti) {
         const uint32_t buf = ti & 1u;
+        int kb0, kb1;
+        kb_range(u, &kb0, &kb1);
         if (!mbar_wait(&tempty[buf], ((ti >> 1) & 1u) ^ 1u)) {  // the epilogue released this accumulator
           report_error(g.err, kErrTimeoutMma);
           break;
         }
         tc_fence_after_sync();
         const uint32_t d = tmem + buf * kPNT;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kPStages;
           if (!mbar_wait(&full[s], (it / kPStages) & 1u)) {
             report_error(g.err, kErrTimeoutMma);
@@ -483,7 +495,7 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
           const uint64_t ad = umma_desc_sw128(ring + s * kPStage);
           const uint64_t bd = umma_desc_sw128(ring + s * kPStage + 16384);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) tc_mma_bf16(d, ad + 2 * kk, bd + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) tc_mma_bf16(d, ad + 2 * kk, bd + 2 * kk, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           tc_commit(&empty[s]);
         }
         if (ok) tc_commit(&tfull[buf]);
@@ -495,8 +507,10 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;   // which 16 of the chunk's 32 columns it drains
     pdl_wait();
+    __shared__ int s_last;
     uint32_t ti = 0;
-    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++ti) {
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++ti) {
+      const int t = u / S, sp = u % S;
       const int slab = t / g.n_tok_tiles, tok0 = (t % g.n_tok_tiles) * kPNT;
       const uint32_t buf = ti & 1u;
       if (!mbar_wait(&tfull[buf], (ti >> 1) & 1u)) {
@@ -504,6 +518,8 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
         break;
       }
       tc_fence_after_sync();
+      // split-K: this unit's fp32 partial tile [NT][128] (tile t, split sp)
+      float4* mine = S > 1 ? reinterpret_cast<float4*>(g.ppart + (static_cast<size_t>(t) * S + sp) * kPNT * 128) : nullptr;
       for (int cb = 0; cb < kPNT && tok0 + cb < g.M; cb += kPChunk) {
         uint32_t r[16];
         tmem_ld_32x32b_x16(tmem + buf * kPNT + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(cb + half * 16),
@@ -512,13 +528,57 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
 #pragma unroll
         for (int j = 0; j < 16; ++j) acc[(half * 16 + j) * 128 + q * 32 + lane] = __uint_as_float(r[j]);
         named_sync(1, kPEpi);
-        gemm_epilogue<bf16>(g, acc - static_cast<size_t>(cb) * 128, kPNT, tok0, slab, cb, cb + kPChunk, s_epi, tid,
-                            kPEpi, 1);
+        if (S > 1) {  // publish this split's chunk; the tile's last split finishes the tile
+          const float4* a4 = reinterpret_cast<const float4*>(acc);
+          for (int i = tid; i < kPChunk * 32; i += kPEpi) __stcg(mine + cb * 32 + i, a4[i]);
+        } else {
+          gemm_epilogue<bf16>(g, acc - static_cast<size_t>(cb) * 128, kPNT, tok0, slab, cb, cb + kPChunk, s_epi, tid,
+                              kPEpi, 1);
+        }
         named_sync(1, kPEpi);
       }
       tc_fence_before_sync();
       named_sync(1, kPEpi);
-      if (tid == 0) mbar_arrive(&tempty[buf]);
+      if (tid == 0) mbar_arrive(&tempty[buf]);  // the accumulator is free for the tile after next
+      if (S > 1) {
+        if (tid == 0) {
+          __threadfence();
+          const unsigned old = atomicAdd(g.pctr + t, 1u);
+          s_last = (old == static_cast<unsigned>(S) - 1u) ? 1 : 0;
+          if (s_last) {
+            __threadfence();
+            g.pctr[t] = 0u;  // the last arrival: nobody else touches this counter in this launch
+          }
+        }
+        named_sync(1, kPEpi);
+        if (s_last) {  // sum the S partials in split order (deterministic), then the epilogue
+          const float4* p0 = reinterpret_cast<const float4*>(g.ppart + static_cast<size_t>(t) * S * kPNT * 128);
+          for (int cb = 0; cb < kPNT && tok0 + cb < g.M; cb += kPChunk) {
+            float4* a4 = reinterpret_cast<float4*>(acc);
+            for (int i = tid; i < kPChunk * 32; i += kPEpi) {
+              float4 v[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                v[j] = j < S ? __ldcg(p0 + static_cast<size_t>(j) * kPNT * 32 + cb * 32 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+              float4 sum = v[0];
+#pragma unroll
+              for (int j = 1; j < 4; ++j) {
+                if (j < S) {
+                  sum.x += v[j].x;
+                  sum.y += v[j].y;
+                  sum.z += v[j].z;
+                  sum.w += v[j].w;
+                }
+              }
+              a4[i] = sum;
+            }
+            named_sync(1, kPEpi);
+            gemm_epilogue<bf16>(g, acc - static_cast<size_t>(cb) * 128, kPNT, tok0, slab, cb, cb + kPChunk, s_epi, tid,
+                                kPEpi, 1);
+            named_sync(1, kPEpi);
+          }
+        }
+      }
     }
   }
   __syncwarp();

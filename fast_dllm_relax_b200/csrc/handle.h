@@ -138,6 +138,8 @@ struct fdllm_handle {
   DevBuf<ReqDesc> reqs;
   DevBuf<float> conf_part, tmp_maxp, ss;  // ss: per-slab row sums of squares
   DevBuf<unsigned> post_ctr;                // post-norm arrival counters (zero between launches)
+  DevBuf<float> persist_part;               // persistent-GEMM split-K partial tiles
+  DevBuf<unsigned> persist_ctr;             // persistent-GEMM per-tile split counters (zero between launches)
   // persistent layer-stack kernel: weight maps and per-layer pointers (built at bind), partials,
   // barrier / arrival counters (zeroed before every launch)
   DevBuf<uint8_t> stack_maps, stack_layers;

@@ -98,6 +98,10 @@ struct GemmArgs {
   const void* post_w;
   void* post_out;
   unsigned* post_ctr;
+  // persistent GEMM split-K (splits <= 4): fp32 partial tiles [tiles][splits][NT][128] and per-tile
+  // arrival counters (zero between launches; the last split resets its tile's counter)
+  float* ppart;
+  unsigned* pctr;
   int* err;
   Epilogue epi;
 };

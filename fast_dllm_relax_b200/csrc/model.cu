@@ -227,9 +227,25 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
     // 256-token tiles when they cover half the SMs, else 128 (twice the tiles for few-slab weights)
     const int pnt = 2 * g.n_slabs * ((M + 255) / 256) >= h->num_sms ? 256 : 128;
     g.n_tok_tiles = (M + pnt - 1) / pnt;
-    g.splits = 1;
-    g.kb_per_split = g.K / 64;
-    const int grid = std::min(h->num_sms, g.n_slabs * g.n_tok_tiles);
+    const int tiles = g.n_slabs * g.n_tok_tiles;
+    const int kblocks = g.K / 64;
+    // split K (<= 4 ways, >= 8 k blocks each) while the tiles alone leave SMs idle -- off unless
+    // FDLLM_PERSIST_SPLITK=1: measured slower (the last split's serial merge outweighs the idle SMs)
+    static const bool splitk = [] {
+      const char* v = std::getenv("FDLLM_PERSIST_SPLITK");
+      return v != nullptr && v[0] == '1';
+    }();
+    int splits = 1;
+    while (splitk && splits < 4 && tiles * splits < h->num_sms && kblocks / (2 * splits) >= 8) splits *= 2;
+    g.splits = splits;
+    g.kb_per_split = (kblocks + splits - 1) / splits;
+    if (splits > 1) {
+      FDLLM_TRY(h->persist_part.ensure(static_cast<size_t>(tiles) * splits * pnt * 128));
+      FDLLM_TRY(h->persist_ctr.ensure(static_cast<size_t>(tiles), true));
+      g.ppart = h->persist_part.p;
+      g.pctr = h->persist_ctr.p;
+    }
+    const int grid = std::min(h->num_sms, tiles * splits);
     CUtensorMap tmB;
     FDLLM_TRY(make_map(&tmB, X, M, g.K, pnt));
     return timed_launch(h, g, s, launch_persist_thunk, &w.map, &tmB, grid);
@@ -695,6 +711,8 @@ int fdllm_destroy(fdllm_handle* h) {
   h->stack_layers.release();
   h->stack_sync.release();
   h->post_ctr.release();
+  h->persist_part.release();
+  h->persist_ctr.release();
   h->stack_trace.release();
   h->reqs.release();
   if (h->dec.host) cudaFreeHost(h->dec.host);
