@@ -189,8 +189,13 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
     const int x = v ? std::atoi(v) : 1;
     return x >= 1 && x <= 4 ? x : 1;
   }();
+  static const int split_max = [] {  // tuning override: largest split-K cluster
+    const char* v = std::getenv("FDLLM_SPLIT_MAX");
+    const int x = v ? std::atoi(v) : 16;
+    return x >= 1 && x <= 16 ? x : 16;
+  }();
   if (tiles < target * h->num_sms) {  // split K over a cluster of at most 16 CTAs
-    splits = std::max(1, std::min({kblocks, target * h->num_sms / tiles, 16}));
+    splits = std::max(1, std::min({kblocks, target * h->num_sms / tiles, split_max}));
     const int kpb = (kblocks + splits - 1) / splits;
     splits = (kblocks + kpb - 1) / kpb;
   }
