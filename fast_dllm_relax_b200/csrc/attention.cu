@@ -251,14 +251,16 @@ __global__ void __launch_bounds__(192, MINB) attn_mma_kernel(const AttnArgs a) {
     // needed); member r then merges query rows [r*R/S, (r+1)*R/S) over all members through
     // distributed shared memory: out = sum_s w_s o_s / sum_s w_s, w_s = exp(lse_s - max lse).
     __shared__ float s_lse[kQT * 8];
-    float* o_s = reinterpret_cast<float*>(smem);  // [16 * G][HD] fp32
+    __shared__ float s_w[kQT * 4][kMaxAttnSplits + 1];  // merge weights of this member's rows, 1/sum
+    constexpr int kOP = HD + 4;  // padded fp32 partial rows: the float2 writes hit distinct banks
+    float* o_s = reinterpret_cast<float*>(smem);  // [16 * G][kOP] fp32
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int rr = warp * 16 + g8 + h * 8;
       const float inv = l_run[h] > 0.f ? 1.f / l_run[h] : 0.f;
 #pragma unroll
       for (int n = 0; n < HD / 8; ++n)
-        *reinterpret_cast<float2*>(o_s + rr * HD + n * 8 + 2 * t4) = make_float2(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
+        *reinterpret_cast<float2*>(o_s + rr * kOP + n * 8 + 2 * t4) = make_float2(o[n][2 * h] * inv, o[n][2 * h + 1] * inv);
       if (t4 == 0) s_lse[rr] = (valid_row[h] && l_run[h] > 0.f) ? m_run[h] + logf(l_run[h]) : -INFINITY;
     }
     cluster_sync();  // every member's partial is in its shared memory
@@ -268,11 +270,7 @@ __global__ void __launch_bounds__(192, MINB) attn_mma_kernel(const AttnArgs a) {
     const int rows = kQT * G;
     const int r0 = static_cast<int>(rank * rows / S), r1 = static_cast<int>((rank + 1) * rows / S);
     const uint32_t o_addr = smem_addr(o_s), lse_addr = smem_addr(s_lse);
-    bf16* out = static_cast<bf16*>(a.out);
-    for (int idx = threadIdx.x; idx < (r1 - r0) * (HD / 4); idx += blockDim.x) {
-      const int rr = r0 + idx / (HD / 4), c4 = idx % (HD / 4);
-      const int tq = tq0 + rr / G;
-      if (tq >= r.n_q) continue;
+    for (int rr = r0 + threadIdx.x; rr < r1; rr += blockDim.x) {  // per-row member weights, once
       float l[kMaxS];
       float mx = -INFINITY;
 #pragma unroll
@@ -280,21 +278,36 @@ __global__ void __launch_bounds__(192, MINB) attn_mma_kernel(const AttnArgs a) {
         l[m] = (static_cast<uint32_t>(m) < S) ? ld_dsmem_f32(map_shared_rank(lse_addr + rr * 4, m)) : -INFINITY;
         mx = fmaxf(mx, l[m]);
       }
-      float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
       float den = 0.f;
 #pragma unroll
       for (int m = 0; m < kMaxS; ++m) {
-        if (static_cast<uint32_t>(m) < S && l[m] != -INFINITY) {
-          const float w = expf(l[m] - mx);
-          const float4 v = ld_dsmem_f4(map_shared_rank(o_addr + (rr * HD + c4 * 4) * 4, m));
-          num.x += w * v.x;
-          num.y += w * v.y;
-          num.z += w * v.z;
-          num.w += w * v.w;
-          den += w;
-        }
+        const float w = (static_cast<uint32_t>(m) < S && l[m] != -INFINITY) ? expf(l[m] - mx) : 0.f;
+        s_w[rr - r0][m] = w;
+        den += w;
       }
-      const float inv = den > 0.f ? 1.f / den : 0.f;
+      s_w[rr - r0][kMaxS] = den > 0.f ? 1.f / den : 0.f;
+    }
+    __syncthreads();
+    bf16* out = static_cast<bf16*>(a.out);
+    for (int idx = threadIdx.x; idx < (r1 - r0) * (HD / 4); idx += blockDim.x) {
+      const int rr = r0 + idx / (HD / 4), c4 = idx % (HD / 4);
+      const int tq = tq0 + rr / G;
+      if (tq >= r.n_q) continue;
+      float4 v[kMaxS];
+#pragma unroll
+      for (int m = 0; m < kMaxS; ++m)  // all members' chunks in flight at once
+        v[m] = (static_cast<uint32_t>(m) < S) ? ld_dsmem_f4(map_shared_rank(o_addr + (rr * kOP + c4 * 4) * 4, m))
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int m = 0; m < kMaxS; ++m) {
+        const float w = s_w[rr - r0][m];
+        num.x += w * v[m].x;
+        num.y += w * v[m].y;
+        num.z += w * v[m].z;
+        num.w += w * v[m].w;
+      }
+      const float inv = s_w[rr - r0][kMaxS];
       bf16* op = out + static_cast<size_t>(r.q_tok0 + tq) * (a.hq * HD) + (kvh * G + rr % G) * HD + c4 * 4;
       *reinterpret_cast<__nv_bfloat162*>(op) = __floats2bfloat162_rn(num.x * inv, num.y * inv);
       *reinterpret_cast<__nv_bfloat162*>(op + 2) = __floats2bfloat162_rn(num.z * inv, num.w * inv);
