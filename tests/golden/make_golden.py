@@ -1,9 +1,8 @@
 """Generate the golden decode/scoring fixtures from the reference's own runtime.
 
-Run in a container where the reference checkout exists (default /root/reference; override with
-FDLLM_REFERENCE=<path>):
+Run where a checkout of the reference exists, naming it:
 
-    python tests/golden/make_golden.py
+    FDLLM_REFERENCE=<path to the reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's UNMODIFIED `fast_dllm_relax/runtime.py` (and model/cuda.py's bias and
 shift helpers) on top of this repository's TVM stand-in, with a VirtualMachine whose nine entry
@@ -30,7 +29,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("FDLLM_REFERENCE", "/root/reference"))
+if "FDLLM_REFERENCE" not in os.environ:
+    raise SystemExit("set FDLLM_REFERENCE to the reference checkout")
+REF = Path(os.environ["FDLLM_REFERENCE"])
 
 sys.path.insert(0, str(REPO / "fast_dllm_relax_b200" / "tvm_shim"))
 sys.path.insert(0, str(REPO))
