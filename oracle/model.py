@@ -27,7 +27,8 @@ agree for the 1.5B model (head_dim 128) and only the former keeps cached == dens
 Parity of this restatement against the reference's own execution is unpinned for the model
 arithmetic (TVM and the checkpoint's remote modeling code cannot run here); it is pinned by the
 reference's invariants (cached == dense, partial == full rows, tied == untied, sentinel windows)
-and cross-checked against transformers' Qwen2 in fp32.  The decode-loop restatement in
+and cross-checked against transformers' Qwen2ForCausalLM in fp32 (tests/test_oracle_vs_transformers.py:
+dense forward and logits within 1e-5).  The decode-loop restatement in
 `oracle/decode.py` is pinned against the reference's own runtime.py (tests/golden/).
 """
 
