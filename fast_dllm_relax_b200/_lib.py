@@ -23,6 +23,7 @@ DEVICE_ERRORS = {
     0: "none", 1: "TMA producer wait expired", 2: "MMA issuer wait expired", 3: "epilogue wait expired",
     4: "token id outside the vocabulary", 5: "RoPE position outside the table", 6: "KV write outside the cache",
     7: "bounded-wait self test expired", 8: "layer-stack grid barrier or merge wait expired",
+    9: "device refinement loop exceeded its iteration limit",
 }
 
 

@@ -24,6 +24,7 @@ enum DeviceError : int {
   kErrCacheRange = 6,        // a KV write outside the cache capacity
   kErrTimeoutTest = 7,       // the bounded-wait self test expired (expected in that test)
   kErrTimeoutBarrier = 8,    // the layer-stack kernel waited too long at a grid barrier or merge
+  kErrLoopLimit = 9,         // a device-side refinement loop exceeded its iteration limit
 };
 
 __device__ __forceinline__ void report_error(int* err, int code) {

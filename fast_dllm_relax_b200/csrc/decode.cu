@@ -21,6 +21,63 @@ namespace {
 constexpr int kWin = 32;                  // max sub-block width read back per step
 constexpr int kHostInts = 2 + 2 * kWin;   // pinned read-back: status[2], window tokens, unmask flags
 
+// ---- device-side block loop (CUDA graph WHILE and IF/ELSE nodes) -----------------------------
+// Loop state in device memory, read back once per block.
+enum LoopSlot : int {
+  kLKvValid = 0,    // the block's K/V rows hold a full step's values (partial steps allowed)
+  kLPartial = 1,    // the current step is a partial one
+  kLIter = 2,       // refinement steps in the current sub-block
+  kLUnmask = 3,     // statistics: positions unmasked, refinement forwards, partial forwards
+  kLRecompute = 4,
+  kLPartialCnt = 5,
+  kLToken = 6,      // the block-append forward's next token
+  kLSlots = 8,
+};
+constexpr int kLoopLimit = 64;  // refinement steps per sub-block before the loop gives up (>= width)
+
+// Before a sub-block's WHILE node: loop while the window still holds masks.
+__global__ void loop_init_kernel(const int* block, int s0, int len, int mask_id, int* st,
+                                 cudaGraphConditionalHandle hw) {
+  int any = 0;
+  for (int j = 0; j < len; ++j) any |= block[s0 + j] == mask_id;
+  st[kLIter] = 0;
+  cudaGraphSetConditional(hw, any ? 1u : 0u);
+}
+
+// Body head: the step is partial when the block cache is on, a full step of this block has run
+// and the window's first position is decided (runtime.py:760-764).
+__global__ void loop_choose_kernel(const int* block, int s0, int mask_id, int use_block_cache, int* st,
+                                   cudaGraphConditionalHandle hi) {
+  const int partial = (use_block_cache && st[kLKvValid] && block[s0] != mask_id) ? 1 : 0;
+  st[kLPartial] = partial;
+  cudaGraphSetConditional(hi, static_cast<unsigned>(partial));
+}
+
+// Body tail: statistics, the block-cache state, and whether the window still holds masks.
+__global__ void loop_end_kernel(const int* status, int use_block_cache, int* st, int* err,
+                                cudaGraphConditionalHandle hw) {
+  st[kLUnmask] += status[1];
+  st[kLRecompute] += 1;
+  if (st[kLPartial]) {
+    st[kLPartialCnt] += 1;
+  } else {
+    st[kLKvValid] = use_block_cache;
+  }
+  const int it = ++st[kLIter];
+  unsigned more = status[0] > 0 ? 1u : 0u;
+  if (it >= kLoopLimit && more) {  // every step unmasks at least one position: never reached
+    report_error(err, kErrLoopLimit);
+    more = 0u;
+  }
+  cudaGraphSetConditional(hw, more);
+}
+
+__global__ void loop_reset_kernel(int* st) {
+  for (int i = 0; i < kLSlots; ++i) st[i] = 0;
+}
+
+__global__ void loop_token_kernel(const int* cids, int row, int* st) { st[kLToken] = cids[row]; }
+
 struct Driver {
   fdllm_handle* h;
   cudaStream_t s;  // the handle's own non-blocking decode stream (capturable)
@@ -51,6 +108,7 @@ struct Driver {
     FDLLM_TRY(h->dec.cmax.ensure(static_cast<size_t>(bs)));
     FDLLM_TRY(h->dec.out.ensure(kHostInts));
     FDLLM_TRY(h->dec.plen.ensure(1));
+    FDLLM_TRY(h->dec.loop.ensure(kLSlots));
     if (h->dec.host == nullptr) CUDA_TRY(cudaMallocHost(&h->dec.host, kHostInts * sizeof(int)));
     if (h->dec.host_params == nullptr) CUDA_TRY(cudaMallocHost(&h->dec.host_params, 16 * sizeof(int)));
     if (h->dec.stream == nullptr) CUDA_TRY(cudaStreamCreateWithFlags(&h->dec.stream, cudaStreamNonBlocking));
@@ -84,7 +142,7 @@ struct Driver {
   // partial step; the prefix length is read from h->dec.plen), the fused lm_head + confidence, then
   // either the unmask of window [s0, s0+len) or (append) the last row's token; results are copied
   // to the pinned host buffer.  Recorded once per step shape into a CUDA graph.
-  int record(int kind, int s0, int len) {
+  int record(int kind, int s0, int len, bool host_copy = true) {
     const bool partial = kind == 1;
     const int rows = partial ? len : bs;
     CUDA_TRY(launch_embed(h->dec.block.p + (partial ? s0 : 0), rows, h->embed, h->cfg.vocab_size, h->cfg.hidden_size,
@@ -104,12 +162,164 @@ struct Driver {
     FDLLM_TRY(confidence_locked(h, h->dec.hid.p, rows, h->dec.cids.p, h->dec.cmax.p, nullptr, nullptr, s));
     int* out = h->dec.out.p;
     if (kind == 2) {
-      CUDA_TRY(cudaMemcpyAsync(host(), h->dec.cids.p + bs - 1, sizeof(int), cudaMemcpyDeviceToHost, s));
+      if (host_copy) {
+        CUDA_TRY(cudaMemcpyAsync(host(), h->dec.cids.p + bs - 1, sizeof(int), cudaMemcpyDeviceToHost, s));
+      } else {
+        loop_token_kernel<<<1, 1, 0, s>>>(h->dec.cids.p, bs - 1, h->dec.loop.p);
+        count_launch();
+        CUDA_TRY(cudaGetLastError());
+      }
     } else {
       CUDA_TRY(launch_unmask(h->dec.cids.p, h->dec.cmax.p, rows, h->dec.block.p, s0, len, partial ? 1 : 0, mask_id,
                              thr, out + 2, nullptr, out + 2 + kWin, out, s));
-      CUDA_TRY(cudaMemcpyAsync(host(), out, kHostInts * sizeof(int), cudaMemcpyDeviceToHost, s));
+      if (host_copy) CUDA_TRY(cudaMemcpyAsync(host(), out, kHostInts * sizeof(int), cudaMemcpyDeviceToHost, s));
     }
+    return FDLLM_OK;
+  }
+
+  // Append the work captured on stream `s` to `graph` after `deps`; *leaf receives the captured
+  // work's last node.
+  template <typename F>
+  int capture_into(cudaGraph_t graph, const cudaGraphNode_t* deps, size_t ndeps, cudaGraphNode_t* leaf, F&& body) {
+    CUDA_TRY(cudaStreamBeginCaptureToGraph(s, graph, deps, nullptr, ndeps, cudaStreamCaptureModeRelaxed));
+    const int rc = body();
+    cudaStreamCaptureStatus cs;
+    const cudaGraphNode_t* leaves = nullptr;
+    size_t nleaves = 0;
+    cudaGraph_t g2 = nullptr;
+    const cudaError_t ei = cudaStreamGetCaptureInfo(s, &cs, nullptr, &g2, &leaves, &nleaves);
+    *leaf = (ei == cudaSuccess && nleaves > 0) ? leaves[nleaves - 1] : nullptr;
+    cudaGraph_t out = nullptr;
+    const cudaError_t ee = cudaStreamEndCapture(s, &out);
+    if (rc != FDLLM_OK) return rc;
+    if (ei != cudaSuccess) return fail(FDLLM_ERR_CUDA, std::string("cudaStreamGetCaptureInfo: ") + cudaGetErrorString(ei));
+    if (ee != cudaSuccess) return fail(FDLLM_ERR_CUDA, std::string("capture into graph: ") + cudaGetErrorString(ee));
+    if (nleaves != 1) return fail(FDLLM_ERR_CUDA, "captured block work does not end in a single node");
+    return FDLLM_OK;
+  }
+
+  // Build the graph of one whole block: for each sub-block, WHILE (masks in its window)
+  // { IF (partial) partial step ELSE full step }, then the block-append forward; the block's
+  // tokens and the loop state are copied to the host at the end.
+  int build_block_graph(BlockGraph* bg) {
+    FDLLM_TRY(reserve_workspace(h, bs, 1, cap));
+    const unsigned long long gen = g_ws_generation.load();
+    cudaGraph_t g = nullptr;
+    CUDA_TRY(cudaGraphCreate(&g, 0));
+    struct GraphGuard {
+      cudaGraph_t g;
+      ~GraphGuard() { if (g) cudaGraphDestroy(g); }
+    } guard{g};
+    const long long launches_before = launch_count();
+    int* st = h->dec.loop.p;
+    int* out = h->dec.out.p;
+    int n_full = 0, n_partial = 0;
+    cudaGraphNode_t prev = nullptr;
+    FDLLM_TRY(capture_into(g, nullptr, 0, &prev, [&]() -> int {
+      loop_reset_kernel<<<1, 1, 0, s>>>(st);
+      count_launch();
+      CUDA_TRY(cudaGetLastError());
+      return FDLLM_OK;
+    }));
+    for (int s0 = 0; s0 < bs; s0 += sbs) {
+      const int len = std::min(bs, s0 + sbs) - s0;
+      cudaGraphConditionalHandle hw;
+      CUDA_TRY(cudaGraphConditionalHandleCreate(&hw, g, 0, 0));
+      cudaGraphNode_t init = nullptr;
+      FDLLM_TRY(capture_into(g, &prev, 1, &init, [&]() -> int {
+        loop_init_kernel<<<1, 1, 0, s>>>(h->dec.block.p, s0, len, mask_id, st, hw);
+        count_launch();
+        CUDA_TRY(cudaGetLastError());
+        return FDLLM_OK;
+      }));
+      cudaGraphNodeParams wp{};
+      wp.type = cudaGraphNodeTypeConditional;
+      wp.conditional.handle = hw;
+      wp.conditional.type = cudaGraphCondTypeWhile;
+      wp.conditional.size = 1;
+      cudaGraphNode_t wnode = nullptr;
+      CUDA_TRY(cudaGraphAddNode(&wnode, g, &init, 1, &wp));
+      cudaGraph_t body = wp.conditional.phGraph_out[0];
+      // body: choose -> IF (partial) / ELSE (full) -> end
+      cudaGraphConditionalHandle hi;
+      CUDA_TRY(cudaGraphConditionalHandleCreate(&hi, body, 0, 0));
+      cudaGraphNode_t choose = nullptr;
+      FDLLM_TRY(capture_into(body, nullptr, 0, &choose, [&]() -> int {
+        loop_choose_kernel<<<1, 1, 0, s>>>(h->dec.block.p, s0, mask_id, block_cache ? 1 : 0, st, hi);
+        count_launch();
+        CUDA_TRY(cudaGetLastError());
+        return FDLLM_OK;
+      }));
+      cudaGraphNodeParams ip{};
+      ip.type = cudaGraphNodeTypeConditional;
+      ip.conditional.handle = hi;
+      ip.conditional.type = cudaGraphCondTypeIf;
+      ip.conditional.size = 2;  // body 0: condition true (partial), body 1: else (full)
+      cudaGraphNode_t inode = nullptr;
+      CUDA_TRY(cudaGraphAddNode(&inode, body, &choose, 1, &ip));
+      cudaGraphNode_t leaf = nullptr;
+      long long c0 = launch_count();
+      FDLLM_TRY(capture_into(ip.conditional.phGraph_out[0], nullptr, 0, &leaf, [&]() { return record(1, s0, len, false); }));
+      n_partial = static_cast<int>(launch_count() - c0);
+      c0 = launch_count();
+      FDLLM_TRY(capture_into(ip.conditional.phGraph_out[1], nullptr, 0, &leaf, [&]() { return record(0, s0, len, false); }));
+      n_full = static_cast<int>(launch_count() - c0);
+      cudaGraphNode_t endn = nullptr;
+      FDLLM_TRY(capture_into(body, &inode, 1, &endn, [&]() -> int {
+        loop_end_kernel<<<1, 1, 0, s>>>(out, block_cache ? 1 : 0, st, h->err.p, hw);
+        count_launch();
+        CUDA_TRY(cudaGetLastError());
+        return FDLLM_OK;
+      }));
+      prev = wnode;
+    }
+    cudaGraphNode_t last = nullptr;
+    const long long c_app = launch_count();
+    FDLLM_TRY(capture_into(g, &prev, 1, &last, [&]() -> int {
+      FDLLM_TRY(record(2, 0, bs, false));
+      CUDA_TRY(cudaMemcpyAsync(host(), h->dec.block.p, bs * sizeof(int), cudaMemcpyDeviceToHost, s));
+      CUDA_TRY(cudaMemcpyAsync(host() + kWin, st, kLSlots * sizeof(int), cudaMemcpyDeviceToHost, s));
+      return FDLLM_OK;
+    }));
+    const int n_append = static_cast<int>(launch_count() - c_app);
+    // recorded launches did not run; the block's launches are counted when it replays
+    count_launch(-static_cast<int>(launch_count() - launches_before));
+    if (g_ws_generation.load() != gen) return fail(FDLLM_ERR_CUDA, "workspace reallocated while building the block graph");
+    if (bg->exec) cudaGraphExecDestroy(bg->exec);
+    bg->exec = nullptr;
+    CUDA_TRY(cudaGraphInstantiate(&bg->exec, g, 0));
+    bg->gen = gen;
+    bg->mask_id = mask_id;
+    bg->thr = thr;
+    bg->use_block_cache = block_cache ? 1 : 0;
+    bg->sbs = sbs;
+    bg->n_full = n_full;
+    bg->n_partial = n_partial;
+    bg->n_append = n_append;
+    return FDLLM_OK;
+  }
+
+  // Run one whole block on the device; x_block receives its tokens, *tok the appended token.
+  int run_block(int* x_block, int* tok) {
+    BlockGraph& bg = h->dec.block_graph;
+    const bool stale = bg.exec == nullptr || bg.gen != g_ws_generation.load() || bg.mask_id != mask_id ||
+                       bg.thr != thr || bg.use_block_cache != (block_cache ? 1 : 0) || bg.sbs != sbs;
+    if (stale) FDLLM_TRY(build_block_graph(&bg));
+    h->dec.host_params[0] = prefix_len;
+    CUDA_TRY(cudaMemcpyAsync(h->dec.plen.p, h->dec.host_params, sizeof(int), cudaMemcpyHostToDevice, s));
+    CUDA_TRY(cudaGraphLaunch(bg.exec, s));
+    CUDA_TRY(cudaStreamSynchronize(s));
+    const int* hb = host();
+    std::memcpy(x_block, hb, bs * sizeof(int));
+    const int* ls = hb + kWin;
+    const int full_steps = ls[kLRecompute] - ls[kLPartialCnt];
+    count_launch(1 + (bs + sbs - 1) / sbs + 2 * ls[kLRecompute] + full_steps * bg.n_full +
+                 ls[kLPartialCnt] * bg.n_partial + bg.n_append);  // kernels this replay ran
+    st[0] += ls[kLUnmask];
+    st[1] += ls[kLRecompute] + 1;  // + the block-append forward
+    st[2] += ls[kLPartialCnt];
+    st[3] += 1;
+    *tok = ls[kLToken];
     return FDLLM_OK;
   }
 
@@ -231,6 +441,10 @@ extern "C" int fdllm_generate(fdllm_handle* h, const int32_t* prompt, int prompt
   std::lock_guard<std::mutex> lock(h->mu);
   CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));  // the caller's prior work is done
   Driver d{h, nullptr, block_size, small_block_size, mask_id, stop_token, threshold, use_block_cache != 0};
+  // device-side block loops: without a stop token (checked on the host between steps) and without
+  // per-launch profiling events; FDLLM_BLOCK_GRAPH=0 turns them off
+  const char* bgv = std::getenv("FDLLM_BLOCK_GRAPH");
+  const bool use_block_graph = stop_token < 0 && !h->prof && (bgv == nullptr || bgv[0] != '0');
   const int bs = block_size, sbs = small_block_size;
   std::vector<int> gen(prompt, prompt + prompt_len);
   const size_t n0 = gen.size();
@@ -292,6 +506,17 @@ extern "C" int fdllm_generate(fdllm_handle* h, const int32_t* prompt, int prompt
     }
     FDLLM_TRY(mark_prefill());  // the reference's prefill boundary (runtime.py:741-746)
     FDLLM_TRY(d.upload_block(x.data() + a0));
+    // A block that ends before max_new_tokens, with no stop token to watch, runs as one device-side
+    // graph: the refinement loops of all its sub-blocks and the block-append, one host sync.
+    if (use_block_graph && x.size() - n0 < static_cast<size_t>(max_new_tokens)) {
+      int nxt = 0;
+      FDLLM_TRY(d.run_block(x.data() + a0, &nxt));
+      gen = x;
+      d.prefix_len += bs;
+      kv_valid = false;
+      gen.push_back(nxt);
+      continue;
+    }
     bool length_done = false;
     for (int s0 = 0; s0 < bs && !length_done; s0 += sbs) {
       const int s1 = std::min(bs, s0 + sbs);
@@ -332,6 +557,8 @@ extern "C" int fdllm_generate(fdllm_handle* h, const int32_t* prompt, int prompt
 }
 
 void fdllm::release_step_graphs(fdllm_handle* h) {
+  if (h->dec.block_graph.exec) cudaGraphExecDestroy(h->dec.block_graph.exec);
+  h->dec.block_graph = BlockGraph{};
   for (auto& kv : h->dec.graphs) {
     if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
     for (auto& pp : kv.second.prof) {

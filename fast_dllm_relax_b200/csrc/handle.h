@@ -90,8 +90,21 @@ struct StepGraph {
   std::vector<ProfPair> prof;
 };
 
+// One captured decode block (see decode.cu): every refinement step of the block's sub-blocks run
+// by device-side WHILE / IF-ELSE graph nodes, then the block-append forward.
+struct BlockGraph {
+  cudaGraphExec_t exec = nullptr;
+  unsigned long long gen = 0;
+  int mask_id = 0;
+  double thr = 0.0;
+  int use_block_cache = 0, sbs = 0;
+  int n_full = 0, n_partial = 0, n_append = 0;  // kernels of one full / partial step and of the append
+};
+
 struct DecodeState {
   DevBuf<uint8_t> k, v;        // caches of the native driver
+  BlockGraph block_graph;      // the device-looped block (when the block fits its conditions)
+  DevBuf<int> loop;            // device loop state of the block graph
   DevBuf<int> ids;             // prefill / block token ids
   DevBuf<int> block;           // active block ids (bd_size)
   DevBuf<uint8_t> x, hid;      // embeddings in / hidden out

@@ -725,6 +725,7 @@ int fdllm_destroy(fdllm_handle* h) {
   for (cudaEvent_t e : h->prof_ev) cudaEventDestroy(e);
   release_step_graphs(h);
   h->dec.plen.release();
+  h->dec.loop.release();
   if (h->dec.stream) cudaStreamDestroy(h->dec.stream);
   delete h;
   return FDLLM_OK;
