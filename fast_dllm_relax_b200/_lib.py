@@ -65,6 +65,8 @@ SIGNATURES: dict[str, tuple] = {
     "fdllm_confidence_static": (_I, [_P, _P, _I, _P, _P, _P]),
     "fdllm_stack_trace_enable": (_I, [_P, _I]),
     "fdllm_stack_trace_read": (_I, [_P, _P, ctypes.c_longlong, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
+    "fdllm_kernel_trace_enable": (_I, [_P, _I]),
+    "fdllm_kernel_trace_read": (_I, [_P, _P, _P, _I, ctypes.POINTER(_I)]),
     "fdllm_unmask": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, ctypes.c_double, _P, _P, _P, _P, _P]),
     "fdllm_token_logprob": (_I, [_P, _P, _I, _P, _P, _P]),
     "fdllm_generate": (_I, [_P, _P, _I, _I, _I, _I, ctypes.c_double, _I, _I, _I, _P, ctypes.POINTER(_I), _P, _P, _P]),

@@ -54,6 +54,10 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False, e
     BUILD.mkdir(exist_ok=True)
     LIB_DIR.mkdir(exist_ok=True)
     extra = list(extra or [])
+    stamp = BUILD / "flags"  # objects built with other extra flags are rebuilt
+    key = " ".join(extra)
+    if not stamp.exists() or stamp.read_text() != key:
+        force = True
     hdr = _headers_mtime()
     todo, objs = [], []
     for name in SOURCES:
@@ -74,6 +78,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False, e
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stderr}")
         os.replace(tmp, LIB)
+    stamp.write_text(key)
     return LIB
 
 
@@ -83,8 +88,12 @@ def main() -> None:
     ap.add_argument("--jobs", type=int, default=None)
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-v", action="store_true", help="print register / spill / smem usage")
+    ap.add_argument("--ktrace", action="store_true",
+                    help="compile in the per-launch phase stamps of fdllm_kernel_trace_* (diagnostics; slower)")
     args = ap.parse_args()
     extra = ["-Xptxas", "-v"] if args.ptxas_v else []
+    if args.ktrace:
+        extra.append("-DFDLLM_KTRACE")
     print(build(force=args.force or args.ptxas_v, jobs=args.jobs, verbose=args.verbose or args.ptxas_v, extra=extra))
 
 

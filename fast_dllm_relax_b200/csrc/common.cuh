@@ -56,6 +56,24 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// Kernel trace: tr[2p] / tr[2p + 1] collect the earliest / latest %globaltimer value (ns) at which
+// any CTA of one launch reached phase p (kKtracePhases per launch; 0 entry, 1 dependency wait
+// passed, 2 main loop done, 7 exit, the others kernel-specific).  The host presets the minima to
+// all ones and the maxima to zero.  Compiled in only with FDLLM_KTRACE: even an untaken stamp
+// costs the decode step about 1.5% (registers and scheduling around the atomics).
+constexpr int kKtracePhases = 12;
+__device__ __forceinline__ void ktrace_stamp(unsigned long long* tr, int phase) {
+#ifdef FDLLM_KTRACE
+  if (tr == nullptr) return;
+  const unsigned long long t = global_timer_ns();
+  atomicMin(tr + 2 * phase, t);
+  atomicMax(tr + 2 * phase + 1, t);
+#else
+  (void)tr;
+  (void)phase;
+#endif
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -60,14 +60,85 @@ template <> __device__ __forceinline__ void set_pair<bf16>(bf16* dst, float a, f
 
 constexpr int kEpiBatch = 4;  // chunks in flight per thread
 
+// Epilogue inputs that do not depend on the accumulator, loaded before it is ready so that their
+// latency overlaps the main loop's tail and the split-K reduction.  Only when each thread owns at
+// most kEpiPre chunks (chunks cbeg + tid + b * nthr, b < kEpiPre); n = 0 otherwise.  One chunk
+// covers every decode-sized split-K tile and keeps the GEMM at its former register count: a GEMM
+// CTA must still fit beside an attention CTA on an SM for programmatic launch to overlap them.
+constexpr int kEpiPre = 1;
+template <typename T>
+struct EpiPre {
+  int n = 0;
+  Chunk<T> a[kEpiPre];                // residual: resid chunk; qkv: bias chunk
+  Chunk<T> b[kEpiPre];                // qkv: bias chunk of the RoPE partner features
+  Chunk<T> cs[kEpiPre], sn[kEpiPre];  // qkv: RoPE tables at the token's position
+  T* dst[kEpiPre];                    // qkv: q row, or the request's K / V cache row (null: none)
+};
+
+template <typename T>
+__device__ void epi_prefetch(const GemmArgs& g, int tok0, int slab, int row0, int row1, int tid, int nthr,
+                             EpiPre<T>& p) {
+  const Epilogue& e = g.epi;
+  constexpr int V = Chunk<T>::V;
+  constexpr int CPR = 128 / V;
+  const int cbeg = row0 * CPR, cend = row1 * CPR;
+  p.n = 0;
+  if (cend - cbeg > nthr * kEpiPre) return;
+  if (e.kind == kEpiResidual) {
+    const T* hs = e.resid_src ? static_cast<const T*>(e.resid_src) : static_cast<const T*>(e.resid);
+#pragma unroll
+    for (int b = 0; b < kEpiPre; ++b) {
+      const int c = cbeg + tid + b * nthr;
+      const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
+      if (c < cend && tok < g.M && F0 < g.N) p.a[b] = ld_chunk(hs + (size_t)tok * e.ld_resid + F0);
+    }
+    p.n = kEpiPre;
+  } else if (e.kind == kEpiQkvRope) {
+    const T* bias = static_cast<const T*>(e.bias);
+    const int hd = e.hd, half = e.hd >> 1;
+#pragma unroll
+    for (int b = 0; b < kEpiPre; ++b) {
+      p.dst[b] = nullptr;
+      const int c = cbeg + tid + b * nthr;
+      const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
+      if (c >= cend || tok >= g.M || F0 >= g.N) continue;
+      const int head = F0 / hd, d0 = F0 - head * hd;
+      p.a[b] = ld_chunk(bias + F0);
+      if (head < e.hq + e.hkv) {
+        int pos = e.tok.pos[tok];
+        pos = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // range checked in prepare
+        const bool lo = d0 < half;
+        p.b[b] = ld_chunk(bias + (lo ? F0 + half : F0 - half));
+        const size_t ti = (size_t)pos * half + (lo ? d0 : d0 - half);
+        p.cs[b] = ld_chunk(static_cast<const T*>(e.rope_cos) + ti);
+        p.sn[b] = ld_chunk(static_cast<const T*>(e.rope_sin) + ti);
+      }
+      if (head < e.hq) {
+        p.dst[b] = static_cast<T*>(e.qout) + (size_t)tok * (e.hq * hd) + F0;
+      } else {
+        const ReqDesc& r = e.reqs[e.tok.req[tok]];
+        const int row = e.tok.row[tok];
+        if (row >= 0 && row < r.cap) {
+          const size_t off = (size_t)e.layer * r.layer_stride + (size_t)row * e.hkv * hd;
+          p.dst[b] = head < e.hq + e.hkv ? static_cast<T*>(r.k) + off + (head - e.hq) * hd + d0
+                                         : static_cast<T*>(r.v) + off + (head - e.hq - e.hkv) * hd + d0;
+        }
+      }
+    }
+    p.n = kEpiPre;
+  }
+}
+
 // Rows [row0, row1) of the tile are processed (a split-K cluster member owns a share of the rows).
 // s_epi: 5120 bytes of shared scratch owned by the calling kernel.  The calling threads are
 // tid = 0..nthr-1 (a multiple of 32); they synchronise with named barrier `bar_id` (0 with
 // nthr == blockDim.x is __syncthreads()).
+// pre: inputs loaded by epi_prefetch for the same rows and threads, or null.
 template <typename T>
 __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, int slab, int row0, int row1,
-                              unsigned char* s_epi, int tid, int nthr, int bar_id) {
+                              unsigned char* s_epi, int tid, int nthr, int bar_id, const EpiPre<T>* pre = nullptr) {
   const Epilogue& e = g.epi;
+  const bool have_pre = pre != nullptr && pre->n > 0;
   constexpr int V = Chunk<T>::V;
   constexpr int CPR = 128 / V;  // chunks per 128-feature row of the tile
   const int cbeg = row0 * CPR, cend = row1 * CPR;
@@ -107,7 +178,13 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
         for (int b = 0; b < kEpiBatch; ++b) {  // loads first
           const int c = c0 + b * nthr;
           const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
-          if (c < cend && tok < g.M && F0 < g.N) r[b] = ld_chunk(hs + (size_t)tok * e.ld_resid + F0);
+          if (c < cend && tok < g.M && F0 < g.N) {
+            if (!have_pre) {
+              r[b] = ld_chunk(hs + (size_t)tok * e.ld_resid + F0);
+            } else if (b < kEpiPre) {  // prefetched (chunks past kEpiPre per thread do not exist then)
+              r[b] = pre->a[b < kEpiPre ? b : 0];
+            }
+          }
         }
 #pragma unroll
         for (int b = 0; b < kEpiBatch; ++b) {
@@ -161,6 +238,39 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
       break;
     }
     case kEpiQkvRope: {
+      if (have_pre) {  // one pass: the partner features' biased values are recomputed, no barrier
+        const int hd = e.hd, half = e.hd >> 1;
+#pragma unroll
+        for (int b = 0; b < kEpiPre; ++b) {
+          const int c = cbeg + tid + b * nthr;
+          const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
+          if (c >= cend || tok >= g.M || F0 >= g.N || pre->dst[b] == nullptr) continue;
+          const int head = F0 / hd, d0 = F0 - head * hd;
+          const float* x = acc + t * 128 + f0;
+          Chunk<T> o;
+          if (head < e.hq + e.hkv) {
+            const bool lo = d0 < half;
+            const float* xp = lo ? x + half : x - half;
+#pragma unroll
+            for (int v = 0; v < V; v += 2) {
+              const float2 y = round_pair<T>(x[v] + to_f<T>(pre->a[b].e[v]), x[v + 1] + to_f<T>(pre->a[b].e[v + 1]));
+              const float2 yp = round_pair<T>(xp[v] + to_f<T>(pre->b[b].e[v]), xp[v + 1] + to_f<T>(pre->b[b].e[v + 1]));
+              const float r0 = lo ? -yp.x : yp.x, r1 = lo ? -yp.y : yp.y;
+              const float2 cv = round_pair<T>(y.x * to_f<T>(pre->cs[b].e[v]), y.y * to_f<T>(pre->cs[b].e[v + 1]));
+              const float2 sv = round_pair<T>(r0 * to_f<T>(pre->sn[b].e[v]), r1 * to_f<T>(pre->sn[b].e[v + 1]));
+              set_pair<T>(&o.e[v], cv.x + sv.x, cv.y + sv.y);  // T(round(c + s)) == T(c + s)
+            }
+          } else {
+#pragma unroll
+            for (int v = 0; v < V; v += 2) {
+              const float2 y = round_pair<T>(x[v] + to_f<T>(pre->a[b].e[v]), x[v + 1] + to_f<T>(pre->a[b].e[v + 1]));
+              set_pair<T>(&o.e[v], y.x, y.y);
+            }
+          }
+          st_chunk(pre->dst[b], o);
+        }
+        break;
+      }
       // Per-token destinations (RoPE position, cache row, K / V bases) once per tile, in shared
       // memory, so the element loop below carries no dependent global loads.
       int* s_pos = reinterpret_cast<int*>(s_epi);                 // [256]

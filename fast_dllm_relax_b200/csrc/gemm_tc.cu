@@ -47,8 +47,10 @@ struct TcCfg {
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
 
+// At most 128 registers a thread (min 4 blocks): a CTA must fit beside a 192-thread attention CTA
+// of up to 256 registers a thread in one SM's 64K registers for programmatic launch to overlap them.
 template <int NT>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(128, 4)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmArgs g) {
   using C = TcCfg<NT>;
@@ -74,6 +76,7 @@ __global__ void __launch_bounds__(128, 1)
   const int nk = max(kb1 - kb0, 0);
 
   if (threadIdx.x == 0) {
+    ktrace_stamp(g.ktrace, 0);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&ready[s], 2);  // one arrival per normalizing warp
@@ -121,6 +124,7 @@ __global__ void __launch_bounds__(128, 1)
       load_a(i);
     }
     pdl_wait();
+    ktrace_stamp(g.ktrace, 1);
     for (int i = 0; i < pre; ++i) load_b(i);
     int issued = pre;
     for (int i = pre; i < nk; ++i) {
@@ -214,10 +218,6 @@ __global__ void __launch_bounds__(128, 1)
 
   // ---------------- epilogue: TMEM -> shared fp32 tile ----------------
   pdl_wait();  // every thread below reads or writes memory the previous kernel may still touch
-  if (!mbar_wait(accf, 0)) report_error(g.err, kErrTimeoutEpilogue);
-  tc_fence_after_sync();
-  __syncthreads();  // the producer's drain is complete before the ring is overwritten
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   // The accumulator is finished kChunk token columns at a time (the shared fp32 chunk reuses the
   // ring).  Split-K: the g.splits CTAs of one (slab, token tile) form one cluster; each keeps its
   // fp32 partial chunk in shared memory, member r sums rows [r*kChunk/S, (r+1)*kChunk/S) of the
@@ -226,6 +226,15 @@ __global__ void __launch_bounds__(128, 1)
   const uint32_t S = static_cast<uint32_t>(g.splits > 1 ? g.splits : 1);
   const uint32_t rank = g.splits > 1 ? cluster_ctarank() : 0u;
   const int lr0 = static_cast<int>(rank * C::kChunk / S), lr1 = static_cast<int>((rank + 1) * C::kChunk / S);
+  // One chunk (NT <= 64): this thread's epilogue inputs are loaded before the accumulator is ready.
+  EpiPre<bf16> pre;
+  if (NT <= 64 && (g.tune & kGemmTunePrefetch))
+    epi_prefetch<bf16>(g, tok0, slab, S > 1 ? lr0 : 0, S > 1 ? lr1 : NT, threadIdx.x, blockDim.x, pre);
+  if (!mbar_wait(accf, 0)) report_error(g.err, kErrTimeoutEpilogue);
+  if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 2);
+  tc_fence_after_sync();
+  __syncthreads();  // the producer's drain is complete before the ring is overwritten
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   int row0 = lr0, row1 = lr1;  // rows of the last chunk this CTA finished (the only chunk when NT <= 64)
   for (int ch = 0; ch < NT / C::kChunk; ++ch) {
     const int cb = ch * C::kChunk;
@@ -251,6 +260,7 @@ __global__ void __launch_bounds__(128, 1)
     if (ch == NT / C::kChunk - 1) {  // every column drained: free TMEM
       tc_fence_before_sync();
       __syncthreads();
+      if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 3);
       if (warp == 0) {
         tc_fence_after_sync();
         tmem_dealloc(tmem, C::kTmemCols);
@@ -282,13 +292,16 @@ __global__ void __launch_bounds__(128, 1)
         acc4[c] = sum;  // only this member reads or writes its own rows from here on
       }
       __syncthreads();
+      if (threadIdx.x == 0 && ch == NT / C::kChunk - 1) ktrace_stamp(g.ktrace, 4);
     }
     row0 = cb + lr0;
     row1 = cb + lr1;
     // acc holds token columns [cb, cb + kChunk); the epilogue indexes it as the whole tile
     gemm_epilogue<bf16>(g, acc - static_cast<size_t>(cb) * 128, NT, tok0, slab, S > 1 ? row0 : cb,
-                        S > 1 ? row1 : cb + C::kChunk, s_epi);
+                        S > 1 ? row1 : cb + C::kChunk, s_epi, static_cast<int>(threadIdx.x),
+                        static_cast<int>(blockDim.x), 0, NT <= 64 ? &pre : nullptr);
   }
+  if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 5);
   if (S > 1) cluster_sync();  // no member leaves while another may still read its shared memory
   if (S == 1) {
     row0 = 0;
@@ -314,6 +327,7 @@ __global__ void __launch_bounds__(128, 1)
       }
     }
     __syncthreads();
+    if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 6);
     if (s_last) {
       const int H = g.N;
       const int n_ss = g.epi.ss_ld;
@@ -363,6 +377,7 @@ __global__ void __launch_bounds__(128, 1)
       }
     }
   }
+  if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 7);
 }
 
 // ---- persistent variant for large token counts (M >= 256 rows, no split-K) ------------------------

@@ -161,6 +161,11 @@ struct fdllm_handle {
   bool stack_trace_on = false;            // fdllm_stack_trace_enable
   DevBuf<unsigned long long> stack_trace; // per-CTA phase timeline of the last layer-stack launch
   int stack_trace_grid = 0;
+  // kernel trace (fdllm_kernel_trace_enable / _read): phase stamps of every projection and
+  // attention launch issued outside stream capture while enabled, 8 per launch, and their kinds
+  bool ktrace_on = false;
+  DevBuf<unsigned long long> ktrace;
+  std::vector<int32_t> ktrace_kind;
   DecodeState dec;
 
   // per-launch CUDA-event timing of the projection GEMM (fdllm_profile_enable / _read)

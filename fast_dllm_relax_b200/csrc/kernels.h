@@ -77,6 +77,10 @@ struct Epilogue {
   const int* target;        // LseGather: [M] target ids
 };
 
+// GemmArgs::tune bits (decode-sized tiles, NT <= 64): load the epilogue's inputs before the
+// accumulator is ready.
+constexpr int kGemmTunePrefetch = 1;
+
 struct GemmArgs {
   int M, N, K;              // tokens, output features (weight rows), reduction
   int paired;               // gate/up pairing (N = 2*I; slab s covers rows [64s, 64s+64) and I + same)
@@ -102,6 +106,8 @@ struct GemmArgs {
   // arrival counters (zero between launches; the last split resets its tile's counter)
   float* ppart;
   unsigned* pctr;
+  unsigned long long* ktrace;  // phase stamps of this launch (kernel trace), or null
+  int tune;                 // kGemmTune* bits
   int* err;
   Epilogue epi;
 };
@@ -120,6 +126,7 @@ struct AttnArgs {
   int n_splits;             // key splits per (request, kv head, q tile) = cluster size
   int split_len;            // minimum keys per split (multiple of 64)
   int m_total;              // M: activation rows of all requests
+  unsigned long long* ktrace;  // phase stamps of this launch (kernel trace), or null
   int* err;
 };
 

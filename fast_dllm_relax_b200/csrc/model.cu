@@ -204,6 +204,25 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
   return nt;
 }
 
+// Kernel trace slot of the next launch (null when tracing is off, capturing, or full).
+constexpr size_t kKtraceMax = 8192;
+static unsigned long long* ktrace_slot(fdllm_handle* h, int kind) {
+  if (!h->ktrace_on || h->capturing || h->ktrace_kind.size() >= kKtraceMax) return nullptr;
+  const size_t i = h->ktrace_kind.size();
+  h->ktrace_kind.push_back(kind);
+  return h->ktrace.p + 2 * kKtracePhases * i;
+}
+
+// Minima preset to all ones, maxima to zero (the kernels atomically narrow them).
+static int ktrace_reset(fdllm_handle* h) {
+  h->ktrace_kind.clear();
+  FDLLM_TRY(h->ktrace.ensure(2 * kKtracePhases * kKtraceMax));
+  std::vector<unsigned long long> init(2 * kKtracePhases * kKtraceMax);
+  for (size_t i = 0; i < init.size(); ++i) init[i] = (i % 2 == 0) ? ~0ull : 0ull;
+  CUDA_TRY(cudaMemcpy(h->ktrace.p, init.data(), init.size() * sizeof(unsigned long long), cudaMemcpyHostToDevice));
+  return FDLLM_OK;
+}
+
 // norm_w set (tcgen05 path only): X is the un-normalized input and the kernel applies RMSNorm
 // with weight norm_w while building its B operand.
 static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epilogue epi, cudaStream_t s,
@@ -227,6 +246,12 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
     g.norm_eps = h->cfg.rms_norm_eps;
   }
   if (h->dtype == FDLLM_FLOAT32) return timed_launch(h, g, s, launch_simt_thunk, w.ptr, X, 0);
+  g.ktrace = ktrace_slot(h, 100 + epi.kind + (post_out ? 1000 : 0) + (norm_w ? 2000 : 0));
+  static const int tune = [] {  // tuning override of the kGemmTune* bits
+    const char* v = std::getenv("FDLLM_GEMM_TUNE");
+    return v != nullptr ? std::atoi(v) : kGemmTunePrefetch;
+  }();
+  g.tune = tune;
   if (norm_w == nullptr && post_out == nullptr && use_persist(h, M)) {
     g.n_slabs = w.paired ? (g.N / 2) / 64 : g.N / 128;
     // 256-token tiles when they cover half the SMs, else 128 (twice the tiles for few-slab weights)
@@ -549,6 +574,7 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     a.split_len = split_len;
     a.m_total = M;
     a.err = h->err.p;
+    a.ktrace = h->dtype == FDLLM_BFLOAT16 ? ktrace_slot(h, 1) : nullptr;
     CUDA_TRY(launch_attention(a, max_q, h->dtype, s));
 
     e = base;
@@ -719,6 +745,7 @@ int fdllm_destroy(fdllm_handle* h) {
   h->persist_part.release();
   h->persist_ctr.release();
   h->stack_trace.release();
+  h->ktrace.release();
   h->reqs.release();
   if (h->dec.host) cudaFreeHost(h->dec.host);
   if (h->dec.host_params) cudaFreeHost(h->dec.host_params);
@@ -1015,6 +1042,34 @@ int fdllm_stack_trace_read(fdllm_handle* h, uint64_t* out, long long cap, int32_
   CUDA_TRY(cudaDeviceSynchronize());
   CUDA_TRY(cudaMemcpy(out, h->stack_trace.p, static_cast<size_t>(n) * sizeof(uint64_t), cudaMemcpyDeviceToHost));
   return FDLLM_OK;
+}
+
+int fdllm_kernel_trace_enable(fdllm_handle* h, int enable) {
+  if (h == nullptr) return fail(FDLLM_ERR_INVALID, "null handle");
+#ifndef FDLLM_KTRACE
+  if (enable != 0) return fail(FDLLM_ERR_UNSUPPORTED, "kernel trace not compiled in (build with FDLLM_KTRACE=1)");
+#endif
+  std::lock_guard<std::mutex> lock(h->mu);
+  CUDA_TRY(cudaSetDevice(h->device));
+  CUDA_TRY(cudaDeviceSynchronize());
+  if (enable != 0) FDLLM_TRY(ktrace_reset(h));
+  h->ktrace_on = enable != 0;
+  return FDLLM_OK;
+}
+
+int fdllm_kernel_trace_read(fdllm_handle* h, uint64_t* out, int32_t* kinds, int cap, int32_t* n) {
+  if (h == nullptr || n == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
+  std::lock_guard<std::mutex> lock(h->mu);
+  const int cnt = static_cast<int>(h->ktrace_kind.size());
+  *n = cnt;
+  if (out == nullptr || cnt == 0) return FDLLM_OK;
+  if (cap < cnt || kinds == nullptr) return fail(FDLLM_ERR_INVALID, "trace buffer too small");
+  CUDA_TRY(cudaSetDevice(h->device));
+  CUDA_TRY(cudaDeviceSynchronize());
+  CUDA_TRY(cudaMemcpy(out, h->ktrace.p, static_cast<size_t>(cnt) * 2 * kKtracePhases * sizeof(uint64_t),
+                        cudaMemcpyDeviceToHost));
+  std::copy(h->ktrace_kind.begin(), h->ktrace_kind.end(), kinds);
+  return ktrace_reset(h);
 }
 
 long long fdllm_workspace_bytes(fdllm_handle* h) {

@@ -294,6 +294,23 @@ class Engine:
                                                        ctypes.byref(per)))
         return out
 
+    def kernel_trace_enable(self, enable: bool = True) -> None:
+        """Record per-launch phase stamps of later eager projection / attention launches
+        (diagnostics; clears the record)."""
+        _lib.check(self.lib.fdllm_kernel_trace_enable(self._h, int(bool(enable))))
+
+    def kernel_trace_read(self):
+        """(stamps uint64 ns [n, 12 phases, 2 (min, max)], kinds int32 [n]); clears the record."""
+        import numpy as np  # noqa: PLC0415
+        n = ctypes.c_int(0)
+        _lib.check(self.lib.fdllm_kernel_trace_read(self._h, None, None, 0, ctypes.byref(n)))
+        out = np.zeros((n.value, 12, 2), dtype=np.uint64)
+        kinds = np.zeros(n.value, dtype=np.int32)
+        if n.value:
+            _lib.check(self.lib.fdllm_kernel_trace_read(self._h, out.ctypes.data, kinds.ctypes.data, n.value,
+                                                        ctypes.byref(n)))
+        return out, kinds
+
     def workspace_bytes(self) -> int:
         return int(self.lib.fdllm_workspace_bytes(self._h))
 
