@@ -56,18 +56,18 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
-// Kernel trace: tr[2p] / tr[2p + 1] collect the earliest / latest %globaltimer value (ns) at which
-// any CTA of one launch reached phase p (kKtracePhases per launch; 0 entry, 1 dependency wait
-// passed, 2 main loop done, 7 exit, the others kernel-specific).  The host presets the minima to
-// all ones and the maxima to zero.  Compiled in only with FDLLM_KTRACE: even an untaken stamp
-// costs the decode step about 1.5% (registers and scheduling around the atomics).
+// Kernel trace: tr[cta * kKtracePhases + p] = the %globaltimer value (ns) at which CTA `cta` (linear
+// block index) of one launch reached phase p (0 entry, 1 dependency wait passed, 2 main loop done,
+// 7 exit, the others kernel-specific); 0 = not reached.  Plain stores to distinct words: atomics
+// on one per-launch word serialise in L2 and delay the stamping thread.  Compiled in only with
+// FDLLM_KTRACE: even an untaken stamp costs the decode step about 1.5%.
 constexpr int kKtracePhases = 12;
+constexpr int kKtraceMaxCta = 1280;  // CTAs of one launch recorded
 __device__ __forceinline__ void ktrace_stamp(unsigned long long* tr, int phase) {
 #ifdef FDLLM_KTRACE
   if (tr == nullptr) return;
-  const unsigned long long t = global_timer_ns();
-  atomicMin(tr + 2 * phase, t);
-  atomicMax(tr + 2 * phase + 1, t);
+  const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  if (cta < static_cast<unsigned>(kKtraceMaxCta)) tr[cta * kKtracePhases + phase] = global_timer_ns();
 #else
   (void)tr;
   (void)phase;

@@ -60,6 +60,29 @@ template <> __device__ __forceinline__ void set_pair<bf16>(bf16* dst, float a, f
 
 constexpr int kEpiBatch = 4;  // chunks in flight per thread
 
+// SiLU(g) = g * sigmoid(g) in fp32 (model/cuda.py:319-328).  bf16: the approximate exponential and
+// reciprocal (a few ulp of fp32, far below the bf16 rounding that follows) -- the IEEE division's
+// special-case branch serialises the independent element chains of a chunk.  fp32 keeps IEEE.
+template <typename T> __device__ __forceinline__ float silu_f(float g);
+template <> __device__ __forceinline__ float silu_f<float>(float g) { return g * (1.0f / (1.0f + expf(-g))); }
+template <> __device__ __forceinline__ float silu_f<bf16>(float g) { return g * __fdividef(1.0f, 1.0f + __expf(-g)); }
+
+// V consecutive fp32 accumulator values (16-byte aligned) with 16-byte shared-memory loads: the
+// chunk pattern of the epilogues (8 chunks of one token row per 8 lanes) costs a 2-way bank
+// conflict per 128-bit load instead of an 8-way conflict per scalar load.
+template <int V>
+__device__ __forceinline__ void ld_acc(const float* p, float (&x)[V]) {
+  static_assert(V % 4 == 0, "whole float4s");
+#pragma unroll
+  for (int i = 0; i < V / 4; ++i) {
+    const float4 q = reinterpret_cast<const float4*>(p)[i];
+    x[4 * i] = q.x;
+    x[4 * i + 1] = q.y;
+    x[4 * i + 2] = q.z;
+    x[4 * i + 3] = q.w;
+  }
+}
+
 // Epilogue inputs that do not depend on the accumulator, loaded before it is ready so that their
 // latency overlaps the main loop's tail and the split-K reduction.  Only when each thread owns at
 // most kEpiPre chunks (chunks cbeg + tid + b * nthr, b < kEpiPre); n = 0 otherwise.  One chunk
@@ -150,8 +173,10 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
         const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
         if (tok >= g.M || F0 >= g.N) continue;
         Chunk<T> o;
+        float x[V];
+        ld_acc<V>(acc + t * 128 + f0, x);
 #pragma unroll
-        for (int v = 0; v < V; v += 2) set_pair<T>(&o.e[v], acc[t * 128 + f0 + v], acc[t * 128 + f0 + v + 1]);
+        for (int v = 0; v < V; v += 2) set_pair<T>(&o.e[v], x[v], x[v + 1]);
         st_chunk(out + (size_t)tok * e.ld_out + F0, o);
       }
       break;
@@ -193,9 +218,11 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
           if (c >= cend || tok >= g.M || F0 >= g.N) continue;
           Chunk<T> o;
           float ss = 0.f;
+          float x[V];
+          ld_acc<V>(acc + t * 128 + f0, x);
 #pragma unroll
           for (int v = 0; v < V; v += 2) {
-            const float2 y = round_pair<T>(acc[t * 128 + f0 + v], acc[t * 128 + f0 + v + 1]);
+            const float2 y = round_pair<T>(x[v], x[v + 1]);
             const float2 z = round_pair<T>(to_f<T>(r[b].e[v]) + y.x, to_f<T>(r[b].e[v + 1]) + y.y);
             set_pair<T>(&o.e[v], z.x, z.y);
             ss = fmaf(z.x, z.x, ss);
@@ -225,12 +252,14 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
         const int t = c / CPH, f0 = (c % CPH) * V, tok = tok0 + t, j0 = slab * 64 + f0;
         if (tok >= g.M || j0 >= inter) continue;
         Chunk<T> o;
+        float gx[V], ux[V];
+        ld_acc<V>(acc + t * 128 + f0, gx);
+        ld_acc<V>(acc + t * 128 + 64 + f0, ux);
 #pragma unroll
         for (int v = 0; v < V; v += 2) {
-          const float2 gate = round_pair<T>(acc[t * 128 + f0 + v], acc[t * 128 + f0 + v + 1]);
-          const float2 up = round_pair<T>(acc[t * 128 + 64 + f0 + v], acc[t * 128 + 64 + f0 + v + 1]);
-          const float2 act = round_pair<T>(gate.x * (1.0f / (1.0f + expf(-gate.x))),
-                                           gate.y * (1.0f / (1.0f + expf(-gate.y))));
+          const float2 gate = round_pair<T>(gx[v], gx[v + 1]);
+          const float2 up = round_pair<T>(ux[v], ux[v + 1]);
+          const float2 act = round_pair<T>(silu_f<T>(gate.x), silu_f<T>(gate.y));
           set_pair<T>(&o.e[v], act.x * up.x, act.y * up.y);
         }
         st_chunk(out + (size_t)tok * e.ld_out + j0, o);
@@ -246,11 +275,13 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
           const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
           if (c >= cend || tok >= g.M || F0 >= g.N || pre->dst[b] == nullptr) continue;
           const int head = F0 / hd, d0 = F0 - head * hd;
-          const float* x = acc + t * 128 + f0;
+          float x[V];
+          ld_acc<V>(acc + t * 128 + f0, x);
           Chunk<T> o;
           if (head < e.hq + e.hkv) {
             const bool lo = d0 < half;
-            const float* xp = lo ? x + half : x - half;
+            float xp[V];
+            ld_acc<V>(acc + t * 128 + (lo ? f0 + half : f0 - half), xp);
 #pragma unroll
             for (int v = 0; v < V; v += 2) {
               const float2 y = round_pair<T>(x[v] + to_f<T>(pre->a[b].e[v]), x[v + 1] + to_f<T>(pre->a[b].e[v + 1]));

@@ -17,7 +17,7 @@ __global__ void __launch_bounds__(256) gemm_simt_f32_kernel(const float* __restr
                                                             const float* __restrict__ X, const GemmArgs g) {
   __shared__ float ws[kSimtK][128 + 1];
   __shared__ float xs[kSimtK][kSimtTok + 1];
-  __shared__ float acc[kSimtTok * 128];
+  __shared__ __align__(16) float acc[kSimtTok * 128];
   __shared__ __align__(16) unsigned char s_epi[5120];
   pdl_trigger();
   pdl_wait();

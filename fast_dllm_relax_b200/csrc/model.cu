@@ -204,22 +204,21 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
   return nt;
 }
 
-// Kernel trace slot of the next launch (null when tracing is off, capturing, or full).
-constexpr size_t kKtraceMax = 8192;
+// Kernel trace slot of the next launch (null when tracing is off, capturing, or full): one
+// [kKtraceMaxCta][kKtracePhases] record per launch, zeroed (= not reached) between reads.
+constexpr size_t kKtraceMax = 512;
+constexpr size_t kKtraceRec = static_cast<size_t>(kKtraceMaxCta) * kKtracePhases;
 static unsigned long long* ktrace_slot(fdllm_handle* h, int kind) {
   if (!h->ktrace_on || h->capturing || h->ktrace_kind.size() >= kKtraceMax) return nullptr;
   const size_t i = h->ktrace_kind.size();
   h->ktrace_kind.push_back(kind);
-  return h->ktrace.p + 2 * kKtracePhases * i;
+  return h->ktrace.p + kKtraceRec * i;
 }
 
-// Minima preset to all ones, maxima to zero (the kernels atomically narrow them).
 static int ktrace_reset(fdllm_handle* h) {
   h->ktrace_kind.clear();
-  FDLLM_TRY(h->ktrace.ensure(2 * kKtracePhases * kKtraceMax));
-  std::vector<unsigned long long> init(2 * kKtracePhases * kKtraceMax);
-  for (size_t i = 0; i < init.size(); ++i) init[i] = (i % 2 == 0) ? ~0ull : 0ull;
-  CUDA_TRY(cudaMemcpy(h->ktrace.p, init.data(), init.size() * sizeof(unsigned long long), cudaMemcpyHostToDevice));
+  FDLLM_TRY(h->ktrace.ensure(kKtraceRec * kKtraceMax));
+  CUDA_TRY(cudaMemset(h->ktrace.p, 0, kKtraceRec * kKtraceMax * sizeof(unsigned long long)));
   return FDLLM_OK;
 }
 
@@ -1066,8 +1065,21 @@ int fdllm_kernel_trace_read(fdllm_handle* h, uint64_t* out, int32_t* kinds, int 
   if (cap < cnt || kinds == nullptr) return fail(FDLLM_ERR_INVALID, "trace buffer too small");
   CUDA_TRY(cudaSetDevice(h->device));
   CUDA_TRY(cudaDeviceSynchronize());
-  CUDA_TRY(cudaMemcpy(out, h->ktrace.p, static_cast<size_t>(cnt) * 2 * kKtracePhases * sizeof(uint64_t),
-                        cudaMemcpyDeviceToHost));
+  std::vector<unsigned long long> rec(kKtraceRec * static_cast<size_t>(cnt));
+  CUDA_TRY(cudaMemcpy(rec.data(), h->ktrace.p, rec.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+  for (int i = 0; i < cnt; ++i) {  // earliest and latest stamp of each phase over the launch's CTAs
+    for (int p = 0; p < kKtracePhases; ++p) {
+      unsigned long long lo = ~0ull, hi = 0;
+      for (int c = 0; c < kKtraceMaxCta; ++c) {
+        const unsigned long long t = rec[kKtraceRec * i + static_cast<size_t>(c) * kKtracePhases + p];
+        if (t == 0) continue;
+        lo = std::min(lo, t);
+        hi = std::max(hi, t);
+      }
+      out[(static_cast<size_t>(i) * kKtracePhases + p) * 2] = lo;
+      out[(static_cast<size_t>(i) * kKtracePhases + p) * 2 + 1] = hi;
+    }
+  }
   std::copy(h->ktrace_kind.begin(), h->ktrace_kind.end(), kinds);
   return ktrace_reset(h);
 }

@@ -189,12 +189,12 @@ FDLLM_API int fdllm_stack_trace_read(fdllm_handle* h, uint64_t* out, long long c
  * out[24*i + 2p + 1] for launch i and p = 0..11 (UINT64_MAX / 0: not reached; the large-tile
  * persistent GEMM records nothing).  Phases: 0 entry, 1 dependency wait passed, 2 main loop done,
  * 7 exit; projection 3 accumulator drained from TMEM, 4 split-K partials summed, 5 epilogue done,
- * 6 post-norm arrival counted; attention 3 partials published, 4 merge weights, 5 merge done;
- * 8-11 unused.  The stamps are compiled in only by `python -m fast_dllm_relax_b200.build --ktrace`
+ * 6 post-norm arrival counted, 8 TMEM released; attention 3 partials published, 4 merge weights,
+ * 5 merge done; 9-11 unused.  The stamps are compiled in only by `python -m fast_dllm_relax_b200.build --ktrace`
  * (they slow every launch); otherwise enabling returns FDLLM_ERR_UNSUPPORTED.
  * kinds[i]: 1 attention; 100 + epilogue kind for a projection, +1000 with the post-norm, +2000
- * with the fused input norm.  Enabling, and every read, clears the record; at most 8192
- * launches are kept.  Both calls synchronise the device.  With out == NULL only *n is written. */
+ * with the fused input norm.  Enabling, and every read, clears the record; at most 512
+ * launches (1280 CTAs each) are kept.  Both calls synchronise the device.  With out == NULL only *n is written. */
 FDLLM_API int fdllm_kernel_trace_enable(fdllm_handle* h, int enable);
 FDLLM_API int fdllm_kernel_trace_read(fdllm_handle* h, uint64_t* out, int32_t* kinds, int cap, int32_t* n);
 
