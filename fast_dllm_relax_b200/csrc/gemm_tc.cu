@@ -25,6 +25,28 @@
 
 namespace fdllm {
 
+// Sum of a row's n per-slab statistics in slab order with every load in flight at once (a
+// load-add loop waits for each load; L2 round trips are the cost of these short phases).
+// kL2: L2-only loads, for statistics that other CTAs of the same launch wrote; otherwise plain
+// loads (written by an earlier launch), which one L1 line fill serves for several rows.
+constexpr int kMaxRowSs = 20;  // hidden <= 2560 (the fused norms' limit)
+template <bool kL2>
+__device__ __forceinline__ float sum_row_ss(const float* p, int n) {
+  if (n > kMaxRowSs) {
+    float ss = 0.f;
+    for (int j = 0; j < n; ++j) ss += kL2 ? __ldcg(p + j) : p[j];
+    return ss;
+  }
+  float v[kMaxRowSs];
+#pragma unroll
+  for (int j = 0; j < kMaxRowSs; ++j) v[j] = j < n ? (kL2 ? __ldcg(p + j) : p[j]) : 0.f;
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kMaxRowSs; ++j)
+    if (j < n) ss += v[j];
+  return ss;
+}
+
 template <int NT>
 struct TcCfg {
   static constexpr int kA = 128 * 64 * 2;  // weight tile: 128 rows x 64 bf16
@@ -158,13 +180,20 @@ __global__ void __launch_bounds__(128, 4)
     pdl_wait();
     const int nrow = min(NT, g.M - tok0);
     for (int t = wt; t < nrow; t += 64) {
-      const float* ssr = g.norm_ss + static_cast<size_t>(tok0 + t) * g.norm_ss_ld;
-      float ss = 0.f;
-      for (int j = 0; j < g.norm_ss_ld; ++j) ss += ssr[j];
+      const float ss = sum_row_ss<false>(g.norm_ss + static_cast<size_t>(tok0 + t) * g.norm_ss_ld, g.norm_ss_ld);
       rs[t] = rsqrtf(ss / static_cast<float>(g.K) + g.norm_eps);
     }
-    const uint4* wsrc = static_cast<const uint4*>(g.norm_w);
-    for (int c = wt; c < g.K / 8; c += 64) reinterpret_cast<uint4*>(s_w)[c] = wsrc[c];
+    {  // norm weights to shared memory, every load in flight at once (K <= 2560: 5 chunks a thread)
+      constexpr int kWPer = 5;
+      const uint4* wsrc = static_cast<const uint4*>(g.norm_w);
+      uint4 wr[kWPer];
+#pragma unroll
+      for (int i = 0; i < kWPer; ++i)
+        if (wt + 64 * i < g.K / 8) wr[i] = wsrc[wt + 64 * i];
+#pragma unroll
+      for (int i = 0; i < kWPer; ++i)
+        if (wt + 64 * i < g.K / 8) reinterpret_cast<uint4*>(s_w)[wt + 64 * i] = wr[i];
+    }
     asm volatile("bar.sync 1, 64;" ::: "memory");  // the two normalizing warps only
     const int cc = wt & 7;  // 16-byte chunk (8 columns) of the 64-column k-block this thread handles
     for (int i = 0; i < nk; ++i) {
@@ -264,6 +293,7 @@ __global__ void __launch_bounds__(128, 4)
       if (warp == 0) {
         tc_fence_after_sync();
         tmem_dealloc(tmem, C::kTmemCols);
+        if (lane == 0) ktrace_stamp(g.ktrace, 8);
       }
     } else {
       __syncthreads();
@@ -337,9 +367,7 @@ __global__ void __launch_bounds__(128, 4)
       float* rs = reinterpret_cast<float*>(s_epi);  // rows of this group
       for (int t = row0 + threadIdx.x; t < row1; t += blockDim.x) {
         const int tok = tok0 + t;
-        float ss = 0.f;
-        if (tok < g.M)
-          for (int j = 0; j < n_ss; ++j) ss += __ldcg(g.epi.ss_out + static_cast<size_t>(tok) * n_ss + j);
+        const float ss = tok < g.M ? sum_row_ss<true>(g.epi.ss_out + static_cast<size_t>(tok) * n_ss, n_ss) : 0.f;
         rs[t - row0] = rsqrtf(ss / static_cast<float>(H) + g.norm_eps);
       }
       __syncthreads();
