@@ -38,6 +38,15 @@ __device__ __forceinline__ Chunk<T> ld_chunk(const T* p) {
   return c;
 }
 
+// Read-only-path load (ld.global.nc) for tables that no kernel writes (bias, RoPE): the chunks
+// that several tokens share stay in L1.
+template <typename T>
+__device__ __forceinline__ Chunk<T> ld_const_chunk(const T* p) {
+  Chunk<T> c;
+  c.u = __ldg(reinterpret_cast<const uint4*>(p));
+  return c;
+}
+
 template <typename T>
 __device__ __forceinline__ void st_chunk(T* p, const Chunk<T>& c) {
   *reinterpret_cast<uint4*>(p) = c.u;
@@ -126,15 +135,15 @@ __device__ void epi_prefetch(const GemmArgs& g, int tok0, int slab, int row0, in
       const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
       if (c >= cend || tok >= g.M || F0 >= g.N) continue;
       const int head = F0 / hd, d0 = F0 - head * hd;
-      p.a[b] = ld_chunk(bias + F0);
+      p.a[b] = ld_const_chunk(bias + F0);
       if (head < e.hq + e.hkv) {
         int pos = e.tok.pos[tok];
         pos = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // range checked in prepare
         const bool lo = d0 < half;
-        p.b[b] = ld_chunk(bias + (lo ? F0 + half : F0 - half));
+        p.b[b] = ld_const_chunk(bias + (lo ? F0 + half : F0 - half));
         const size_t ti = (size_t)pos * half + (lo ? d0 : d0 - half);
-        p.cs[b] = ld_chunk(static_cast<const T*>(e.rope_cos) + ti);
-        p.sn[b] = ld_chunk(static_cast<const T*>(e.rope_sin) + ti);
+        p.cs[b] = ld_const_chunk(static_cast<const T*>(e.rope_cos) + ti);
+        p.sn[b] = ld_const_chunk(static_cast<const T*>(e.rope_sin) + ti);
       }
       if (head < e.hq) {
         p.dst[b] = static_cast<T*>(e.qout) + (size_t)tok * (e.hq * hd) + F0;
@@ -354,8 +363,8 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
           const int head = F0 / hd, d0 = F0 - head * hd;
           if (head < hq + hkv) {
             const size_t ti = (size_t)s_pos[t] * half + (d0 < half ? d0 : d0 - half);
-            cs[b] = ld_chunk(cos_t + ti);
-            sn[b] = ld_chunk(sin_t + ti);
+            cs[b] = ld_const_chunk(cos_t + ti);
+            sn[b] = ld_const_chunk(sin_t + ti);
           }
         }
 #pragma unroll
