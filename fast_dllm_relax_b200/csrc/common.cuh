@@ -196,6 +196,13 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
 
 // 2D tiled load of box (c0 = inner/contiguous coordinate, c1 = row) into shared memory; completion
 // is signalled as transaction bytes on `bar`.
+// L2 prefetch of one tile of a tensor map (no shared memory, no completion to wait for).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             uint64_t policy) {
   asm volatile(

@@ -139,12 +139,24 @@ __global__ void __launch_bounds__(128, 4)
       const int s = i % C::kStages;
       tma_load_2d(sB + s * C::kB, &tmB, &full[s], (kb0 + i) * 64, tok0, pol_x);
     };
+    const int l2_ahead = (g.tune >> kGemmTuneL2Shift) & 0xff;
+    auto prefetch_a = [&](int i) {  // k block i of the weights into L2
+      if (i >= nk) return;
+      const int k0 = (kb0 + i) * 64;
+      if (g.paired) {
+        tma_prefetch_l2_2d(&tmA, k0, slab * 64);
+        tma_prefetch_l2_2d(&tmA, k0, g.N / 2 + slab * 64);
+      } else {
+        tma_prefetch_l2_2d(&tmA, k0, slab * 128);
+      }
+    };
     // Weights do not depend on the previous kernel: fill the ring with them before waiting for it.
     const int pre = min(nk, C::kStages);
     for (int i = 0; i < pre; ++i) {
       mbar_arrive_expect_tx(&full[i], C::kStage);  // A + B bytes; the B half lands after the wait
       load_a(i);
     }
+    for (int i = pre; i < pre + l2_ahead; ++i) prefetch_a(i);  // and a few more into L2
     pdl_wait();
     ktrace_stamp(g.ktrace, 1);
     for (int i = 0; i < pre; ++i) load_b(i);
@@ -159,6 +171,7 @@ __global__ void __launch_bounds__(128, 4)
       mbar_arrive_expect_tx(&full[s], C::kStage);
       load_a(i);
       load_b(i);
+      prefetch_a(i + l2_ahead);
       ++issued;
     }
     // Drain: every copy this thread issued must have landed before shared memory is reused.

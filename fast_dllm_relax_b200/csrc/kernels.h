@@ -78,8 +78,10 @@ struct Epilogue {
 };
 
 // GemmArgs::tune bits (decode-sized tiles, NT <= 64): load the epilogue's inputs before the
-// accumulator is ready.
+// accumulator is ready; bits 8-15: weight k blocks prefetched into L2 ahead of the shared-memory
+// ring (more bytes in flight per SM than the ring holds).
 constexpr int kGemmTunePrefetch = 1;
+constexpr int kGemmTuneL2Shift = 8;
 
 struct GemmArgs {
   int M, N, K;              // tokens, output features (weight rows), reduction

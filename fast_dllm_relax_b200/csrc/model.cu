@@ -248,7 +248,9 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
   g.ktrace = ktrace_slot(h, 100 + epi.kind + (post_out ? 1000 : 0) + (norm_w ? 2000 : 0));
   static const int tune = [] {  // tuning override of the kGemmTune* bits
     const char* v = std::getenv("FDLLM_GEMM_TUNE");
-    return v != nullptr ? std::atoi(v) : kGemmTunePrefetch;
+    // default: epilogue prefetch, 2 weight k blocks into L2 ahead of the ring (measured per 32-row
+    // step: 2 -1.3 %; 4 / 8 / 16 slower, their traffic delays the latency-bound kernels before them)
+    return v != nullptr ? std::atoi(v) : (kGemmTunePrefetch | (2 << kGemmTuneL2Shift));
   }();
   g.tune = tune;
   if (norm_w == nullptr && post_out == nullptr && use_persist(h, M)) {
