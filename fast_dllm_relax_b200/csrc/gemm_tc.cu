@@ -385,10 +385,11 @@ __global__ void __launch_bounds__(128, 4)
       }
       __syncthreads();
       const int cpr = H / 8;
-      for (int c0 = threadIdx.x; c0 < (row1 - row0) * cpr; c0 += blockDim.x * 4) {
-        uint4 xv[4], wv[4];
+      constexpr int kPB = 5;  // chunks per thread and batch: one batch for 3 rows of 1536 features
+      for (int c0 = threadIdx.x; c0 < (row1 - row0) * cpr; c0 += blockDim.x * kPB) {
+        uint4 xv[kPB], wv[kPB];
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {  // loads first
+        for (int b = 0; b < kPB; ++b) {  // loads first
           const int c = c0 + b * blockDim.x;
           const int t = row0 + c / cpr, col = (c % cpr) * 8;
           if (c < (row1 - row0) * cpr && tok0 + t < g.M) {
@@ -397,7 +398,7 @@ __global__ void __launch_bounds__(128, 4)
           }
         }
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
+        for (int b = 0; b < kPB; ++b) {
           const int c = c0 + b * blockDim.x;
           const int t = row0 + c / cpr, col = (c % cpr) * 8;
           if (c >= (row1 - row0) * cpr || tok0 + t >= g.M) continue;
