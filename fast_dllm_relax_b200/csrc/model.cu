@@ -296,7 +296,11 @@ static void plan_attention(const fdllm_handle* h, int max_q, int max_l, int nreq
   *n_splits = 1;
   *split_len = std::max(64, static_cast<int>(round_up(std::max(max_l, 1), 64)));
   if (h->dtype == FDLLM_BFLOAT16 && !dense && base_ctas < h->num_sms) {
-    int want = std::min({(2 * h->num_sms + base_ctas - 1) / base_ctas, (max_l + 63) / 64, kMaxAttnSplits});
+    // as many splits as keep the grid within one CTA per SM: a second wave, or two CTAs per SM
+    // merging through distributed shared memory, costs more than the longer key loop (measured
+    // per layer: 32 requests x 768 keys 32 µs unsplit vs 47 µs with 3 splits; 8 x 4096 keys 44 µs
+    // with 4 splits vs 59 µs with 8)
+    int want = std::min({h->num_sms / base_ctas, (max_l + 63) / 64, kMaxAttnSplits});
     const char* ev = std::getenv("FDLLM_ATTN_SPLITS");  // tuning override
     if (ev != nullptr && std::atoi(ev) > 0) want = std::min(std::atoi(ev), kMaxAttnSplits);
     if (want > 1) {
