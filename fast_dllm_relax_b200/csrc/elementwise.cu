@@ -189,28 +189,67 @@ __device__ __forceinline__ Top warp_merge(Top t) {
   return t;
 }
 
-// Partials from the fused lm_head epilogue: [rows, n_slabs, 4] = (max, argmax bits, sum, target).
-__global__ void conf_combine_kernel(const float* __restrict__ part, int rows, int n_slabs, int* ids, float* maxp) {
+// Partials from the fused lm_head epilogue: [rows, n_slabs, 4] = (max, argmax bits, sum exp,
+// target logit).  One CTA per row: each thread merges the slabs tid + 256 j with every load of a
+// batch in flight first (a one-warp loop over 37 slabs serialised a memory round trip and two
+// exponentials per slab), the warps merge by shuffles and thread 0 merges the warps' results in
+// warp order -- a fixed order, so the result is deterministic.
+constexpr int kTopThreads = 256;
+constexpr int kTopPer = 8;  // slabs per thread and batch (vocab 151936: 1187 slabs, one batch)
+
+template <bool kLse>
+__global__ void __launch_bounds__(kTopThreads) top_combine_kernel(const float* __restrict__ part, int n_slabs,
+                                                                  int* ids, float* maxp, float* logprob) {
   pdl_trigger();
   pdl_wait();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (row >= rows) return;
+  const int row = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float4* p4 = reinterpret_cast<const float4*>(part) + static_cast<size_t>(row) * n_slabs;
   Top t{-INFINITY, 0x7fffffff, 0.f};
-  for (int sl = lane; sl < n_slabs; sl += 32) {
-    const float* p = part + (static_cast<size_t>(row) * n_slabs + sl) * 4;
-    t = merge_top(t, Top{p[0], __float_as_int(p[1]), p[2]});
+  float tgt = 0.f;  // exactly one slab holds the target's logit, the others hold 0
+  for (int s0 = tid; s0 < n_slabs; s0 += kTopThreads * kTopPer) {
+    float4 v[kTopPer];
+#pragma unroll
+    for (int j = 0; j < kTopPer; ++j)
+      if (s0 + j * kTopThreads < n_slabs) v[j] = p4[s0 + j * kTopThreads];
+#pragma unroll
+    for (int j = 0; j < kTopPer; ++j) {
+      if (s0 + j * kTopThreads >= n_slabs) continue;
+      t = merge_top(t, Top{v[j].x, __float_as_int(v[j].y), v[j].z});
+      if (kLse) tgt += v[j].w;
+    }
   }
   t = warp_merge(t);
+  if (kLse) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) tgt += __shfl_xor_sync(0xffffffffu, tgt, off);
+  }
+  __shared__ Top s_t[kTopThreads / 32];
+  __shared__ float s_g[kTopThreads / 32];
   if (lane == 0) {
-    ids[row] = t.i;
-    maxp[row] = 1.0f / t.s;
+    s_t[warp] = t;
+    s_g[warp] = tgt;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    Top r = s_t[0];
+    float g = s_g[0];
+    for (int w = 1; w < kTopThreads / 32; ++w) {
+      r = merge_top(r, s_t[w]);
+      g += s_g[w];
+    }
+    if (kLse) {
+      logprob[row] = g - (r.m + logf(r.s));
+    } else {
+      ids[row] = r.i;
+      maxp[row] = 1.0f / r.s;
+    }
   }
 }
 
 int launch_conf_combine(const float* part, int rows, int n_slabs, int* ids, float* maxp, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  return launch_k(conf_combine_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, part, rows, n_slabs, ids, maxp);
+  return launch_k(top_combine_kernel<false>, dim3(rows), dim3(kTopThreads), 0, s, part, n_slabs, ids, maxp,
+                  static_cast<float*>(nullptr));
 }
 
 // The same reduction over materialised fp32 logits [rows, vocab] (three passes per row).
@@ -260,28 +299,10 @@ int launch_conf_from_logits(const float* logits, int rows, int vocab, int* ids, 
 }
 
 // log_softmax(logits)[target] per row from the fused partials (runners.py:877-881 on the device).
-__global__ void lse_combine_kernel(const float* __restrict__ part, int rows, int n_slabs, float* logprob) {
-  pdl_trigger();
-  pdl_wait();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (row >= rows) return;
-  Top t{-INFINITY, 0x7fffffff, 0.f};
-  float tgt = 0.f;
-  for (int sl = lane; sl < n_slabs; sl += 32) {
-    const float* p = part + (static_cast<size_t>(row) * n_slabs + sl) * 4;
-    t = merge_top(t, Top{p[0], __float_as_int(p[1]), p[2]});
-    tgt += p[3];  // exactly one slab holds the target's logit, the others hold 0
-  }
-  t = warp_merge(t);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) tgt += __shfl_xor_sync(0xffffffffu, tgt, off);
-  if (lane == 0) logprob[row] = tgt - (t.m + logf(t.s));
-}
-
 int launch_lse_combine(const float* part, int rows, int n_slabs, float* logprob, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  return launch_k(lse_combine_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, part, rows, n_slabs, logprob);
+  return launch_k(top_combine_kernel<true>, dim3(rows), dim3(kTopThreads), 0, s, part, n_slabs,
+                  static_cast<int*>(nullptr), static_cast<float*>(nullptr), logprob);
 }
 
 // ---- unmask decision (runtime.py:158-181 shift, 794-805 rule), one warp ------------------------
