@@ -85,9 +85,69 @@ __global__ void rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w,
   }
 }
 
+// bf16 rows of hidden % 8 == 0 features (<= 8192): 16-byte chunks held in registers between the
+// statistics and the normalisation, so each row is read once and every load of a thread is in
+// flight at once.
+constexpr int kNormChunks = 4;  // chunks per thread (256 threads x 4 x 8 = 8192 features)
+__global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                               bf16* __restrict__ out, int hidden, float eps,
+                                                               bf16* __restrict__ copy_to) {
+  __shared__ float red[32];
+  pdl_trigger();
+  pdl_wait();
+  const int nch = hidden / 8;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(blockIdx.x) * hidden);
+  uint4 xv[kNormChunks];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNormChunks; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < nch) xv[k] = xr[c];
+  }
+#pragma unroll
+  for (int k = 0; k < kNormChunks; ++k) {
+    if (threadIdx.x + k * blockDim.x >= nch) continue;
+    const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv[k]);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const float2 f = __bfloat1622float2(x2[v]);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+    }
+  }
+  const float rs = rsqrtf(block_sum(ss, red) / static_cast<float>(hidden) + eps);
+  uint4* orow = reinterpret_cast<uint4*>(out + static_cast<size_t>(blockIdx.x) * hidden);
+  uint4* crow = copy_to ? reinterpret_cast<uint4*>(copy_to + static_cast<size_t>(blockIdx.x) * hidden) : nullptr;
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+#pragma unroll
+  for (int k = 0; k < kNormChunks; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c >= nch) continue;
+    const uint4 wv = __ldg(w4 + c);
+    const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv[k]);
+    const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const float2 f = __bfloat1622float2(x2[v]);
+      const float2 xn = round2_bf16(f.x * rs, f.y * rs);
+      const float2 wf = __bfloat1622float2(w2[v]);
+      o2[v] = __floats2bfloat162_rn(wf.x * xn.x, wf.y * xn.y);
+    }
+    orow[c] = o;
+    if (crow) crow[c] = xv[k];  // the residual stream starts as a copy of the input
+  }
+}
+
 int launch_rmsnorm(const void* x, const void* w, void* out, int rows, int hidden, float eps, int dtype,
                    cudaStream_t s, void* copy_x_to) {
   if (rows <= 0) return cudaSuccess;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (dtype == 1 && hidden % 8 == 0 && hidden <= 8 * 256 * kNormChunks && a16(x) && a16(w) && a16(out) &&
+      a16(copy_x_to))
+    return launch_k(rmsnorm_bf16_vec_kernel, dim3(rows), dim3(256), 0, s, static_cast<const bf16*>(x),
+                    static_cast<const bf16*>(w), static_cast<bf16*>(out), hidden, eps, static_cast<bf16*>(copy_x_to));
   if (dtype == 1)
     return launch_k(rmsnorm_kernel<bf16>, dim3(rows), dim3(256), 0, s, static_cast<const bf16*>(x),
                     static_cast<const bf16*>(w), static_cast<bf16*>(out), hidden, eps, static_cast<bf16*>(copy_x_to));
