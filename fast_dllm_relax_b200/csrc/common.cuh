@@ -150,6 +150,15 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// cluster_sync in two halves (every thread calls arrive, then wait, alternately); the work between
+// them overlaps the barrier.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // The address of the same shared-memory location in cluster member `rank`.
 __device__ __forceinline__ uint32_t map_shared_rank(uint32_t addr, uint32_t rank) {
   uint32_t r;

@@ -336,6 +336,9 @@ __global__ void __launch_bounds__(128, 4)
       }
       __syncthreads();
       if (threadIdx.x == 0 && ch == NT / C::kChunk - 1) ktrace_stamp(g.ktrace, 4);
+      // Last chunk: this member's reads of its peers' partials are done.  Arrive now and wait
+      // only before leaving, so the closing barrier overlaps the epilogue.
+      if (ch == NT / C::kChunk - 1) cluster_arrive();
     }
     row0 = cb + lr0;
     row1 = cb + lr1;
@@ -345,7 +348,6 @@ __global__ void __launch_bounds__(128, 4)
                         static_cast<int>(blockDim.x), 0, NT <= 64 ? &pre : nullptr);
   }
   if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 5);
-  if (S > 1) cluster_sync();  // no member leaves while another may still read its shared memory
   if (S == 1) {
     row0 = 0;
     row1 = NT;
@@ -419,6 +421,7 @@ __global__ void __launch_bounds__(128, 4)
       }
     }
   }
+  if (S > 1) cluster_wait();  // no member leaves while another may still read its shared memory
   if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 7);
 }
 
