@@ -60,6 +60,7 @@ SIGNATURES: dict[str, tuple] = {
     "fdllm_build_prefix_cache": (_I, [_P, _P, _P, _I, _P, _P, _I, _P]),
     "fdllm_forward_cached": (_I, [_P, _P, _I, _P, _P, _I, _P, _I, _I, _I, _P, _P]),
     "fdllm_forward_cached_batch": (_I, [_P, ctypes.POINTER(FdllmRequest), _I, _P, _P, _P]),
+    "fdllm_build_prefix_cache_batch": (_I, [_P, ctypes.POINTER(FdllmRequest), _I, _P, _P]),
     "fdllm_confidence": (_I, [_P, _P, _I, _P, _P, _P]),
     "fdllm_confidence_from_logits": (_I, [_P, _P, _I, _P, _P, _P]),
     "fdllm_confidence_static": (_I, [_P, _P, _I, _P, _P, _P]),

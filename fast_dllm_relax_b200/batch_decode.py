@@ -11,7 +11,8 @@ needs next; the scheduler gathers the pending work of all requests and runs it t
 * every cached step of every request that needs one (full 32-row refinements, 8-row partial
   refinements, block appends, in any mix) is ONE batched forward (fdllm_forward_cached_batch)
   plus ONE fused lm_head + confidence launch over all rows;
-* prefix-cache builds run per request (the implicit block-causal mask, no O(P^2) bias);
+* every pending prefix-cache build is ONE batched forward (fdllm_build_prefix_cache_batch, the
+  implicit block-causal mask inside each request, no O(P^2) bias);
 * the unmask decision (runtime.py:158-181 shift, 794-805 rule) runs on the host from the
   per-row (argmax, max-probability) pairs, 8 bytes per row read back per step.
 
@@ -207,24 +208,26 @@ def generate_batch(engine: Engine, prompts: Sequence[Sequence[int]], *, max_new_
     for i in range(len(progs)):
         advance(i, None)
     while pending:
-        # prefix-cache builds and stateless dense forwards: one request at a time
-        for i in [i for i, op in pending.items() if op[0] != "step"]:
-            op = pending[i]
-            if op[0] == "prefill":
-                _, cache, ids = op
-                if timing is not None:
-                    ev.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
-                    ev[-1][0].record()
-                x = engine.embed(torch.tensor(ids, dtype=torch.int32, device=dev))[None]
-                engine.build_prefix_cache(x, None, cache.k, cache.v)
-                if timing is not None:
-                    ev[-1][1].record()
+        # every pending prefix-cache build in one forward (fdllm_build_prefix_cache_batch: the
+        # block-causal mask inside each request, runtime.py:718-739 per request)
+        pre = [i for i, op in pending.items() if op[0] == "prefill"]
+        if pre:
+            if timing is not None:
+                ev.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+                ev[-1][0].record()
+            ids_all = torch.tensor([t for i in pre for t in pending[i][2]], dtype=torch.int32, device=dev)
+            engine.build_prefix_cache_batch(engine.embed(ids_all), [(pending[i][1].k, pending[i][1].v) for i in pre],
+                                            [len(pending[i][2]) for i in pre])
+            if timing is not None:
+                ev[-1][1].record()
+            for i in pre:
                 advance(i, None)
-            else:
-                _, seq = op
-                x = engine.embed(torch.tensor(seq, dtype=torch.int32, device=dev))[None]
-                hidden = engine.forward_hidden(x, None)
-                advance(i, engine.get_logits(hidden)[0].float().cpu().numpy())
+        # stateless dense forwards (the first block of short prompts): one request at a time
+        for i in [i for i, op in pending.items() if op[0] == "dense"]:
+            _, seq = pending[i]
+            x = engine.embed(torch.tensor(seq, dtype=torch.int32, device=dev))[None]
+            hidden = engine.forward_hidden(x, None)
+            advance(i, engine.get_logits(hidden)[0].float().cpu().numpy())
         steps = [(i, op) for i, op in pending.items() if op[0] == "step"]
         if not steps:
             continue

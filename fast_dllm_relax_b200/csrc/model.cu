@@ -879,6 +879,38 @@ int fdllm_build_prefix_cache(fdllm_handle* h, const void* x, const float* bias, 
   return dense_forward(h, x, bias, P, k, v, cap, false, nullptr, static_cast<cudaStream_t>(stream));
 }
 
+int fdllm_build_prefix_cache_batch(fdllm_handle* h, const fdllm_request* reqs_host, int n, const void* x,
+                                   void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (n <= 0 || reqs_host == nullptr || x == nullptr) return fail(FDLLM_ERR_INVALID, "bad prefix batch arguments");
+  std::vector<ReqDesc> reqs(n);
+  int tok = 0;
+  for (int i = 0; i < n; ++i) {
+    const fdllm_request& q = reqs_host[i];
+    if (q.rows <= 0 || q.k_cache == nullptr || q.v_cache == nullptr)
+      return fail(FDLLM_ERR_INVALID, "prefix request " + std::to_string(i) + ": bad rows or cache");
+    if (q.rows > q.cap)
+      return fail(FDLLM_ERR_INVALID, "prefix request " + std::to_string(i) + ": KV write [0, " + std::to_string(q.rows) +
+                                         ") outside cache capacity " + std::to_string(q.cap));
+    if (q.rows > h->cfg.max_positions) return fail(FDLLM_ERR_INVALID, "prefix longer than max_positions");
+    ReqDesc d{};
+    d.k = q.k_cache;
+    d.v = q.v_cache;
+    d.layer_stride = layer_stride(h, q.cap);
+    d.cap = q.cap;
+    d.q_tok0 = tok;
+    d.n_q = q.rows;
+    d.write_start = 0;
+    d.attend_len = q.rows;
+    d.rope_base = 0;
+    d.rope_off = nullptr;
+    reqs[i] = d;
+    tok += q.rows;
+  }
+  std::lock_guard<std::mutex> lock(h->mu);
+  return forward_core(h, x, tok, reqs, nullptr, 0, h->cfg.bd_size, nullptr, static_cast<cudaStream_t>(stream));
+}
+
 int fdllm_forward_cached(fdllm_handle* h, const void* x, int rows, void* k, void* v, int cap,
                          const int32_t* cache_offset_dev, int prefix_len, int write_rel, int attend_rel, void* out,
                          void* stream) {

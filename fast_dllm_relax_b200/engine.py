@@ -154,6 +154,20 @@ class Engine:
                                    attend_rel=self.cfg.bd_size)
 
     # ---- batched / fused extensions ----------------------------------------------------------
+    def build_prefix_cache_batch(self, x: torch.Tensor, caches: Sequence[tuple[torch.Tensor, torch.Tensor]],
+                                 rows: Sequence[int]) -> None:
+        """build_prefix_cache of several requests in one forward: x [sum(rows), hidden], request i's
+        prefix is the next rows[i] rows, written to caches[i] = (k, v) rows [0, rows[i])."""
+        x2 = self._act(x, "build_prefix_cache_batch")
+        if len(caches) != len(rows) or not rows:
+            raise ValueError("one (k, v) cache per request")
+        if sum(int(r) for r in rows) != x2.shape[0]:
+            raise ValueError(f"requests cover {sum(rows)} rows, x has {x2.shape[0]}")
+        arr = (_lib.FdllmRequest * len(rows))()
+        for i, ((k, v), r) in enumerate(zip(caches, rows)):
+            arr[i] = _lib.FdllmRequest(k.data_ptr(), v.data_ptr(), self._cache(k, v), int(r), 0, 0, int(r), 0, None)
+        _lib.check(self.lib.fdllm_build_prefix_cache_batch(self._h, arr, len(rows), x2.data_ptr(), self._stream()))
+
     def forward_cached_batch(self, x: torch.Tensor, requests: Sequence[dict]) -> torch.Tensor:
         """x: [sum(rows), hidden]; each request: dict(k, v, rows, prefix_len, write_rel=0,
         attend_rel=rows, cache_offset=int or device int32 tensor)."""

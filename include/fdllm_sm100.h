@@ -100,6 +100,14 @@ FDLLM_API int fdllm_get_logits(fdllm_handle* h, const void* hidden, int rows, fl
 FDLLM_API int fdllm_build_prefix_cache(fdllm_handle* h, const void* x, const float* bias, int P, void* k_cache,
                              void* v_cache, int cap, void* stream);
 
+/* fdllm_build_prefix_cache for n requests in one forward (no counterpart in the reference, which
+ * builds one prefix per call): request i's prefix is rows [sum(rows[<i]), + rows[i]) of x, under
+ * the implicit block-causal mask (block = bd_size) within the request, written to its own cache
+ * rows [0, rows[i]).  Only k_cache, v_cache, cap and rows of each descriptor are read.  Results
+ * match n single calls up to the bf16 rounding of the larger GEMM tiles. */
+FDLLM_API int fdllm_build_prefix_cache_batch(fdllm_handle* h, const fdllm_request* reqs, int n, const void* x,
+                                             void* stream);
+
 /* vm["forward_cached"] (write_rel 0, attend_rel rows) and vm["forward_block_partial_rp{0,8,16,24}"]
  * (write_rel = rp, attend_rel = bd_size) -- model/cuda.py:723-788, 639-666; callback semantics
  * runtime.py:63-73.  cache_offset_dev is the reference's 0-d int32 device tensor, prefix_len its

@@ -101,6 +101,25 @@ def test_batched_requests_match_single(mid, n_req, prefix):
     assert eng.device_error() == 0
 
 
+def test_batched_prefix_build_matches_single(mid):
+    """fdllm_build_prefix_cache_batch == one build_prefix_cache per request (ragged prefixes, the
+    block-causal mask inside each request), up to the bf16 rounding of the larger GEMM tiles."""
+    eng, _ = mid
+    lens = [96, 160, 64, 224]
+    xs = [_act(P, 300 + i).to(_dev()) for i, P in enumerate(lens)]
+    batched = [eng.new_cache(P + 32) for P in lens]
+    single = [eng.new_cache(P + 32) for P in lens]
+    eng.build_prefix_cache_batch(torch.cat([x[0] for x in xs]), batched, lens)
+    for x, (k, v) in zip(xs, single):
+        eng.build_prefix_cache(x, None, k, v)
+    for i, (P, (kb, vb), (ks, vs)) in enumerate(zip(lens, batched, single)):
+        for a, b, name in ((kb, ks, "k"), (vb, vs, "v")):
+            a, b = a[:, :, :P].float().cpu(), b[:, :, :P].float().cpu()
+            torch.testing.assert_close(a, b, rtol=2e-2, atol=4e-2, msg=lambda m: f"request {i} {name}: {m}")
+            assert ((a - b).abs() > 2e-2 + 2e-2 * b.abs()).float().mean() < 1e-3, f"request {i} {name}"
+    assert eng.device_error() == 0
+
+
 def test_masked_continuation_scoring(mid):
     """context 512, continuation 16 in a masked 32-row block (eos at row 16, pad
     masks after), log-softmax gathered on the device, batch 4."""
