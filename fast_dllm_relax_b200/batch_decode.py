@@ -47,16 +47,19 @@ class _Cache:
 #   ("step", cache, ids, write_rel, attend_rel)  -> (ids int64[rows], maxp float32[rows]), unshifted
 #   ("dense", seq_ids)                           -> float32 logits [len(seq_ids), vocab] (stateless path)
 
-def _shift(ids: np.ndarray, maxp: np.ndarray):
+def _shifted(vals, row: int):
     """runtime.py:169-174: row i takes row i-1's prediction, row 0 its own."""
-    return np.concatenate([ids[:1], ids[:-1]]), np.concatenate([maxp[:1], maxp[:-1]])
+    return vals[row - 1] if row > 0 else vals[0]
 
 
-def _unmask_rows(masked: list[int], prob: np.ndarray, threshold: float) -> list[int]:
-    """runtime.py:796-805: masked rows above the threshold, else the first most confident one."""
-    rows = [r for r in masked if float(prob[r]) > threshold]
+def _unmask_rows(masked: list[int], prob, threshold: float) -> list[int]:
+    """runtime.py:796-805: masked rows above the threshold, else the first most confident one.
+    `prob(r)` is the shifted confidence of window row r."""
+    conf = [prob(r) for r in masked]
+    rows = [r for r, c in zip(masked, conf) if c > threshold]
     if not rows:
-        rows = [masked[int(np.argmax([float(prob[r]) for r in masked]))]]
+        best = max(range(len(conf)), key=lambda j: (conf[j], -j))  # first index on ties, as argmax
+        rows = [masked[best]]
     return rows
 
 
@@ -125,19 +128,18 @@ def request_program(engine: Engine, prompt_ids: Sequence[int], *, max_new_tokens
                     return continuation(x)
                 if use_cache:
                     partial = use_block_cache and kv_valid and x[a0 + s0] != mask_id
-                    if partial:
+                    if partial:  # the step's rows are the window itself
                         ids, maxp = yield ("step", cache, x[a0 + s0:a0 + s1], s0, bs)
-                        tok, prob = _shift(ids, maxp)
-                    else:
+                        base = 0
+                    else:  # the step's rows are the whole block; the window starts at row s0
                         ids, maxp = yield ("step", cache, x[a0:], 0, bs)
-                        tok, prob = _shift(ids, maxp)
-                        tok, prob = tok[s0:s1], prob[s0:s1]
+                        base = s0
                         kv_valid = use_block_cache
                     stats["block_recomputes"] += 1
                     stats["partial_recomputes"] += int(partial)
-                    rows = _unmask_rows(masked, prob, threshold)
+                    rows = _unmask_rows(masked, lambda r: float(_shifted(maxp, base + r)), threshold)
                     for r in rows:
-                        x[a0 + s0 + r] = int(tok[r])
+                        x[a0 + s0 + r] = int(_shifted(ids, base + r))
                     stats["unmask_updates"] += len(rows)
                 else:  # stateless first block (runtime.py:806-837): dense forward over the sequence
                     logits = yield ("dense", x)
@@ -241,7 +243,8 @@ def generate_batch(engine: Engine, prompts: Sequence[Sequence[int]], *, max_new_
                              attend_rel=attend_rel))
         hidden = engine.forward_cached_batch(x, reqs)
         cid, cmax = engine.confidence(hidden)
-        cid, cmax = cid.cpu().numpy().astype(np.int64), cmax.cpu().numpy()
+        both = torch.cat([cid.view(torch.float32), cmax]).cpu().numpy()  # one device-to-host copy
+        cid, cmax = both[:len(cid)].view(np.int32).astype(np.int64), both[len(cid):]
         o = 0
         for i, op in steps:
             rows = len(op[2])
