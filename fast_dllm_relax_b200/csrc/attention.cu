@@ -7,8 +7,8 @@
 //
 // bf16: one CTA per (request, 16-token query tile, KV head, key split).  The 16 tokens x G query
 // heads that share a KV head form 16*G query rows, one m16 tile per warp, so each K/V byte staged in
-// shared memory serves all G heads.  K/V tiles of 64 keys are double-buffered with cp.async into a
-// XOR-swizzled layout and read with ldmatrix; QK^T and PV run on mma.sync m16n8k16 (bf16 in,
+// shared memory serves all G heads.  K/V tiles of 64 keys stream through a ring of three with
+// cp.async into a XOR-swizzled layout and are read with ldmatrix; QK^T and PV run on mma.sync m16n8k16 (bf16 in,
 // fp32 accumulate) with an online (flash) softmax in registers and quad shuffles for the row
 // reductions.  Long key ranges are split across the CTAs of a thread-block cluster, which merge
 // their partial outputs by log-sum-exp through distributed shared memory.
@@ -22,6 +22,8 @@ namespace fdllm {
 
 constexpr int kQT = 16;  // query tokens per CTA
 constexpr int kKT = 64;  // keys per shared-memory tile
+constexpr int kKV = 3;   // K/V tile ring depth: two tiles in flight while one is computed
+static_assert(kKV == 3, "the tail waits of the tile loop are written for a ring of three");
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -66,8 +68,8 @@ __global__ void __launch_bounds__(192, MINB) attn_mma_kernel(const AttnArgs a) {
   constexpr int kChunks = HD / 8;          // 16-byte chunks per key row
   constexpr int kTileBytes = kKT * HD * 2;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* Ks = smem;                      // [2][kKT][HD]
-  uint8_t* Vs = smem + 2 * kTileBytes;     // [2][kKT][HD]
+  uint8_t* Ks = smem;                        // [kKV][kKT][HD]
+  uint8_t* Vs = smem + kKV * kTileBytes;     // [kKV][kKT][HD]
 
   const int G = a.hq / a.hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -134,11 +136,14 @@ __global__ void __launch_bounds__(192, MINB) attn_mma_kernel(const AttnArgs a) {
     cp_async_commit();
   };
 
-  if (n_tiles > 0) load_tile(0, 0);
+  for (int p = 0; p < kKV - 1 && p < n_tiles; ++p) load_tile(p, p);
   for (int it = 0; it < n_tiles; ++it) {
-    const int buf = it & 1;
-    if (it + 1 < n_tiles) {
-      load_tile(it + 1, buf ^ 1);
+    const int buf = it % kKV;
+    // tile it must have landed: the groups still pending may only be the later tiles issued
+    if (it + kKV - 1 < n_tiles) {
+      load_tile(it + kKV - 1, (it + kKV - 1) % kKV);  // into the buffer tile it-1 used
+      cp_async_wait<kKV - 1>();
+    } else if (it + 1 < n_tiles) {
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
@@ -371,7 +376,7 @@ __global__ void attn_simt_kernel(const AttnArgs a) {
 template <int HD>
 static int launch_mma(const AttnArgs& a, int max_q, cudaStream_t s) {
   const int G = a.hq / a.hkv;
-  constexpr int smem = 4 * kKT * HD * 2;
+  constexpr int smem = 2 * kKV * kKT * HD * 2;
   cudaError_t e;
   dim3 grid((max_q + kQT - 1) / kQT, a.hkv, a.n_reqs * a.n_splits);
   int dev = 0, sms = 148;
@@ -388,7 +393,8 @@ int init_gemm_tc_attributes();
 
 template <int HD, int MINB>
 static cudaError_t attn_attrs() {
-  cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<HD, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * kKT * HD * 2);
+  cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<HD, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       2 * kKV * kKT * HD * 2);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_mma_kernel<HD, MINB>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   return e;
 }
