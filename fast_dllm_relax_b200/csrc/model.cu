@@ -525,23 +525,21 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
   // their B tiles in place, with row statistics left by the previous down projection); large calls
   // normalize once in a separate kernel.
   const bool fuse_norm = h->dtype == FDLLM_BFLOAT16 && M <= 64 && c.hidden_size <= 2560;
-  // The post-attention RMSNorm folds into gate_up for 8/16-row calls (partial steps); at 32 rows its
-  // per-stage normalisation outlasts the weight tile it waits for, so a separate kernel runs it.
-  // FDLLM_FUSE_GU_NORM=0/1 overrides.
-  // post-attention RMSNorm: "post" = the o projection's last CTAs normalise each finished row
-  // group (no separate kernel, gate_up reads the result); "fused" = gate_up normalises its B tiles
-  // (fastest for <= 16 rows, where a stage's normalisation is short); "kernel" = a separate rmsnorm
-  // kernel.  FDLLM_GU_NORM overrides the choice.
+  // post-attention RMSNorm: "fused" = gate_up normalises its B tiles (fastest for <= 16 rows, where
+  // a stage's normalisation is short); "kernel" = a separate rmsnorm kernel (fastest above: at 32
+  // rows 1.41 ms per step vs 1.46 for "post" and 1.52 for "fused"); "post" = the o projection's
+  // last CTAs normalise each finished row group.  FDLLM_GU_NORM overrides the choice.
   const char* gn = std::getenv("FDLLM_GU_NORM");
   const std::string gu_norm =
-      gn != nullptr ? std::string(gn) : std::string(!fuse_norm ? "kernel" : (M <= 16 ? "fused" : "post"));
+      gn != nullptr ? std::string(gn) : std::string(!fuse_norm ? "kernel" : (M <= 16 ? "fused" : "kernel"));
   const bool fuse_norm_gu = fuse_norm && gu_norm == "fused";
   const bool post_norm_gu = fuse_norm && gu_norm == "post" && M <= 64;
   // The next layer's input RMSNorm (and the final norm): "fused" = the qkv projection normalises
   // its B tiles with the statistics the down projection left; "post" = the down projection's last
-  // CTAs write the normalised rows (FDLLM_QKV_NORM overrides).
+  // CTAs write the normalised rows; "kernel" = a separate rmsnorm kernel (FDLLM_QKV_NORM overrides).
   const char* qn = std::getenv("FDLLM_QKV_NORM");
   const bool post_norm_qkv = fuse_norm && M <= 64 && qn != nullptr && std::string(qn) == "post";
+  const bool kernel_norm_qkv = qn != nullptr && std::string(qn) == "kernel";
 
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const LayerW& L = h->layers[l];
@@ -553,7 +551,7 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     e.qout = h->q.p;
     if (post_norm_qkv && l > 0) {  // the previous down projection wrote the normalised input
       FDLLM_TRY(run_gemm(h, L.qkv, h->xn.p, M, e, s));
-    } else if (fuse_norm && l > 0) {  // layer 0's input has no producer epilogue: normalized separately
+    } else if (fuse_norm && l > 0 && !kernel_norm_qkv) {  // layer 0's input has no producer epilogue
       FDLLM_TRY(run_gemm(h, L.qkv, layer_in, M, e, s, L.ln1));
     } else {
       // layer 0 reads the input embeddings and starts the residual stream h as their copy
