@@ -148,6 +148,14 @@ def cpu_baseline_sample(params_cpu, steps: int = 2) -> dict:
             "ms_per_step": ms}
 
 
+def workload_config(world: int, block_cache: bool) -> dict:
+    """The `config` object both arms print (same workload, same keys)."""
+    return {"workload": "BASELINE configs[1]: Fast-dLLM v2 1.5B bf16, batch 1 per GPU, prompt 256, "
+                        "generate 256, block 32, sub-block 8, threshold 0.9",
+            "use_block_cache": bool(block_cache), "parallelism": f"dp{world} (requests)",
+            "l2": "inputs larger than L2: 3.09 GB of weights streamed per step"}
+
+
 def run_reference(args) -> None:
     """--impl reference: the oracle port on the host cores (the reference's own stack, TVM Relax +
     the checkpoint's remote code, cannot run here), rank 0 only."""
@@ -175,8 +183,14 @@ def run_reference(args) -> None:
     v = (torch.randn(shape, generator=g) * 0.5).to(torch.bfloat16)
     ids = torch.randint(0, 151000, (BLOCK,), generator=g)
 
+    # use_block_cache=True refines with 8-row partial steps (write_rel 8, attend the full block)
+    rows = 8 if args.block_cache else BLOCK
+
     def one():
-        h = orc.forward_cached(orc.embed(ids)[None], k, v, PROMPT_LEN, PROMPT_LEN)
+        if rows == BLOCK:
+            h = orc.forward_cached(orc.embed(ids)[None], k, v, PROMPT_LEN, PROMPT_LEN)
+        else:
+            h = orc.forward_block_partial(orc.embed(ids[8:16])[None], k, v, PROMPT_LEN + 8, PROMPT_LEN, 8)
         confidence(orc.get_logits(h)[0])
 
     for _ in range(warm):
@@ -191,10 +205,10 @@ def run_reference(args) -> None:
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
         "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "BASELINE configs[1]: 1.5B bf16, batch 1, prompt 256, generate 256, block 32/8, thr 0.9",
-                   "sample": "one full refinement step per bench step (1 token committed per step)"},
+        "config": workload_config(world, args.block_cache),
+        "sample": f"one {rows}-row refinement step per bench step (1 token committed per step)",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": f"{steps} full 32-row refinement steps at prefix 256 on the host cores; "
+                         "sample": f"{steps} {rows}-row refinement steps at prefix 256 on the host cores; "
                                    "oracle/ is the PyTorch CPU restatement of the reference graph "
                                    "(TVM Relax cannot be installed here)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -304,12 +318,9 @@ def main() -> None:
             "metric": METRIC, "value": tokens / (dec_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": tot_ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random N(0,0.02) weights, uniform prompts)",
-            "config": {"workload": "BASELINE configs[1]: Fast-dLLM v2 1.5B bf16, batch 1 per GPU, prompt 256, "
-                                   "generate 256, block 32, sub-block 8, threshold 0.9",
-                       "use_block_cache": bool(args.block_cache), "parallelism": f"dp{world} (requests)",
-                       "l2": "inputs larger than L2: 3.09 GB of weights streamed per step",
-                       "tokens_per_generation": tokens / max(1, args.steps * world),
-                       "refinement_forwards_per_generation": steps_per_gen},
+            "config": workload_config(world, args.block_cache),
+            "tokens_per_generation": tokens / max(1, args.steps * world),
+            "refinement_forwards_per_generation": steps_per_gen,
             "ms_per_block_step": blk["full_ms"], "ms_per_partial_step": blk["partial_ms"],
             "prefill_ms": (tot_ms - dec_ms) / args.steps,
             "e2e": {"value": e2e_tokens / e2e_dec_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
