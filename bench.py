@@ -16,6 +16,9 @@ inside the native driver (the max over ranks).  e2e: the same metric through the
 (Engine.generate: host prompt in, host tokens out, per-step host reads) on the host clock.
 roofline: the projection GEMM (tcgen05) -- algorithmic bytes (weights + activations + outputs) per
 launch over its CUDA-event duration, against the measured HBM copy bandwidth.
+step_roofline: one whole 32-row (and 8-row partial) refinement step at prefix 384 -- the slower of
+(weights + KV bytes) / HBM and FLOPs / bf16 tensor peak, over the step's CUDA-event time, against
+the measured peaks and the nominal 8 TB/s and 2.25 PFLOP/s.
 """
 
 from __future__ import annotations
@@ -42,6 +45,34 @@ def _peaks() -> tuple[float, str]:
     if p.exists():
         return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def _tensor_peak() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+# 1.5B bf16 algorithmic units of one refinement step (weights incl. biases and norms, tied lm_head)
+STEP_WEIGHT_BYTES = 3_087_428_608
+STEP_MACS_PER_ROW = 1_543_569_408
+KV_BYTES_PER_KEY = 28 * 2 * 2 * 128 * 2  # layers x (K, V) x kv heads x head_dim x bf16
+
+
+def step_roofline(rows: int, prefix: int, ms: float, hbm_gbs: float, tensor_tflops: float) -> dict:
+    """Whole-step roofline of one refinement forward of `rows` query rows attending prefix + 32 keys:
+    the slower of (weights + KV reads + KV writes) / HBM and FLOPs / bf16 tensor peak, over the
+    measured step time."""
+    keys = prefix + BLOCK
+    nbytes = STEP_WEIGHT_BYTES + KV_BYTES_PER_KEY * keys + KV_BYTES_PER_KEY * rows
+    flops = 2 * rows * STEP_MACS_PER_ROW + 28 * 12 * 4 * 128 * rows * keys
+    out = {"rows": rows, "prefix": prefix, "bytes": nbytes, "flops": flops, "ms": ms}
+    for tag, bw, tf in (("measured", hbm_gbs, tensor_tflops), ("nominal", 8000.0, 2250.0)):
+        floor_ms = max(nbytes / (bw * 1e9), flops / (tf * 1e12)) * 1e3
+        out[tag] = {"hbm_gbs": bw, "bf16_tflops": tf, "floor_ms": floor_ms,
+                    "frac": floor_ms / ms if ms > 0 else None}
+    return out
 
 
 def _traffic() -> dict | None:
@@ -332,6 +363,10 @@ def main() -> None:
                          "algorithmic_bytes_per_launch": prof["bytes"] / max(1, prof["launches"]),
                          "avg_launch_us": 1e3 * prof["ms"] / max(1, prof["launches"]),
                          "launches": prof["launches"]},
+            "step_roofline": {
+                "full": step_roofline(BLOCK, 384, blk["full_ms"], peak, _tensor_peak()[0]),
+                "partial": step_roofline(SUB_BLOCK, 384, blk["partial_ms"], peak, _tensor_peak()[0]),
+                "bound": "hbm", "peak_kind": f"{peak_kind} / nominal 8 TB/s, 2.25 PFLOP/s"},
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
         }
