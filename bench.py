@@ -330,12 +330,22 @@ def main() -> None:
         w = time.perf_counter() - w0
         e2e_tokens += len(toks)
         e2e_dec_s += w - t["prefill_ms"] / 1e3
+    # the other use_block_cache setting, device-timed the same way (the reference evaluates with
+    # use_block_cache=True, scripts/eval.sh:50; the headline keeps BASELINE's default)
+    alt_kw = dict(gen_kw, use_block_cache=not args.block_cache)
+    eng.generate(prompt, **alt_kw)  # captures that setting's step graphs
+    alt_tokens, alt_dec_ms = 0, 0.0
+    for _ in range(args.steps):
+        t = {}
+        toks, _ = eng.generate(prompt, timing=t, **alt_kw)
+        alt_tokens += len(toks)
+        alt_dec_ms += t["total_ms"] - t["prefill_ms"]
     # ms per 32-token block step (embed + forward_cached(32) + fused confidence + unmask) at P = 384
     blk = block_step_ms(eng, torch, dev)
 
     # off the decode path: max over ranks of the device-timed durations, sum of the work
-    (dec_ms, tot_ms, e2e_dec_s), (tokens, launches, e2e_tokens) = dp.reduce_max_sum(
-        [dec_ms, tot_ms, e2e_dec_s], [tokens, launches, e2e_tokens], device=dev)
+    (dec_ms, tot_ms, e2e_dec_s, alt_dec_ms), (tokens, launches, e2e_tokens, alt_tokens) = dp.reduce_max_sum(
+        [dec_ms, tot_ms, e2e_dec_s, alt_dec_ms], [tokens, launches, e2e_tokens, alt_tokens], device=dev)
 
     if rank == 0:
         peak, peak_kind = _peaks()
@@ -353,6 +363,10 @@ def main() -> None:
             "tokens_per_generation": tokens / max(1, args.steps * world),
             "refinement_forwards_per_generation": steps_per_gen,
             "ms_per_block_step": blk["full_ms"], "ms_per_partial_step": blk["partial_ms"],
+            "ms_per_append_step": blk["append_ms"],
+            "other_block_cache_setting": {"use_block_cache": not args.block_cache,
+                                          "value": alt_tokens / (alt_dec_ms / 1e3) if alt_dec_ms > 0 else None,
+                                          "unit": UNIT},
             "prefill_ms": (tot_ms - dec_ms) / args.steps,
             "e2e": {"value": e2e_tokens / e2e_dec_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "path": "Engine.generate -> fdllm_generate (host buffers)"},
@@ -380,7 +394,8 @@ def main() -> None:
 
 
 def block_step_ms(eng, torch, dev, iters: int = 20) -> dict:
-    """CUDA-event time of one full refinement step and one rp8 partial step at P = 384."""
+    """CUDA-event time of one full refinement step, one rp8 partial step and one block append
+    (the 32-row cached forward alone) at P = 384."""
     from fast_dllm_relax_b200.config import QWEN_MASK_ID
     P = 384
     k, v = eng.new_cache(P + BLOCK)
@@ -400,8 +415,11 @@ def block_step_ms(eng, torch, dev, iters: int = 20) -> dict:
         i, m = eng.confidence(h)
         eng.unmask(i, m, block.clone(), 8, 8, True, QWEN_MASK_ID, THRESHOLD)
 
+    def append():  # the committed block written into the cache (runtime.py's block append)
+        eng.forward_cached(eng.embed(ids)[None], k, v, P, P)
+
     out = {}
-    for name, fn in (("full_ms", full), ("partial_ms", partial)):
+    for name, fn in (("full_ms", full), ("partial_ms", partial), ("append_ms", append)):
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
