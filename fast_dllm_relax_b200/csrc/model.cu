@@ -184,11 +184,14 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
   const int kblocks = g->K / 64;
   const int tiles = g->n_slabs * g->n_tok_tiles;
   int splits = 1;
-  static const int target = [] {  // tuning override: CTAs per SM the split-K plan aims for
+  // CTAs per SM the split-K plan aims for: 2 at <= 16 token rows (the 8-row partial step: 1.348 ->
+  // 1.329 ms at prefix 384; 32 rows unchanged, 3 or 4 slower at both), else 1.
+  static const int target_override = [] {  // tuning override
     const char* v = std::getenv("FDLLM_SPLIT_TARGET");
-    const int x = v ? std::atoi(v) : 1;
-    return x >= 1 && x <= 4 ? x : 1;
+    const int x = v ? std::atoi(v) : 0;
+    return x >= 1 && x <= 4 ? x : 0;
   }();
+  const int target = target_override > 0 ? target_override : (M <= 16 ? 2 : 1);
   static const int split_max = [] {  // tuning override: largest split-K cluster
     const char* v = std::getenv("FDLLM_SPLIT_MAX");
     const int x = v ? std::atoi(v) : 16;
