@@ -52,3 +52,19 @@ class LoggingOracle:
     def forward_block_partial(self, x, k, v, off, plen, rp):
         self.calls.append([f"forward_block_partial_rp{rp}", int(x.shape[1]), int(off), int(plen)])
         return self.m.forward_block_partial(x, k, v, off, plen, rp)
+
+
+def score_choices(model, g, mask_id: int) -> list[tuple]:
+    """Score the multiple-choice plan recorded in tiny_choices.npz in order with the oracle's
+    restatement of runtime.score_masked_continuation, each call handed the (aligned prefix, cache)
+    pair the previous call returned (runtime.py:546-548).  Returns (logits, continuation, cache)
+    per choice."""
+    from oracle import decode as od
+
+    out, cached = [], None
+    for i in range(int(g["n_choices"])):
+        ctx, cont = g[f"choice{i}/context"].tolist(), g[f"choice{i}/continuation"].tolist()
+        logits, cached = od.score_masked_continuation(model, ctx, cont, block_size=32, mask_id=mask_id,
+                                                      eos_token_id=1022, cached_prefix=cached)
+        out.append((logits, cont, cached[1]))
+    return out

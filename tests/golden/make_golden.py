@@ -13,7 +13,9 @@ step statistics and the exact sequence of entry-point calls -- so that tests can
 decode restatement (oracle/decode.py) and the product's drivers against the reference's code.
 
 Outputs (committed): tests/golden/tiny_decode.json, tests/golden/tiny_scoring.npz,
-tests/golden/helpers.npz.  Nothing at test time reads the reference checkout.
+tests/golden/helpers.npz, tests/golden/tiny_choices.npz.  Nothing at test time reads the
+reference checkout.  `--only choices` regenerates the last file alone (it draws from its own
+random stream, so the others are unaffected).
 """
 
 from __future__ import annotations
@@ -115,7 +117,41 @@ class OracleModule:
         return OracleBackend(self.model)
 
 
+CHOICE_CONTINUATIONS = (2, 5, 25, 1)  # the third needs more than one block: the cache grows
+
+
+def make_choices(vm, params, dev, reshape, spec) -> None:
+    """Multiple-choice scoring with prefix-cache reuse (runtime.py:546-548): one context scored
+    against several continuations in turn, each call handed the (aligned prefix, cache) pair the
+    previous call returned, then a different context (the cache is rebuilt).  Records every
+    choice's logits and log-likelihood and the entry-point calls, which show one prefix build per
+    context."""
+    rng = np.random.default_rng(2)
+    ctx_a = rng.integers(0, 1000, 75).tolist()
+    ctx_b = rng.integers(0, 1000, 40).tolist()
+    plan = [(ctx_a, rng.integers(0, 1000, n).tolist()) for n in CHOICE_CONTINUATIONS]
+    plan.append((ctx_b, rng.integers(0, 1000, 3).tolist()))
+    out = {}
+    cached = None
+    vm.backend.calls.clear()
+    for i, (ctx, cont) in enumerate(plan):
+        logits, cached = ref_rt.score_masked_continuation(
+            vm, params, dev, reshape, ctx, cont, num_attention_heads=TINY.num_attention_heads, block_size=32,
+            mask_id=TINY_MASK_ID, cache_spec=spec, eos_token_id=1022, cached_prefix=cached)
+        lp = torch.log_softmax(torch.from_numpy(np.asarray(logits, dtype=np.float32)), dim=-1)
+        ll = float(lp.gather(-1, torch.tensor(cont).unsqueeze(-1)).squeeze(-1).sum().item())
+        out[f"choice{i}/context"] = np.asarray(ctx, np.int32)
+        out[f"choice{i}/continuation"] = np.asarray(cont, np.int32)
+        out[f"choice{i}/logits"] = np.asarray(logits, np.float32)
+        out[f"choice{i}/loglik"] = np.asarray(ll, np.float64)
+        print(f"choice{i}", len(ctx), len(cont), ll, flush=True)
+    out["n_choices"] = np.asarray(len(plan), np.int32)
+    out["calls"] = np.asarray(json.dumps(vm.backend.calls))
+    np.savez_compressed(HERE / "tiny_choices.npz", **out)
+
+
 def main() -> None:
+    only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
     torch.manual_seed(0)
     params_t = make_synthetic_params(TINY, seed=0, dtype="float32", mask_id=TINY_MASK_ID)
     model = OracleModel(oracle_config(TINY), params_t, "float32")
@@ -124,6 +160,9 @@ def main() -> None:
     params = [tvm.runtime.Tensor(p) for p in params_t]
     reshape = tvm.get_global_func("vm.builtin.reshape")
     spec = ref_rt.CacheSpec(TINY.num_hidden_layers, TINY.num_key_value_heads, TINY.head_dim, "float32")
+    if only == "choices":
+        make_choices(vm, params, dev, reshape, spec)
+        return
     rng = np.random.default_rng(0)
 
     def prompt(n):
@@ -191,6 +230,7 @@ def main() -> None:
     helpers["shift/p0_b12"] = extract_shifted_block_logits(arr, prefix_len=0, block_len=12)
     helpers["shift/p4_b8"] = extract_shifted_block_logits(arr, prefix_len=4, block_len=8)
     np.savez_compressed(HERE / "helpers.npz", **helpers)
+    make_choices(vm, params, dev, reshape, spec)
 
 
 if __name__ == "__main__":

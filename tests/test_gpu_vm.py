@@ -15,7 +15,7 @@ from fast_dllm_relax_b200 import artifacts, install_tvm_shim
 from fast_dllm_relax_b200.config import TINY, TINY_MASK_ID, make_synthetic_params
 from oracle import decode as od
 from oracle.model import confidence as oracle_confidence
-from tests._oracle_util import make_oracle
+from tests._oracle_util import make_oracle, score_choices
 
 install_tvm_shim()
 import tvm  # noqa: E402
@@ -119,6 +119,20 @@ def test_vm_scoring_matches_reference_runtime(name, vm_fp32, golden_dir):
                                              mask_id=TINY_MASK_ID, eos_token_id=1022)
     np.testing.assert_allclose(logits, g[f"{name}/logits"], rtol=1e-4, atol=1e-4)
     assert od.loglikelihood(logits, cont) == pytest.approx(float(g[f"{name}/loglik"]), rel=1e-4, abs=1e-4)
+
+
+def test_vm_choice_scoring_reuses_the_prefix_cache(vm_fp32, golden_dir):
+    """Answer choices scored one after another against one context through vm[name]: one prefix
+    build per context, the cached prefix reused (and grown for a 36-row tail), the reference
+    runtime's logits and call sequence (runtime.py:546-548)."""
+    vm, vparams, dev, _ = vm_fp32
+    g = np.load(golden_dir / "tiny_choices.npz")
+    m = VmModel(vm, vparams, dev, TINY)
+    res = score_choices(m, g, TINY_MASK_ID)
+    for i, (logits, cont, _) in enumerate(res):
+        np.testing.assert_allclose(logits, g[f"choice{i}/logits"], rtol=1e-4, atol=1e-4)
+        assert od.loglikelihood(logits, cont) == pytest.approx(float(g[f"choice{i}/loglik"]), rel=1e-4, abs=1e-4)
+    assert m.calls == json.loads(str(g["calls"]))
 
 
 @pytest.mark.parametrize("rows", [8, 32])

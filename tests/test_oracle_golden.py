@@ -11,7 +11,7 @@ import torch
 from fast_dllm_relax_b200.config import TINY, TINY_MASK_ID, make_synthetic_params
 from oracle import decode as od
 from oracle.model import build_block_bias
-from tests._oracle_util import LoggingOracle, make_oracle
+from tests._oracle_util import LoggingOracle, make_oracle, score_choices
 
 
 @pytest.fixture(scope="module")
@@ -54,6 +54,21 @@ def test_scoring_matches_reference_runtime(name, tiny_oracle, golden_dir):
                                              eos_token_id=1022)
     np.testing.assert_array_equal(logits, g[f"{name}/logits"])
     assert od.loglikelihood(logits, cont) == pytest.approx(float(g[f"{name}/loglik"]), abs=0)
+
+
+def test_choice_scoring_reuses_the_prefix_cache(tiny_oracle, golden_dir):
+    """Several answer choices against one context (runtime.py:546-548): the prefix cache is built
+    once and reused, grown for a tail longer than a block, and rebuilt for a new context."""
+    g = np.load(golden_dir / "tiny_choices.npz")
+    m = LoggingOracle(tiny_oracle)
+    res = score_choices(m, g, TINY_MASK_ID)
+    for i, (logits, cont, _) in enumerate(res):
+        np.testing.assert_array_equal(logits, g[f"choice{i}/logits"])
+        assert od.loglikelihood(logits, cont) == pytest.approx(float(g[f"choice{i}/loglik"]), abs=0)
+    caches = [c for _, _, c in res]
+    assert all(c is caches[0] for c in caches[1:4]) and caches[4] is not caches[0]
+    assert caches[0].capacity >= 64 + 36  # grown for the 36-row tail
+    assert m.calls == json.loads(str(g["calls"]))
 
 
 def test_bias_helper_matches_reference(golden_dir):
