@@ -23,6 +23,7 @@ computes, up to the bf16 rounding of the larger token tiles.
 from __future__ import annotations
 
 import dataclasses
+import itertools
 from typing import Generator, Sequence
 
 import numpy as np
@@ -46,6 +47,12 @@ class _Cache:
 #   ("prefill", cache, ids)                      -> None; rows [0, len(ids)) of `cache` written
 #   ("step", cache, ids, write_rel, attend_rel)  -> (ids int64[rows], maxp float32[rows]), unshifted
 #   ("dense", seq_ids)                           -> float32 logits [len(seq_ids), vocab] (stateless path)
+
+def _id_tensor(seqs, n: int, dev) -> torch.Tensor:
+    """The token ids of several requests, concatenated, as int32 on `dev` (one host buffer)."""
+    flat = np.fromiter(itertools.chain.from_iterable(seqs), dtype=np.int32, count=n)
+    return torch.from_numpy(flat).to(dev)
+
 
 def _shifted(vals, row: int):
     """runtime.py:169-174: row i takes row i-1's prediction, row 0 its own."""
@@ -217,7 +224,7 @@ def generate_batch(engine: Engine, prompts: Sequence[Sequence[int]], *, max_new_
             if timing is not None:
                 ev.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
                 ev[-1][0].record()
-            ids_all = torch.tensor([t for i in pre for t in pending[i][2]], dtype=torch.int32, device=dev)
+            ids_all = _id_tensor([pending[i][2] for i in pre], sum(len(pending[i][2]) for i in pre), dev)
             engine.build_prefix_cache_batch(engine.embed(ids_all), [(pending[i][1].k, pending[i][1].v) for i in pre],
                                             [len(pending[i][2]) for i in pre])
             if timing is not None:
@@ -234,7 +241,7 @@ def generate_batch(engine: Engine, prompts: Sequence[Sequence[int]], *, max_new_
         if not steps:
             continue
         # every pending cached step in one batched forward + one fused confidence launch
-        ids_all = torch.tensor([t for _, op in steps for t in op[2]], dtype=torch.int32, device=dev)
+        ids_all = _id_tensor([op[2] for _, op in steps], sum(len(op[2]) for _, op in steps), dev)
         x = engine.embed(ids_all)
         reqs = []
         for _, (_, cache, ids, write_rel, attend_rel) in steps:
