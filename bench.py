@@ -40,18 +40,28 @@ UNIT = "tokens/s"
 PROMPT_LEN, GEN_LEN, BLOCK, SUB_BLOCK, THRESHOLD = 256, 256, 32, 8, 0.9
 
 
+PEAKS_FILE = REPO / "MEASURED_PEAKS.json"  # written by the measuring driver on each pod
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}  # an earlier measurement on this pool
+
+
+def _peak(key: str, path: Path | None = None) -> tuple[float, str]:
+    """The measured peak `key` from the peaks file, else the fallback figure (and which it is)."""
+    p = PEAKS_FILE if path is None else path
+    try:
+        val = json.loads(p.read_text()).get(key)
+        if isinstance(val, (int, float)) and val > 0:
+            return float(val), "measured"
+    except (OSError, ValueError, AttributeError):
+        pass
+    return FALLBACK_PEAKS[key], "fallback"
+
+
 def _peaks() -> tuple[float, str]:
-    p = REPO / "MEASURED_PEAKS.json"
-    if p.exists():
-        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+    return _peak("hbm_gbs")
 
 
 def _tensor_peak() -> tuple[float, str]:
-    p = REPO / "MEASURED_PEAKS.json"
-    if p.exists():
-        return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
-    return 1590.0, "fallback"
+    return _peak("bf16_tflops")
 
 
 # 1.5B bf16 algorithmic units of one refinement step (weights incl. biases and norms, tied lm_head)

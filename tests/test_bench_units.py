@@ -28,3 +28,16 @@ def test_step_roofline_is_weight_bound_at_decode_rows():
     assert r["nominal"]["floor_ms"] < m["floor_ms"]
     big = bench.step_roofline(8192, 384, 1.0, 6552.0, 1618.1)      # enough rows to turn tensor-bound
     assert abs(big["measured"]["floor_ms"] - big["flops"] / 1618.1e12 * 1e3) < 1e-9
+
+
+def test_peaks_fall_back_per_key(tmp_path):
+    p = tmp_path / "peaks.json"
+    assert bench._peak("hbm_gbs", p) == (6650.0, "fallback")  # no file
+    p.write_text('{"hbm_gbs": 6552.0}')
+    assert bench._peak("hbm_gbs", p) == (6552.0, "measured")
+    assert bench._peak("bf16_tflops", p) == (1590.0, "fallback")  # key absent
+    p.write_text("not json")
+    assert bench._peak("hbm_gbs", p) == (6650.0, "fallback")
+    p.write_text('{"hbm_gbs": null, "bf16_tflops": 1618.1}')
+    assert bench._peak("hbm_gbs", p) == (6650.0, "fallback")
+    assert bench._peak("bf16_tflops", p) == (1618.1, "measured")
