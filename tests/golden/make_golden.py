@@ -13,9 +13,10 @@ step statistics and the exact sequence of entry-point calls -- so that tests can
 decode restatement (oracle/decode.py) and the product's drivers against the reference's code.
 
 Outputs (committed): tests/golden/tiny_decode.json, tests/golden/tiny_scoring.npz,
-tests/golden/helpers.npz, tests/golden/tiny_choices.npz.  Nothing at test time reads the
-reference checkout.  `--only choices` regenerates the last file alone (it draws from its own
-random stream, so the others are unaffected).
+tests/golden/helpers.npz, tests/golden/tiny_choices.npz, tests/golden/tiny_decode_edges.json.
+Nothing at test time reads the reference checkout.  `--only choices` and `--only edges`
+regenerate one of the last two files alone (each draws from its own random stream, so the others
+are unaffected).
 """
 
 from __future__ import annotations
@@ -150,6 +151,36 @@ def make_choices(vm, params, dev, reshape, spec) -> None:
     np.savez_compressed(HERE / "tiny_choices.npz", **out)
 
 
+def make_edges(vm, params, dev, reshape, spec) -> None:
+    """Decode edge cases of runtime.py:591-880: no new tokens, one new token after a block-aligned
+    prompt (:679-708 alone), a stop on the very first committed token, and limits that cut the
+    first block mid-refinement (:839-849, the continuation trimmed at the first mask)."""
+    rng = np.random.default_rng(3)
+    p64, p40 = rng.integers(0, 1000, 64).tolist(), rng.integers(0, 1000, 40).tolist()
+    cases = [dict(name="zero_new_tokens", prompt=p64, max_new_tokens=0, use_block_cache=True),
+             dict(name="one_new_token_aligned", prompt=p64, max_new_tokens=1, use_block_cache=False),
+             dict(name="cut_mid_block", prompt=p40, max_new_tokens=5, use_block_cache=True),
+             dict(name="cut_mid_block_nocache", prompt=p64, max_new_tokens=11, use_block_cache=False)]
+    out = {"mask_id": TINY_MASK_ID, "cases": []}
+
+    def run(case):
+        vm.backend.calls.clear()
+        kw = dict(num_attention_heads=TINY.num_attention_heads, max_new_tokens=case["max_new_tokens"],
+                  block_size=32, small_block_size=8, threshold=0.9, temperature=0.0, top_p=0.95,
+                  use_block_cache=case["use_block_cache"], mask_id=TINY_MASK_ID,
+                  stop_token=case.get("stop_token"), cache_spec=spec)
+        toks, stats = ref_rt.relax_greedy_generate(vm, params, dev, reshape, None, list(case["prompt"]), **kw)
+        print(case["name"], len(toks), stats, flush=True)
+        return dict(case, tokens=[int(t) for t in toks], stats=stats, calls=list(vm.backend.calls))
+
+    for c in cases:
+        out["cases"].append(run(c))
+    first = out["cases"][1]["tokens"][0]  # the token the aligned prompt's commit step yields
+    out["cases"].append(run(dict(name="stop_on_first_token", prompt=p64, max_new_tokens=40,
+                                 use_block_cache=True, stop_token=int(first))))
+    (HERE / "tiny_decode_edges.json").write_text(json.dumps(out, indent=1) + "\n", encoding="utf-8")
+
+
 def main() -> None:
     only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
     torch.manual_seed(0)
@@ -162,6 +193,9 @@ def main() -> None:
     spec = ref_rt.CacheSpec(TINY.num_hidden_layers, TINY.num_key_value_heads, TINY.head_dim, "float32")
     if only == "choices":
         make_choices(vm, params, dev, reshape, spec)
+        return
+    if only == "edges":
+        make_edges(vm, params, dev, reshape, spec)
         return
     rng = np.random.default_rng(0)
 
@@ -231,6 +265,7 @@ def main() -> None:
     helpers["shift/p4_b8"] = extract_shifted_block_logits(arr, prefix_len=4, block_len=8)
     np.savez_compressed(HERE / "helpers.npz", **helpers)
     make_choices(vm, params, dev, reshape, spec)
+    make_edges(vm, params, dev, reshape, spec)
 
 
 if __name__ == "__main__":

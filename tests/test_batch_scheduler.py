@@ -104,3 +104,16 @@ def test_scheduler_mixed_batch_matches_reference_runtime(engine, golden):
     # batched: far fewer step launches than the requests' steps summed
     steps = engine.calls["step_batch"] - before["step_batch"]
     assert steps < sum(s["block_recomputes"] for s in stats)
+
+
+@pytest.mark.parametrize("name", ["zero_new_tokens", "one_new_token_aligned", "cut_mid_block",
+                                  "cut_mid_block_nocache", "stop_on_first_token"])
+def test_scheduler_edge_cases_match_reference_runtime(name, engine, golden_dir):
+    """The decode loop's edge cases (tests/golden/tiny_decode_edges.json) through the scheduler."""
+    golden = json.loads((golden_dir / "tiny_decode_edges.json").read_text())
+    case = next(c for c in golden["cases"] if c["name"] == name)
+    toks, stats = generate_batch(engine, [case["prompt"]], max_new_tokens=case["max_new_tokens"], block_size=32,
+                                 small_block_size=8, threshold=0.9, use_block_cache=case["use_block_cache"],
+                                 mask_id=golden["mask_id"], stop_token=case.get("stop_token"))
+    assert toks[0] == case["tokens"]
+    assert stats[0] == case["stats"]

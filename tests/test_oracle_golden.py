@@ -45,6 +45,26 @@ def test_decode_matches_reference_runtime(name, tiny_oracle, decode_golden):
     assert m.calls == case["calls"]
 
 
+EDGE_CASES = ["zero_new_tokens", "one_new_token_aligned", "cut_mid_block", "cut_mid_block_nocache",
+              "stop_on_first_token"]
+
+
+@pytest.mark.parametrize("name", EDGE_CASES)
+def test_decode_edge_cases_match_reference_runtime(name, tiny_oracle, golden_dir):
+    """No new tokens, one token after a block-aligned prompt, limits that cut the first block, a
+    stop on the first committed token (tests/golden/tiny_decode_edges.json)."""
+    golden = json.loads((golden_dir / "tiny_decode_edges.json").read_text())
+    case = next(c for c in golden["cases"] if c["name"] == name)
+    m = LoggingOracle(tiny_oracle)
+    toks, stats = od.relax_greedy_generate(
+        m, case["prompt"], max_new_tokens=case["max_new_tokens"], block_size=32, small_block_size=8,
+        threshold=0.9, use_block_cache=case["use_block_cache"], mask_id=golden["mask_id"],
+        stop_token=case.get("stop_token"))
+    assert toks == case["tokens"]
+    assert stats == case["stats"]
+    assert m.calls == case["calls"]
+
+
 @pytest.mark.parametrize("name", ["ctx70_cont5", "ctx20_cont4", "ctx64_cont40", "ctx96_cont16"])
 def test_scoring_matches_reference_runtime(name, tiny_oracle, golden_dir):
     g = np.load(golden_dir / "tiny_scoring.npz")
