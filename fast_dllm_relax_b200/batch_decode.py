@@ -45,7 +45,7 @@ class _Cache:
 
 # Work items a request program yields (and what it receives back):
 #   ("prefill", cache, ids)                      -> None; rows [0, len(ids)) of `cache` written
-#   ("step", cache, ids, write_rel, attend_rel)  -> (ids int64[rows], maxp float32[rows]), unshifted
+#   ("step", cache, ids, write_rel, attend_rel)  -> (ids, maxp): lists of rows ints / floats, unshifted
 #   ("dense", seq_ids)                           -> float32 logits [len(seq_ids), vocab] (stateless path)
 
 def _id_tensor(seqs, n: int, dev) -> torch.Tensor:
@@ -251,7 +251,8 @@ def generate_batch(engine: Engine, prompts: Sequence[Sequence[int]], *, max_new_
         hidden = engine.forward_cached_batch(x, reqs)
         cid, cmax = engine.confidence(hidden)
         both = torch.cat([cid.view(torch.float32), cmax]).cpu().numpy()  # one device-to-host copy
-        cid, cmax = both[:len(cid)].view(np.int32).astype(np.int64), both[len(cid):]
+        # Python lists: each request reads a few of its rows one by one, which lists serve faster
+        cid, cmax = both[:len(cid)].view(np.int32).tolist(), both[len(cid):].tolist()
         o = 0
         for i, op in steps:
             rows = len(op[2])
