@@ -1,11 +1,13 @@
 """CPU checks of the C ABI boundary: the library loads without a GPU, exports every function that
 include/fdllm_sm100.h declares, and the ctypes signatures cover exactly that set."""
 
+import ctypes
 import re
 import subprocess
 from pathlib import Path
 
 import pytest
+import torch
 
 from fast_dllm_relax_b200 import _lib
 
@@ -59,3 +61,43 @@ def test_build_targets_sm100a_only():
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(ImportError, match="build"):
         _lib.load(tmp_path / "nope.so")
+
+
+def _zero(t):
+    if t in (ctypes.c_int, ctypes.c_int32, ctypes.c_longlong, ctypes.c_ulonglong):
+        return 0
+    if t in (ctypes.c_double, ctypes.c_float):
+        return 0.0
+    return None
+
+
+def test_every_handle_call_rejects_a_null_handle_without_a_gpu(lib):
+    """Errors cross the ABI as a status and a message, never as a crash: every entry point that
+    takes a handle returns FDLLM_ERR_INVALID for a null one before touching a device."""
+    checked = 0
+    for name, (res, args) in _lib.SIGNATURES.items():
+        if not args or args[0] is not ctypes.c_void_p or name == "fdllm_destroy":
+            continue
+        rc = getattr(lib, name)(*[_zero(a) for a in args])
+        if name == "fdllm_workspace_bytes":
+            assert rc == 0
+        else:
+            assert rc == _lib.FDLLM_ERR_INVALID, name
+            assert lib.fdllm_last_error().decode() in ("null handle", "null argument"), name
+        checked += 1
+    assert checked >= 20
+    assert lib.fdllm_destroy(None) == _lib.FDLLM_OK
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device error path")
+def test_create_without_a_device_returns_a_cuda_error(lib):
+    from fast_dllm_relax_b200.config import TINY
+    c = _lib.FdllmConfig(TINY.vocab_size, TINY.hidden_size, TINY.intermediate_size, TINY.num_hidden_layers,
+                         TINY.num_attention_heads, TINY.num_key_value_heads, TINY.head_dim, TINY.rms_norm_eps,
+                         TINY.rope_theta, 1, TINY.bd_size, 4096, 0)
+    h = ctypes.c_void_p()
+    assert lib.fdllm_create(ctypes.byref(c), 0, ctypes.byref(h)) == _lib.FDLLM_ERR_CUDA
+    assert h.value is None
+    assert lib.fdllm_last_error()
+    with pytest.raises(_lib.FdllmError):
+        _lib.check(_lib.FDLLM_ERR_CUDA)
