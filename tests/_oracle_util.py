@@ -68,3 +68,29 @@ def score_choices(model, g, mask_id: int) -> list[tuple]:
                                                       eos_token_id=1022, cached_prefix=cached)
         out.append((logits, cont, cached[1]))
     return out
+
+
+# The small architecture the oracle is pinned on against the reference's own model graph
+# (tests/golden/make_model_golden.py): head_dim 128, because the reference's cached-attention
+# callback hard-codes the 1/sqrt(128) softmax scale (runtime.py:27), and 2 query heads per KV head.
+def pin_config():
+    from fast_dllm_relax_b200.config import ModelConfig
+    return ModelConfig(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                       num_attention_heads=2, num_key_value_heads=1, head_dim=128, rms_norm_eps=1e-6,
+                       rope_theta=1e6, context_window_size=4096, tie_word_embeddings=True)
+
+
+def pin_params(dtype: str):
+    """Weights of the reference-graph pin: N(0, 0.05) matrices and biases (seed 11) and RMSNorm
+    weights 1 + N(0, 0.1) (seed 12), so that the norms' weight multiply is exercised too."""
+    import torch
+
+    from fast_dllm_relax_b200.config import make_synthetic_params, param_names
+    cfg = pin_config()
+    g = torch.Generator().manual_seed(12)
+    out = []
+    for name, p in zip(param_names(cfg), make_synthetic_params(cfg, seed=11, dtype="float32", std=0.05)):
+        if name.endswith("norm.weight"):
+            p = 1.0 + 0.1 * torch.randn(p.shape, generator=g)
+        out.append(p.to({"float32": torch.float32, "bfloat16": torch.bfloat16}[dtype]))
+    return out

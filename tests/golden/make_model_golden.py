@@ -1,0 +1,133 @@
+"""Generate golden vectors of the reference's OWN model graph (fast_dllm_relax/model/cuda.py).
+
+Run where a checkout of the reference exists, naming it:
+
+    FDLLM_REFERENCE=<path to the reference checkout> python tests/golden/make_model_golden.py
+
+TVM cannot be installed here, so the reference's model definition is executed op by op through
+tests/golden/eager_nn.py, an eager PyTorch stand-in for the slice of TVM's Relax `nn` frontend it
+is written against.  The cached entry points call the reference runtime's own packed callbacks
+(`fast_dllm.attn_inplace`, `fast_dllm.kv_write`, runtime.py:46-73; their PyTorch SDPA branch, as
+flash_attn cannot run on the CPU).  The model is FastDLLMRelaxForCausalLM with fused qkv and
+gate_up projections (the artifact layout), on the small head_dim-128 architecture and weights of
+tests/_oracle_util.pin_config / pin_params, in fp32 and bf16.
+
+Recorded per dtype (tests/golden/model_graph.npz; bf16 values stored as uint16 bit patterns):
+  dense/h        forward_hidden over 96 rows with the block-causal bias: the last 32 rows
+  dense/logits   get_logits of those 32 rows (fp32)
+  prefill/k, v   build_prefix_cache over the first 64 rows: the last layer's K/V rows [0, 64)
+  cached/h       forward_cached of rows [64, 96) (cache_offset 64, prefix_len 64)
+  cached/k, v    the last layer's K/V rows [64, 96) it wrote
+  partial/h      forward_block_partial_rp8 of 8 new rows (cache_offset 72, prefix_len 64)
+  partial/k, v   the last layer's K/V rows [72, 80) it overwrote
+Nothing at test time reads the reference checkout.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+if "FDLLM_REFERENCE" not in os.environ:
+    raise SystemExit("set FDLLM_REFERENCE to the reference checkout")
+REF = Path(os.environ["FDLLM_REFERENCE"])
+
+sys.path.insert(0, str(REPO / "fast_dllm_relax_b200" / "tvm_shim"))
+sys.path.insert(0, str(REPO))
+sys.path.insert(0, str(HERE))
+sys.path.insert(1, str(REF))
+
+import tvm  # noqa: E402  (the stand-in)
+
+import eager_nn  # noqa: E402
+
+assert getattr(tvm, "IS_FDLLM_SHIM", False), "expected the repository's TVM stand-in"
+eager_nn.install(tvm)
+sys.modules["flash_attn"] = None  # the runtime's attention callback takes its SDPA branch
+
+import fast_dllm_relax.runtime  # noqa: E402,F401  (registers the packed callbacks)
+from fast_dllm_relax.model.cuda import (  # noqa: E402
+    FastDLLMRelaxConfig,
+    FastDLLMRelaxForCausalLM,
+    build_prefix_block_attention_bias,
+)
+
+from fast_dllm_relax_b200.config import param_names  # noqa: E402
+from tests._oracle_util import pin_config, pin_params  # noqa: E402
+
+P, B, S, RP = 64, 32, 8, 8
+
+
+def run(dtype: str) -> dict[str, np.ndarray]:
+    cfg = pin_config()
+    rcfg = FastDLLMRelaxConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size,
+                               intermediate_size=cfg.intermediate_size, num_hidden_layers=cfg.num_hidden_layers,
+                               num_attention_heads=cfg.num_attention_heads,
+                               num_key_value_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
+                               rms_norm_eps=cfg.rms_norm_eps, rope_theta=cfg.rope_theta,
+                               context_window_size=cfg.context_window_size,
+                               tie_word_embeddings=cfg.tie_word_embeddings, bd_size=cfg.bd_size,
+                               pad_token_id=cfg.pad_token_id)
+    model = FastDLLMRelaxForCausalLM(rcfg, dtype=dtype, fused_qkv=True, fused_gate_up=True)
+    named = list(model.named_parameters())
+    assert [n for n, _ in named] == param_names(cfg), "parameter order differs from the artifact's"
+    for (_, p), t in zip(named, pin_params(dtype)):
+        p.bind(t)
+    T = eager_nn.Tensor
+    g = torch.Generator().manual_seed(21)
+    ids = torch.randint(0, cfg.vocab_size, (P + B,), generator=g, dtype=torch.int32)
+    ids8 = torch.randint(0, cfg.vocab_size, (S,), generator=g, dtype=torch.int32)
+    x = model.embed(T(ids))._expr.as_subclass(torch.Tensor).reshape(1, P + B, -1)
+    x8 = model.embed(T(ids8))._expr.as_subclass(torch.Tensor).reshape(1, S, -1)
+    out = {"ids": ids.numpy(), "ids8": ids8.numpy()}
+
+    bias = torch.from_numpy(build_prefix_block_attention_bias(0, P + B, block_size=B))
+    h = model.forward_hidden(T(x), T(bias))._expr.as_subclass(torch.Tensor)
+    logits = model.get_logits(T(h[:, P:]))._expr.as_subclass(torch.Tensor)
+    out["dense/h"], out["dense/logits"] = h[0, P:], logits[0]
+
+    shape = (cfg.num_hidden_layers, 1, P + B, cfg.num_key_value_heads, cfg.head_dim)
+    k = torch.zeros(shape, dtype=x.dtype)
+    v = torch.zeros(shape, dtype=x.dtype)
+    pbias = torch.from_numpy(build_prefix_block_attention_bias(0, P, block_size=B))
+    model.build_prefix_cache(T(x[:, :P].contiguous()), T(pbias), T(k), T(v))
+    out["prefill/k"], out["prefill/v"] = k[-1, 0, :P].clone(), v[-1, 0, :P].clone()
+
+    off = T(torch.tensor(P, dtype=torch.int32))
+    hc = model.forward_cached(T(x[:, P:].contiguous()), T(k), T(v), off, P)._expr.as_subclass(torch.Tensor)
+    out["cached/h"], out["cached/k"], out["cached/v"] = hc[0], k[-1, 0, P:P + B].clone(), v[-1, 0, P:P + B].clone()
+
+    off8 = T(torch.tensor(P + RP, dtype=torch.int32))
+    hp = model.forward_block_partial_rp8(T(x8), T(k), T(v), off8, P)._expr.as_subclass(torch.Tensor)
+    out["partial/h"] = hp[0]
+    out["partial/k"], out["partial/v"] = k[-1, 0, P + RP:P + RP + S].clone(), v[-1, 0, P + RP:P + RP + S].clone()
+
+    res = {}
+    for key, val in out.items():
+        if isinstance(val, torch.Tensor):
+            val = val.detach()
+            val = val.view(torch.int16).numpy().view(np.uint16) if val.dtype == torch.bfloat16 else val.numpy()
+        res[f"{dtype}/{key}"] = np.ascontiguousarray(val)
+    return res
+
+
+def main() -> None:
+    torch.set_num_threads(1)  # deterministic CPU reductions
+    res = {"model_cuda_sha256": np.asarray(hashlib.sha256((REF / "fast_dllm_relax/model/cuda.py").read_bytes())
+                                           .hexdigest())}
+    with torch.no_grad():
+        for dtype in ("float32", "bfloat16"):
+            res.update(run(dtype))
+            print(dtype, "ok", flush=True)
+    np.savez_compressed(HERE / "model_graph.npz", **res)
+
+
+if __name__ == "__main__":
+    main()
