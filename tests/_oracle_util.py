@@ -80,16 +80,21 @@ def pin_config():
                        rope_theta=1e6, context_window_size=4096, tie_word_embeddings=True)
 
 
-def pin_params(dtype: str):
+PIN_MASK_ID = 511
+
+
+def pin_params(dtype: str, mask_id: int | None = None):
     """Weights of the reference-graph pin: N(0, 0.05) matrices and biases (seed 11) and RMSNorm
-    weights 1 + N(0, 0.1) (seed 12), so that the norms' weight multiply is exercised too."""
+    weights 1 + N(0, 0.1) (seed 12), so that the norms' weight multiply is exercised too.
+    `mask_id`: zero that embedding row (decode runs; see make_synthetic_params)."""
     import torch
 
     from fast_dllm_relax_b200.config import make_synthetic_params, param_names
     cfg = pin_config()
     g = torch.Generator().manual_seed(12)
     out = []
-    for name, p in zip(param_names(cfg), make_synthetic_params(cfg, seed=11, dtype="float32", std=0.05)):
+    for name, p in zip(param_names(cfg), make_synthetic_params(cfg, seed=11, dtype="float32", std=0.05,
+                                                               mask_id=mask_id)):
         if name.endswith("norm.weight"):
             p = 1.0 + 0.1 * torch.randn(p.shape, generator=g)
         out.append(p.to({"float32": torch.float32, "bfloat16": torch.bfloat16}[dtype]))

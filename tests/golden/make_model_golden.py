@@ -20,12 +20,18 @@ Recorded per dtype (tests/golden/model_graph.npz; bf16 values stored as uint16 b
   cached/k, v    the last layer's K/V rows [64, 96) it wrote
   partial/h      forward_block_partial_rp8 of 8 new rows (cache_offset 72, prefix_len 64)
   partial/k, v   the last layer's K/V rows [72, 80) it overwrote
+
+Decode runs of the whole reference stack (tests/golden/model_decode.json): the reference's
+runtime.py (`relax_greedy_generate`) drives a VirtualMachine whose entry points are this eager
+reference graph, in fp32 on the same architecture (mask id 511, its embedding row zeroed); the
+tokens, step statistics and entry-point calls are recorded.
 Nothing at test time reads the reference checkout.
 """
 
 from __future__ import annotations
 
 import hashlib
+import json
 import os
 import sys
 from pathlib import Path
@@ -60,26 +66,15 @@ from fast_dllm_relax.model.cuda import (  # noqa: E402
 )
 
 from fast_dllm_relax_b200.config import param_names  # noqa: E402
-from tests._oracle_util import pin_config, pin_params  # noqa: E402
+import fast_dllm_relax.runtime as ref_rt  # noqa: E402
+from tests._oracle_util import PIN_MASK_ID, pin_config, pin_params  # noqa: E402
 
 P, B, S, RP = 64, 32, 8, 8
 
 
 def run(dtype: str) -> dict[str, np.ndarray]:
     cfg = pin_config()
-    rcfg = FastDLLMRelaxConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size,
-                               intermediate_size=cfg.intermediate_size, num_hidden_layers=cfg.num_hidden_layers,
-                               num_attention_heads=cfg.num_attention_heads,
-                               num_key_value_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
-                               rms_norm_eps=cfg.rms_norm_eps, rope_theta=cfg.rope_theta,
-                               context_window_size=cfg.context_window_size,
-                               tie_word_embeddings=cfg.tie_word_embeddings, bd_size=cfg.bd_size,
-                               pad_token_id=cfg.pad_token_id)
-    model = FastDLLMRelaxForCausalLM(rcfg, dtype=dtype, fused_qkv=True, fused_gate_up=True)
-    named = list(model.named_parameters())
-    assert [n for n, _ in named] == param_names(cfg), "parameter order differs from the artifact's"
-    for (_, p), t in zip(named, pin_params(dtype)):
-        p.bind(t)
+    model = ref_model(dtype)
     T = eager_nn.Tensor
     g = torch.Generator().manual_seed(21)
     ids = torch.randint(0, cfg.vocab_size, (P + B,), generator=g, dtype=torch.int32)
@@ -118,6 +113,104 @@ def run(dtype: str) -> dict[str, np.ndarray]:
     return res
 
 
+def ref_model(dtype: str, mask_id: int | None = None):
+    cfg = pin_config()
+    rcfg = FastDLLMRelaxConfig(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size,
+                               intermediate_size=cfg.intermediate_size, num_hidden_layers=cfg.num_hidden_layers,
+                               num_attention_heads=cfg.num_attention_heads,
+                               num_key_value_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim,
+                               rms_norm_eps=cfg.rms_norm_eps, rope_theta=cfg.rope_theta,
+                               context_window_size=cfg.context_window_size,
+                               tie_word_embeddings=cfg.tie_word_embeddings, bd_size=cfg.bd_size,
+                               pad_token_id=cfg.pad_token_id)
+    model = FastDLLMRelaxForCausalLM(rcfg, dtype=dtype, fused_qkv=True, fused_gate_up=True)
+    named = list(model.named_parameters())
+    assert [n for n, _ in named] == param_names(cfg), "parameter order differs from the artifact's"
+    for (_, p), t in zip(named, pin_params(dtype, mask_id)):
+        p.bind(t)
+    return model
+
+
+class RefGraphBackend:
+    """vm[name] served by the eager reference graph over the stand-in's tensors; logs every call
+    in the golden call-log format [name, rows, cache_offset, prefix_len]."""
+
+    def __init__(self, model):
+        self.model = model
+        self.calls: list[list] = []
+
+    def function(self, name: str):
+        m, E, R = self.model, eager_nn.Tensor, tvm.runtime.Tensor
+
+        def out(t):
+            return R(t._expr.as_subclass(torch.Tensor))
+
+        if name == "embed":
+            def embed(ids, params):
+                self.calls.append(["embed", int(ids.shape[0]), -1, -1])
+                return out(m.embed(E(ids.torch)))
+            return embed
+        if name == "forward_hidden":
+            def forward_hidden(x, bias, params):
+                self.calls.append(["forward_hidden", int(x.shape[1]), -1, -1])
+                return out(m.forward_hidden(E(x.torch), E(bias.torch)))
+            return forward_hidden
+        if name == "get_logits":
+            def get_logits(h, params):
+                self.calls.append(["get_logits", int(h.shape[1]), -1, -1])
+                return out(m.get_logits(E(h.torch)))
+            return get_logits
+        if name == "build_prefix_cache":
+            def build_prefix_cache(x, bias, k, v, params):
+                self.calls.append(["build_prefix_cache", int(x.shape[1]), -1, -1])
+                m.build_prefix_cache(E(x.torch), E(bias.torch), E(k.torch), E(v.torch))
+                return k, v
+            return build_prefix_cache
+        if name == "forward_cached" or name.startswith("forward_block_partial_rp"):
+            def cached(x, k, v, off, plen, params):
+                o, p = int(off.torch.item()), int(plen[0])
+                self.calls.append([name, int(x.shape[1]), o, p])
+                fn = m.forward_cached if name == "forward_cached" else getattr(m, name)
+                return out(fn(E(x.torch), E(k.torch), E(v.torch), E(off.torch), p))
+            return cached
+        raise KeyError(name)  # no static or confidence siblings: the reference's host path runs
+
+
+class RefGraphModule:
+    def __init__(self, model):
+        self.model = model
+
+    def create_backend(self, dev):
+        return RefGraphBackend(self.model)
+
+
+def make_decode() -> None:
+    cfg = pin_config()
+    model = ref_model("float32", PIN_MASK_ID)
+    dev = tvm.cpu(0)
+    vm = tvm.relax.VirtualMachine(RefGraphModule(model), dev)
+    params = [tvm.runtime.Tensor(t) for t in pin_params("float32", PIN_MASK_ID)]
+    reshape = tvm.get_global_func("vm.builtin.reshape")
+    spec = ref_rt.CacheSpec(cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim, "float32")
+    rng = np.random.default_rng(4)
+    p64, p45, p20 = (rng.integers(0, 500, n).tolist() for n in (64, 45, 20))
+    cases = [dict(name="aligned_nocache", prompt=p64, max_new_tokens=64, use_block_cache=False),
+             dict(name="aligned_blockcache", prompt=p64, max_new_tokens=64, use_block_cache=True),
+             dict(name="unaligned_blockcache", prompt=p45, max_new_tokens=40, use_block_cache=True),
+             dict(name="short_prompt_stateless", prompt=p20, max_new_tokens=20, use_block_cache=True)]
+    out = {"mask_id": PIN_MASK_ID, "cases": []}
+    for case in cases:
+        vm.backend.calls.clear()
+        toks, stats = ref_rt.relax_greedy_generate(
+            vm, params, dev, reshape, None, list(case["prompt"]), num_attention_heads=cfg.num_attention_heads,
+            max_new_tokens=case["max_new_tokens"], block_size=32, small_block_size=8, threshold=0.9,
+            temperature=0.0, top_p=0.95, use_block_cache=case["use_block_cache"], mask_id=PIN_MASK_ID,
+            stop_token=None, cache_spec=spec)
+        print(case["name"], len(toks), stats, flush=True)
+        out["cases"].append(dict(case, tokens=[int(t) for t in toks], stats=stats, calls=list(vm.backend.calls)))
+    (HERE / "model_decode.json").write_text(json.dumps(out, indent=1) + "\n", encoding="utf-8")
+
+
 def main() -> None:
     torch.set_num_threads(1)  # deterministic CPU reductions
     res = {"model_cuda_sha256": np.asarray(hashlib.sha256((REF / "fast_dllm_relax/model/cuda.py").read_bytes())
@@ -126,7 +219,10 @@ def main() -> None:
         for dtype in ("float32", "bfloat16"):
             res.update(run(dtype))
             print(dtype, "ok", flush=True)
-    np.savez_compressed(HERE / "model_graph.npz", **res)
+        if "--only" not in sys.argv or "graph" in sys.argv:
+            np.savez_compressed(HERE / "model_graph.npz", **res)
+        if "--only" not in sys.argv or "decode" in sys.argv:
+            make_decode()
 
 
 if __name__ == "__main__":

@@ -8,14 +8,20 @@ attention differs only in the summation order of the callback's SDPA).  bf16: th
 rounds after every op (a projection's bias is added after the matmul is rounded), whereas the
 compiled module fuses some of them, so the bf16 check is a 2e-2 relative error of each tensor and
 identical logit argmax, not a per-element bound.
+
+Decode: the reference's runtime.py driving that graph (tests/golden/model_decode.json) and the
+oracle's decode loop over the oracle produce the same tokens, statistics and entry-point calls.
 """
+
+import json
 
 import numpy as np
 import pytest
 import torch
 
+from oracle import decode as od
 from oracle.model import build_block_bias
-from tests._oracle_util import make_oracle, pin_config, pin_params
+from tests._oracle_util import PIN_MASK_ID, LoggingOracle, make_oracle, pin_config, pin_params
 
 P, B, S, RP = 64, 32, 8, 8
 
@@ -71,3 +77,17 @@ def test_bf16_oracle_agrees_with_the_reference_graph(graph):
 
 def test_fixture_records_which_reference_graph(graph):
     assert len(str(graph["model_cuda_sha256"])) == 64
+
+
+@pytest.mark.parametrize("name", ["aligned_nocache", "aligned_blockcache", "unaligned_blockcache",
+                                  "short_prompt_stateless"])
+def test_decode_matches_the_whole_reference_stack(name, golden_dir):
+    golden = json.loads((golden_dir / "model_decode.json").read_text())
+    case = next(c for c in golden["cases"] if c["name"] == name)
+    m = LoggingOracle(make_oracle(pin_config(), pin_params("float32", PIN_MASK_ID), "float32"))
+    toks, stats = od.relax_greedy_generate(m, case["prompt"], max_new_tokens=case["max_new_tokens"], block_size=32,
+                                           small_block_size=8, threshold=0.9, use_block_cache=case["use_block_cache"],
+                                           mask_id=golden["mask_id"])
+    assert toks == case["tokens"]
+    assert stats == case["stats"]
+    assert m.calls == case["calls"]
