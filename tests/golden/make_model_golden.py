@@ -24,7 +24,8 @@ Recorded per dtype (tests/golden/model_graph.npz; bf16 values stored as uint16 b
 Decode runs of the whole reference stack (tests/golden/model_decode.json): the reference's
 runtime.py (`relax_greedy_generate`) drives a VirtualMachine whose entry points are this eager
 reference graph, in fp32 on the same architecture (mask id 511, its embedding row zeroed); the
-tokens, step statistics and entry-point calls are recorded.
+tokens, step statistics and entry-point calls are recorded, and so are the log-likelihoods and
+argmax rows of three answer choices scored against one context with the prefix cache reused.
 Nothing at test time reads the reference checkout.
 """
 
@@ -208,6 +209,21 @@ def make_decode() -> None:
             stop_token=None, cache_spec=spec)
         print(case["name"], len(toks), stats, flush=True)
         out["cases"].append(dict(case, tokens=[int(t) for t in toks], stats=stats, calls=list(vm.backend.calls)))
+    # masked-continuation scoring (runtime.py:485-588), the second and third choices reusing the
+    # first one's prefix cache (runtime.py:546-548)
+    ctx = rng.integers(0, 500, 70).tolist()
+    cached, scoring = None, []
+    vm.backend.calls.clear()
+    for n in (3, 9, 1):
+        cont = rng.integers(0, 500, n).tolist()
+        logits, cached = ref_rt.score_masked_continuation(
+            vm, params, dev, reshape, ctx, cont, num_attention_heads=cfg.num_attention_heads, block_size=32,
+            mask_id=PIN_MASK_ID, cache_spec=spec, eos_token_id=PIN_MASK_ID - 1, cached_prefix=cached)
+        lp = torch.log_softmax(torch.from_numpy(np.asarray(logits, dtype=np.float32)), dim=-1)
+        scoring.append(dict(continuation=cont, loglik=float(lp.gather(-1, torch.tensor(cont)[:, None]).sum()),
+                            argmax=[int(i) for i in np.asarray(logits).argmax(-1)]))
+    out["scoring"] = dict(context=ctx, choices=scoring, calls=list(vm.backend.calls))
+    print("scoring", [c["loglik"] for c in scoring], flush=True)
     (HERE / "model_decode.json").write_text(json.dumps(out, indent=1) + "\n", encoding="utf-8")
 
 

@@ -91,3 +91,18 @@ def test_decode_matches_the_whole_reference_stack(name, golden_dir):
     assert toks == case["tokens"]
     assert stats == case["stats"]
     assert m.calls == case["calls"]
+
+
+def test_choice_scoring_matches_the_whole_reference_stack(golden_dir):
+    """runtime.score_masked_continuation over the reference graph, three choices of one context
+    with the prefix cache reused (runtime.py:485-588, 546-548)."""
+    sc = json.loads((golden_dir / "model_decode.json").read_text())["scoring"]
+    m = LoggingOracle(make_oracle(pin_config(), pin_params("float32", PIN_MASK_ID), "float32"))
+    cached = None
+    for choice in sc["choices"]:
+        logits, cached = od.score_masked_continuation(m, sc["context"], choice["continuation"], block_size=32,
+                                                      mask_id=PIN_MASK_ID, eos_token_id=PIN_MASK_ID - 1,
+                                                      cached_prefix=cached)
+        assert od.loglikelihood(logits, choice["continuation"]) == pytest.approx(choice["loglik"], rel=1e-5, abs=1e-5)
+        assert [int(i) for i in logits.argmax(-1)] == choice["argmax"]
+    assert m.calls == sc["calls"]
