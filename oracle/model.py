@@ -26,10 +26,10 @@ agree for the 1.5B model (head_dim 128) and only the former keeps cached == dens
 
 Parity of this restatement is pinned against the reference's own model graph: model/cuda.py
 executed op by op through an eager stand-in of TVM's nn frontend, with the reference runtime's
-packed callbacks for the cached calls (tests/golden/make_model_golden.py).  In fp32 this module
-reproduces it bit for bit on the dense path and within 1e-5 on the cached path
-(tests/test_oracle_vs_reference_graph.py); in bf16 within a 2e-2 relative error per tensor, since
-the compiled module's fused rounding points cannot be executed here (TVM is absent).  It also
+packed callbacks for the cached calls (tests/golden/make_model_golden.py).  This module reproduces
+its dense path bit for bit in fp32 and bf16, and its cached path within 1e-5 in fp32 (2e-2
+relative in bf16, where the callback's CPU attention computes in bf16;
+tests/test_oracle_vs_reference_graph.py).  It also
 satisfies the reference's invariants (cached == dense, partial == full rows, tied == untied,
 sentinel windows; tests/test_oracle_invariants.py) and agrees with transformers'
 Qwen2ForCausalLM in fp32 (tests/test_oracle_vs_transformers.py).  The decode-loop restatement in

@@ -10,11 +10,13 @@ Semantics follow TVM's op definitions:
   compute in fp32 and round once, as TVM's bf16 legalisation does;
 * `matmul(a, b, out_dtype)` accumulates in fp32 and rounds once to `out_dtype` (default: a's);
 * `repeat` is numpy.repeat (each element repeated), `split` with a list splits at those indices;
-* `nn.Linear` is matmul(x, weight^T) then + bias, `nn.Embedding` is take(weight, ids, axis=0);
+* `nn.Linear` is matmul(x, weight^T) + bias accumulated in fp32 and rounded once: the reference's
+  production pipeline (model/cuda.py:31-60) hands matmul + bias to cuBLAS, whose bias epilogue
+  adds the bias before the single rounding; `nn.Embedding` is take(weight, ids, axis=0);
 * `call_inplace_packed` calls the registered global function with the in-place buffers (shared
   storage through DLPack) and returns what it returns.
-Where the compiled module fuses ops (for example a projection's bias into the cuBLAS epilogue),
-the rounding points in bf16 can differ from this eager order; in fp32 they cannot.
+Elementwise bf16 ops round after every op, as TVM's bf16 legalisation does even inside fused
+kernels; in fp32 none of these choices changes a result beyond summation order.
 """
 
 from __future__ import annotations
@@ -146,8 +148,13 @@ class Linear(Module):
         self.out_dtype = out_dtype
 
     def forward(self, x: Tensor) -> Tensor:
-        y = op.matmul(x, op.permute_dims(self.weight), out_dtype=self.out_dtype)
-        return op.add(y, self.bias) if self.bias is not None else y
+        if self.bias is None:
+            return op.matmul(x, op.permute_dims(self.weight), out_dtype=self.out_dtype)
+        xt, wt, bt = _raw(x), _raw(self.weight), _raw(self.bias)
+        _same(xt, wt, "linear")
+        _same(xt, bt, "linear bias")
+        out = _DT[self.out_dtype] if self.out_dtype else xt.dtype
+        return Tensor((torch.matmul(xt.float(), wt.float().t()) + bt.float()).to(out))
 
 
 class Embedding(Module):

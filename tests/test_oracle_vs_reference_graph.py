@@ -3,11 +3,13 @@ op by op (tests/golden/make_model_golden.py, fixture tests/golden/model_graph.np
 forward_hidden -> get_logits, build_prefix_cache, forward_cached and forward_block_partial_rp8,
 the cached calls through the reference runtime's own packed callbacks (runtime.py:46-73).
 
-fp32: the oracle reproduces the graph to 1e-5 (bit for bit on the dense path; the cached path's
-attention differs only in the summation order of the callback's SDPA).  bf16: the eager graph
-rounds after every op (a projection's bias is added after the matmul is rounded), whereas the
-compiled module fuses some of them, so the bf16 check is a 2e-2 relative error of each tensor and
-identical logit argmax, not a per-element bound.
+Dense path (forward_hidden, get_logits, build_prefix_cache): the oracle reproduces the graph bit
+for bit in fp32 and in bf16 (the stand-in rounds a projection once after its bias, as the
+reference's cuBLAS bias epilogue does); the bound checked is one rounding step.  Cached path: the
+reference's attention callback runs PyTorch SDPA on the CPU here, which sums in another order in
+fp32 (3.6e-6 measured, bound 1e-5) and computes in bf16 for bf16 inputs (0.8% relative error
+measured, bound 2e-2 per tensor), where the oracle keeps the softmax in fp32 as the model's dense
+path does.
 
 Decode: the reference's runtime.py driving that graph (tests/golden/model_decode.json) and the
 oracle's decode loop over the oracle produce the same tokens, statistics and entry-point calls.
@@ -56,19 +58,23 @@ def _oracle_outputs(dtype: str, g) -> dict[str, torch.Tensor]:
     return {key: t.float() for key, t in out.items()}
 
 
-KEYS = ["dense/h", "dense/logits", "prefill/k", "prefill/v", "cached/h", "cached/k", "cached/v", "partial/h",
-        "partial/k", "partial/v"]
+DENSE = ["dense/h", "dense/logits", "prefill/k", "prefill/v"]
+CACHED = ["cached/h", "cached/k", "cached/v", "partial/h", "partial/k", "partial/v"]
 
 
 def test_fp32_oracle_reproduces_the_reference_graph(graph):
     mine = _oracle_outputs("float32", graph)
-    for key in KEYS:
+    for key in DENSE:
+        torch.testing.assert_close(mine[key], _get(graph, "float32", key), rtol=1e-6, atol=1e-6, msg=key)
+    for key in CACHED:
         torch.testing.assert_close(mine[key], _get(graph, "float32", key), rtol=1e-5, atol=1e-5, msg=key)
 
 
-def test_bf16_oracle_agrees_with_the_reference_graph(graph):
+def test_bf16_oracle_reproduces_the_reference_graph(graph):
     mine = _oracle_outputs("bfloat16", graph)
-    for key in KEYS:
+    for key in DENSE:  # within one bf16 rounding step (bit for bit when measured)
+        torch.testing.assert_close(mine[key], _get(graph, "bfloat16", key), rtol=2 ** -7, atol=1e-6, msg=key)
+    for key in CACHED:
         ref = _get(graph, "bfloat16", key)
         rel = float((mine[key] - ref).norm() / ref.norm())
         assert rel <= 2e-2, f"{key}: relative error {rel:.4f}"
