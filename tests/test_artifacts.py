@@ -87,3 +87,32 @@ def test_runner_style_param_loading(tmp_path):
         arr = z["arr_1"]
         t = tvm.runtime.empty(arr.shape, "bfloat16", tvm.cpu(0)).copyfrom(arr)
     assert torch.equal(t.torch, params[1])
+
+
+def test_writer_matches_the_reference_exporter_byte_for_byte(tmp_path, golden_dir):
+    """tests/golden/artifact_format.json describes what the reference's own exporter writes for
+    the tiny bf16 weights (export_utils.remap_params fusing q/k/v and gate/up, np.savez in the
+    model's parameter order, the names, the dtype, write_kv_cache_manifest).  This package's
+    writer produces the same files, texts and arrays; the loader reads them back without the
+    config file the reference does not write."""
+    import hashlib
+    import json
+
+    import numpy as np
+
+    want = json.loads((golden_dir / "artifact_format.json").read_text())
+    params = make_synthetic_params(TINY, seed=0, dtype="bfloat16", mask_id=TINY_MASK_ID)
+    d = artifacts.write_artifact(tmp_path / "a", TINY, params, "bfloat16", library=tmp_path / "missing.so")
+    for f in ("fast_dllm_relax_nn_kv_cache.json", "fast_dllm_relax_nn_param_names.txt", "fast_dllm_relax_nn_dtype.txt"):
+        assert (d / f).read_text(encoding="utf-8") == want[f], f
+    with np.load(d / artifacts.PARAMS) as z:
+        got = [dict(name=k, shape=list(z[k].shape), dtype=str(z[k].dtype),
+                    sha256=hashlib.sha256(np.ascontiguousarray(z[k]).tobytes()).hexdigest()) for k in z.files]
+    assert got == want["arrays"]
+    assert set(want["files"]) <= {p.name for p in d.iterdir()}
+    (d / artifacts.CONFIG).unlink()  # as the reference exports it
+    cfg = artifacts.read_config(d)
+    assert (cfg.num_hidden_layers, cfg.hidden_size, cfg.num_attention_heads, cfg.num_key_value_heads,
+            cfg.head_dim, cfg.vocab_size) == (2, 256, 4, 2, 64, 1024)
+    loaded = artifacts.load_params(d, "cpu", cfg)
+    assert all(torch.equal(a, b) for a, b in zip(loaded, params))
