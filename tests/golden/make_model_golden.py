@@ -200,15 +200,26 @@ def make_decode() -> None:
              dict(name="unaligned_blockcache", prompt=p45, max_new_tokens=40, use_block_cache=True),
              dict(name="short_prompt_stateless", prompt=p20, max_new_tokens=20, use_block_cache=True)]
     out = {"mask_id": PIN_MASK_ID, "cases": []}
-    for case in cases:
+
+    def run_case(case):
         vm.backend.calls.clear()
         toks, stats = ref_rt.relax_greedy_generate(
             vm, params, dev, reshape, None, list(case["prompt"]), num_attention_heads=cfg.num_attention_heads,
-            max_new_tokens=case["max_new_tokens"], block_size=32, small_block_size=8, threshold=0.9,
-            temperature=0.0, top_p=0.95, use_block_cache=case["use_block_cache"], mask_id=PIN_MASK_ID,
-            stop_token=None, cache_spec=spec)
+            max_new_tokens=case["max_new_tokens"], block_size=32, small_block_size=8,
+            threshold=case.get("threshold", 0.9), temperature=0.0, top_p=0.95,
+            use_block_cache=case["use_block_cache"], mask_id=PIN_MASK_ID, stop_token=case.get("stop_token"),
+            cache_spec=spec, chunked_prefill=case.get("chunked_prefill", False))
         print(case["name"], len(toks), stats, flush=True)
         out["cases"].append(dict(case, tokens=[int(t) for t in toks], stats=stats, calls=list(vm.backend.calls)))
+
+    for case in cases:
+        run_case(case)
+    p96 = rng.integers(0, 500, 96).tolist()
+    run_case(dict(name="chunked_prefill", prompt=p96, max_new_tokens=33, use_block_cache=True, chunked_prefill=True))
+    first = out["cases"][1]["tokens"]  # stop on the first token that differs from the first one
+    run_case(dict(name="stop_token", prompt=p64, max_new_tokens=64, use_block_cache=True,
+                  stop_token=next(t for t in first if t != first[0])))
+    run_case(dict(name="low_threshold", prompt=p64, max_new_tokens=64, use_block_cache=True, threshold=0.0025))
     # masked-continuation scoring (runtime.py:485-588), the second and third choices reusing the
     # first one's prefix cache (runtime.py:546-548)
     ctx = rng.integers(0, 500, 70).tolist()

@@ -120,7 +120,7 @@ def test_scheduler_edge_cases_match_reference_runtime(name, engine, golden_dir):
 
 
 @pytest.mark.parametrize("name", ["aligned_nocache", "aligned_blockcache", "unaligned_blockcache",
-                                  "short_prompt_stateless"])
+                                  "short_prompt_stateless", "stop_token", "low_threshold"])
 def test_scheduler_matches_the_whole_reference_stack(name, golden_dir):
     """Decode runs of the reference's runtime driving the reference's own model graph
     (tests/golden/model_decode.json), reproduced by the scheduler over the pinned oracle."""
@@ -129,7 +129,8 @@ def test_scheduler_matches_the_whole_reference_stack(name, golden_dir):
     case = next(c for c in golden["cases"] if c["name"] == name)
     eng = OracleEngine(pin_config(), pin_params("float32", PIN_MASK_ID))
     toks, stats = generate_batch(eng, [case["prompt"]], max_new_tokens=case["max_new_tokens"], block_size=32,
-                                 small_block_size=8, threshold=0.9, use_block_cache=case["use_block_cache"],
-                                 mask_id=golden["mask_id"])
+                                 small_block_size=8, threshold=case.get("threshold", 0.9),
+                                 use_block_cache=case["use_block_cache"], mask_id=golden["mask_id"],
+                                 stop_token=case.get("stop_token"))
     assert toks[0] == case["tokens"]
     assert stats[0] == case["stats"]

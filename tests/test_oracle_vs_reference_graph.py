@@ -86,14 +86,16 @@ def test_fixture_records_which_reference_graph(graph):
 
 
 @pytest.mark.parametrize("name", ["aligned_nocache", "aligned_blockcache", "unaligned_blockcache",
-                                  "short_prompt_stateless"])
+                                  "short_prompt_stateless", "chunked_prefill", "stop_token", "low_threshold"])
 def test_decode_matches_the_whole_reference_stack(name, golden_dir):
     golden = json.loads((golden_dir / "model_decode.json").read_text())
     case = next(c for c in golden["cases"] if c["name"] == name)
     m = LoggingOracle(make_oracle(pin_config(), pin_params("float32", PIN_MASK_ID), "float32"))
     toks, stats = od.relax_greedy_generate(m, case["prompt"], max_new_tokens=case["max_new_tokens"], block_size=32,
-                                           small_block_size=8, threshold=0.9, use_block_cache=case["use_block_cache"],
-                                           mask_id=golden["mask_id"])
+                                           small_block_size=8, threshold=case.get("threshold", 0.9),
+                                           use_block_cache=case["use_block_cache"], mask_id=golden["mask_id"],
+                                           stop_token=case.get("stop_token"),
+                                           chunked_prefill=case.get("chunked_prefill", False))
     assert toks == case["tokens"]
     assert stats == case["stats"]
     assert m.calls == case["calls"]
