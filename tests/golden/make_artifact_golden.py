@@ -108,6 +108,14 @@ def main() -> None:
         export_utils.write_kv_cache_manifest(d, rcfg, dtype)
         desc = describe(d)
     desc["weights"] = "make_synthetic_params(TINY, seed=0, bfloat16, mask_id=1023)"
+    # the parameter list the reference's model class exports, tied and untied (the artifact's
+    # params.npz order; tests/test_tiny_compile.py:74-84 checks the same split)
+    desc["param_lists"] = {}
+    for tied in (True, False):
+        import dataclasses  # noqa: PLC0415
+        m = FastDLLMRelaxForCausalLM(dataclasses.replace(rcfg, tie_word_embeddings=tied), dtype=dtype,
+                                     fused_qkv=True, fused_gate_up=True)
+        desc["param_lists"]["tied" if tied else "untied"] = [[n, list(p._shape)] for n, p in m.named_parameters()]
     (HERE / "artifact_format.json").write_text(json.dumps(desc, indent=1) + "\n", encoding="utf-8")
     print(len(desc["arrays"]), "arrays;", desc["files"])
 

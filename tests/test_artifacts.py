@@ -116,3 +116,15 @@ def test_writer_matches_the_reference_exporter_byte_for_byte(tmp_path, golden_di
             cfg.head_dim, cfg.vocab_size) == (2, 256, 4, 2, 64, 1024)
     loaded = artifacts.load_params(d, "cpu", cfg)
     assert all(torch.equal(a, b) for a, b in zip(loaded, params))
+
+
+def test_param_lists_match_the_reference_model_tied_and_untied(golden_dir):
+    """param_names / param_shapes against the parameter list the reference's own model class
+    exports (tests/golden/artifact_format.json), for a tied and an untied lm_head."""
+    from fast_dllm_relax_b200.config import param_shapes
+
+    want = json.loads((golden_dir / "artifact_format.json").read_text())["param_lists"]
+    for tied in (True, False):
+        cfg = dataclasses.replace(TINY, tie_word_embeddings=tied)
+        got = [[n, list(s)] for n, s in zip(param_names(cfg), param_shapes(cfg))]
+        assert got == want["tied" if tied else "untied"]
