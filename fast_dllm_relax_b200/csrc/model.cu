@@ -207,6 +207,17 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
   return nt;
 }
 
+// kGemmTune* bits of every tcgen05 projection launch.  Default: epilogue prefetch, 2 weight k
+// blocks into L2 ahead of the ring (measured per 32-row step: 2 -1.3 %; 4 / 8 / 16 slower, their
+// traffic delays the latency-bound kernels before them).
+static int gemm_tune() {
+  static const int tune = [] {  // tuning override of the kGemmTune* bits
+    const char* v = std::getenv("FDLLM_GEMM_TUNE");
+    return v != nullptr ? std::atoi(v) : (kGemmTunePrefetch | (2 << kGemmTuneL2Shift));
+  }();
+  return tune;
+}
+
 // Kernel trace slot of the next launch (null when tracing is off, capturing, or full): one
 // [kKtraceMaxCta][kKtracePhases] record per launch, zeroed (= not reached) between reads.
 constexpr size_t kKtraceMax = 512;
@@ -249,13 +260,7 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
   }
   if (h->dtype == FDLLM_FLOAT32) return timed_launch(h, g, s, launch_simt_thunk, w.ptr, X, 0);
   g.ktrace = ktrace_slot(h, 100 + epi.kind + (post_out ? 1000 : 0) + (norm_w ? 2000 : 0));
-  static const int tune = [] {  // tuning override of the kGemmTune* bits
-    const char* v = std::getenv("FDLLM_GEMM_TUNE");
-    // default: epilogue prefetch, 2 weight k blocks into L2 ahead of the ring (measured per 32-row
-    // step: 2 -1.3 %; 4 / 8 / 16 slower, their traffic delays the latency-bound kernels before them)
-    return v != nullptr ? std::atoi(v) : (kGemmTunePrefetch | (2 << kGemmTuneL2Shift));
-  }();
-  g.tune = tune;
+  g.tune = gemm_tune();
   if (norm_w == nullptr && post_out == nullptr && use_persist(h, M)) {
     g.n_slabs = w.paired ? (g.N / 2) / 64 : g.N / 128;
     // 256-token tiles when they cover half the SMs, else 128 (twice the tiles for few-slab weights)
@@ -1149,7 +1154,26 @@ constexpr size_t kStaticConfFloats = size_t(1) << 20;  // 4 MiB
 __device__ __align__(256) float g_static_conf_part[kStaticConfFloats];
 constexpr int kMaxStaticDevices = 64;
 std::mutex g_static_mu;
+// The array's device address per device, and the CUDA context it was looked up in: after a
+// cudaDeviceReset (or any teardown of the primary context) the module is loaded again at another
+// address, so a changed context triggers a fresh lookup instead of reusing a stale pointer.
 float* g_static_conf_addr[kMaxStaticDevices] = {};
+CUcontext g_static_conf_ctx[kMaxStaticDevices] = {};
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+CUcontext current_context() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  CUcontext c = nullptr;
+  if (fn != nullptr && fn(&c) != CUDA_SUCCESS) c = nullptr;
+  return c;
+}
 }  // namespace
 
 extern "C" int fdllm_confidence_static(fdllm_handle* h, const void* hidden, int rows, int32_t* ids, float* maxp,
@@ -1166,12 +1190,15 @@ extern "C" int fdllm_confidence_static(fdllm_handle* h, const void* hidden, int 
   float* part = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_static_mu);
-    if (g_static_conf_addr[h->device] == nullptr) {  // first call on this device
-      void* p = nullptr;
-      cudaError_t e = cudaGetSymbolAddress(&p, g_static_conf_part);
+    // check_handle made h->device current; the runtime call below initialises its context if needed
+    void* p = nullptr;
+    const CUcontext ctx = current_context();
+    if (g_static_conf_addr[h->device] == nullptr || ctx == nullptr || ctx != g_static_conf_ctx[h->device]) {
+      cudaError_t e = cudaGetSymbolAddress(&p, g_static_conf_part);  // first call on this device / context
       if (e != cudaSuccess || p == nullptr)
         return fail(FDLLM_ERR_CUDA, std::string("cudaGetSymbolAddress(static confidence scratch): ") + cudaGetErrorString(e));
       g_static_conf_addr[h->device] = static_cast<float*>(p);
+      g_static_conf_ctx[h->device] = current_context();
     }
     part = g_static_conf_addr[h->device];
   }
@@ -1184,12 +1211,15 @@ extern "C" int fdllm_confidence_static(fdllm_handle* h, const void* hidden, int 
   const int nt = plan_gemm(h, h->lm, rows, &g);
   g.err = h->err.p;
   g.epi = e;
+  // The same launch path as fdllm_confidence (profiling counters, kernel trace, tuning bits).
   if (h->dtype == FDLLM_FLOAT32) {
-    CUDA_TRY(launch_gemm_simt_f32(g, static_cast<const float*>(h->lm.ptr), static_cast<const float*>(hidden), s));
+    FDLLM_TRY(timed_launch(h, g, s, launch_simt_thunk, h->lm.ptr, hidden, 0));
   } else {
+    g.ktrace = ktrace_slot(h, 100 + e.kind);
+    g.tune = gemm_tune();
     CUtensorMap tmB;
     FDLLM_TRY(make_map(&tmB, hidden, rows, g.K, nt));
-    CUDA_TRY(launch_gemm_tc(g, h->lm.map, tmB, nt, s));
+    FDLLM_TRY(timed_launch(h, g, s, launch_tc_thunk, &h->lm.map, &tmB, nt));
   }
   CUDA_TRY(launch_conf_combine(part, rows, n_slabs, ids, maxp, s));
   return FDLLM_OK;

@@ -219,10 +219,15 @@ class Engine:
     def confidence_static(self, hidden: torch.Tensor, ids: torch.Tensor, maxp: torch.Tensor) -> None:
         """confidence() into caller-owned ids / maxp through fdllm_confidence_static, which
         allocates no device memory (its scratch is a fixed 4 MiB device array per device)."""
+        # The kernel writes ids / maxp through raw pointers: a host tensor, a tensor on another GPU or
+        # a strided view would be written at the wrong addresses, so refuse them before any launch.
+        for t, dt, name in ((ids, torch.int32, "ids"), (maxp, torch.float32, "maxp")):
+            if t.device != self.device or t.dtype != dt or not t.is_contiguous():
+                raise ValueError(f"confidence_static: {name} must be a contiguous {dt} tensor on {self.device}")
         h2 = self._act(hidden, "confidence_static")
         n = h2.shape[0]
-        if ids.numel() < n or maxp.numel() < n or ids.dtype != torch.int32 or maxp.dtype != torch.float32:
-            raise ValueError("confidence_static: ids int32 and maxp float32 with at least rows elements")
+        if ids.numel() < n or maxp.numel() < n:
+            raise ValueError("confidence_static: ids and maxp need at least rows elements")
         _lib.check(self.lib.fdllm_confidence_static(self._h, h2.data_ptr(), n, ids.data_ptr(), maxp.data_ptr(),
                                                     self._stream()))
 

@@ -213,7 +213,10 @@ FDLLM_API int fdllm_kernel_trace_read(fdllm_handle* h, uint64_t* out, int32_t* k
  * on that device, so rows must satisfy rows * ceil(vocab / 128) * 16 <= 4 MiB (220 rows at vocab
  * 151936); larger calls return FDLLM_ERR_INVALID with the limit in fdllm_last_error.
  * - The first call on each device looks up the array's address (cudaGetSymbolAddress, which may
- *   load the module); make that first call before any stream capture.
+ *   load the module); make that first call before any stream capture.  The address is kept per
+ *   device together with the CUDA context it belongs to; a call made after that context was torn
+ *   down and recreated (cudaDeviceReset) looks it up again, so that call too belongs before any
+ *   capture.
  * - The array keeps the previous call's contents; nothing in it needs to start at zero, because
  *   every entry a call reads is written earlier in that same call.
  * - Calls whose kernels can overlap on one device (different streams, or different handles on the

@@ -99,3 +99,15 @@ def pin_params(dtype: str, mask_id: int | None = None):
             p = 1.0 + 0.1 * torch.randn(p.shape, generator=g)
         out.append(p.to({"float32": torch.float32, "bfloat16": torch.bfloat16}[dtype]))
     return out
+
+
+def assert_close_rel(got, ref, rtol: float, msg: str = "") -> None:
+    """Element-wise |got - ref| <= rtol * |ref| + rtol * rms(ref): the stated relative tolerance per
+    element, with an absolute floor of rtol times the tensor's RMS for elements near zero, where a
+    purely relative bound is undefined (a value that rounds to 1e-5 in one order of summation and
+    to 2e-5 in another differs by 100% relative)."""
+    import torch
+
+    g, r = got.float().cpu(), ref.float().cpu()
+    rms = float(r.pow(2).mean().sqrt())
+    torch.testing.assert_close(g, r, rtol=rtol, atol=rtol * rms, msg=lambda m: f"{msg}: {m}" if msg else m)

@@ -50,3 +50,26 @@ def test_cache_validation_rejects_bad_layouts():
     k, v = eng.new_cache(64)
     with pytest.raises(ValueError, match="contiguous"):
         eng._cache(k.transpose(3, 4).contiguous().transpose(3, 4), v)
+
+
+def test_confidence_static_rejects_outputs_it_cannot_write():
+    """The allocation-free confidence writes ids / maxp through raw device pointers, so host
+    tensors, tensors on another device, strided views and wrong dtypes are refused before any
+    library call (the shell's device is cuda:0; nothing is launched)."""
+    eng = _shell()
+    eng.device, eng.dtype = torch.device("cuda", 0), torch.bfloat16
+    h = torch.empty((4, TINY.hidden_size), dtype=torch.bfloat16)
+    ids, maxp = torch.empty(4, dtype=torch.int32), torch.empty(4, dtype=torch.float32)
+    with pytest.raises(ValueError, match="ids must be a contiguous torch.int32 tensor on cuda:0"):
+        eng.confidence_static(h, ids, maxp)  # host ids
+    meta_ids = torch.empty(4, dtype=torch.int32, device="meta")
+    with pytest.raises(ValueError, match="ids must be"):
+        eng.confidence_static(h, meta_ids, maxp)  # another device
+    eng.device = torch.device("cpu")  # a shell whose device the CPU tensors match: layout checks
+    eng.dtype = torch.bfloat16
+    with pytest.raises(ValueError, match="ids must be"):
+        eng.confidence_static(h, torch.empty(8, dtype=torch.int32)[::2], maxp)  # strided view
+    with pytest.raises(ValueError, match="maxp must be"):
+        eng.confidence_static(h, ids, torch.empty(4, dtype=torch.float64))  # wrong dtype
+    with pytest.raises(ValueError, match="at least rows elements"):
+        eng.confidence_static(h, ids[:2], maxp)  # too short

@@ -2,8 +2,10 @@
 tests/golden/make_model_golden.py: model/cuda.py run op by op, and runtime.py driving it), on the
 small head_dim-128 architecture with 2 query heads per KV head and random norm weights.
 
-Entry points (fp32 within 1e-4, the stated fp32 tolerance; bf16 within a 2e-2 relative error per
-tensor) and the native decode driver in fp32 (identical tokens and step statistics)."""
+Entry points: fp32 within 1e-4, the stated fp32 tolerance; bf16 element-wise within rtol 2e-2
+(near-zero elements within 2e-2 of the tensor's RMS) on the dense path, and on the cached path
+against the oracle (the recorded cached vectors carry a CPU bf16 attention; see below).  The
+native decode driver in fp32: identical tokens and step statistics."""
 
 import json
 
@@ -12,7 +14,7 @@ import pytest
 import torch
 
 from oracle.model import build_block_bias
-from tests._oracle_util import PIN_MASK_ID, pin_config, pin_params
+from tests._oracle_util import PIN_MASK_ID, assert_close_rel, make_oracle, pin_config, pin_params
 
 pytestmark = pytest.mark.gpu
 
@@ -28,6 +30,21 @@ def _get(g, dtype, key) -> torch.Tensor:
     if a.dtype == np.uint16:
         return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).float()
     return torch.from_numpy(a)
+
+
+def _oracle_cached(g, dtype) -> dict:
+    """The oracle's cached-path outputs on the golden's inputs (CPU), keyed like the golden."""
+    orc = make_oracle(pin_config(), pin_params(dtype), dtype)
+    x = orc.embed(torch.from_numpy(g[f"{dtype}/ids"]))[None]
+    x8 = orc.embed(torch.from_numpy(g[f"{dtype}/ids8"]))[None]
+    shape = (2, 1, P + B, 1, 128)
+    k, v = torch.zeros(shape, dtype=orc.dtype), torch.zeros(shape, dtype=orc.dtype)
+    orc.build_prefix_cache(x[:, :P], build_block_bias(0, P, B), k, v)
+    out = {"cached/h": orc.forward_cached(x[:, P:], k, v, P, P)[0]}
+    out["cached/k"], out["cached/v"] = k[-1, 0, P:P + B].clone(), v[-1, 0, P:P + B].clone()
+    out["partial/h"] = orc.forward_block_partial(x8, k, v, P + RP, P, RP)[0]
+    out["partial/k"], out["partial/v"] = k[-1, 0, P + RP:P + RP + S].clone(), v[-1, 0, P + RP:P + RP + S].clone()
+    return out
 
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
@@ -49,13 +66,24 @@ def test_entry_points_match_the_reference_graph(dtype, golden_dir):
     mine["partial/k"], mine["partial/v"] = k[-1, 0, P + RP:P + RP + S].clone(), v[-1, 0, P + RP:P + RP + S].clone()
     torch.cuda.synchronize()
     assert eng.device_error() == 0
+    orc = _oracle_cached(g, dtype) if dtype == "bfloat16" else {}
     for key, val in mine.items():
         got, ref = val.float().cpu(), _get(g, dtype, key)
         if dtype == "float32":
             torch.testing.assert_close(got, ref, rtol=1e-4, atol=1e-4, msg=key)
+        elif key.startswith(("dense/", "prefill/")):
+            # element-wise rtol 2e-2 (floor: 2e-2 of the tensor's RMS for near-zero elements)
+            assert_close_rel(got, ref, 2e-2, key)
         else:
+            # The recorded bf16 cached-path vectors carry the reference callback's attention as it
+            # ran where they were made: PyTorch SDPA on the CPU in bf16 (runtime.py:30-48; flash_attn
+            # needs a GPU), 0.8% relative error against fp32 softmax.  Element-wise, the cached path
+            # is held to the oracle on the same inputs (its dense path is the reference graph bit
+            # for bit, and its cached attention is that same fp32 softmax); against the recorded
+            # vectors, to a 2e-2 relative error per tensor.
+            assert_close_rel(got, orc[key], 2e-2, f"{key} vs oracle")
             rel = float((got - ref).norm() / ref.norm())
-            assert rel <= 2e-2, f"{key}: relative error {rel:.4f}"
+            assert rel <= 2e-2, f"{key}: relative error {rel:.4f} against the reference graph"
 
 
 @pytest.mark.parametrize("name", ["aligned_nocache", "aligned_blockcache", "unaligned_blockcache", "stop_token",
