@@ -13,7 +13,7 @@ import torch
 
 from fast_dllm_relax_b200.config import ModelConfig, make_synthetic_params
 from oracle.model import build_block_bias
-from tests._oracle_util import assert_close_rel, make_oracle
+from tests._oracle_util import assert_close_rel, assert_within_bf16_noise, make_oracle, make_reordered_oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -32,7 +32,7 @@ def mid():
     from fast_dllm_relax_b200.engine import Engine
     params = make_synthetic_params(MID, seed=7, dtype="bfloat16", mask_id=MASK)
     eng = Engine(MID, [p.to(_dev()) for p in params], dtype="bfloat16")
-    return eng, make_oracle(MID, params, "bfloat16")
+    return eng, make_oracle(MID, params, "bfloat16"), make_reordered_oracle(MID, params, "bfloat16")
 
 
 def _act(n, seed):
@@ -45,7 +45,7 @@ def _close(a, b, label=""):
 
 
 def test_long_prefix_matches_oracle(mid):
-    eng, orc = mid
+    eng, orc, alt = mid
     P = 1024
     prefix, block = _act(P, 1), _act(32, 2)
     k, v = eng.new_cache(P + 32)
@@ -65,72 +65,101 @@ def test_long_prefix_4096_matches_oracle(mid):
     """configs[3]'s prefix length against the oracle: build_prefix_cache at P = 4096 (K/V of both
     layers), the 32-row cached forward and an rp16 partial over the 4128-key window, plus the
     size-independent invariant cached == dense."""
-    eng, orc = mid
+    eng, orc, alt = mid
     P = 4096
     seq = _act(P + 32, 3)
     k, v = eng.new_cache(P + 32)
     eng.build_prefix_cache(seq[:, :P].contiguous().to(_dev()), None, k, v)
     kr, vr = torch.zeros(k.shape, dtype=k.dtype), torch.zeros(v.shape, dtype=v.dtype)
+    ka, va = torch.zeros_like(kr), torch.zeros_like(vr)
     orc.build_prefix_cache(seq[:, :P].contiguous(), build_block_bias(0, P, 32), kr, vr)
-    assert_close_rel(k[:, :, :P], kr[:, :, :P], 2e-2, "prefix k at P=4096")
-    assert_close_rel(v[:, :, :P], vr[:, :, :P], 2e-2, "prefix v at P=4096")
+    alt.build_prefix_cache(seq[:, :P].contiguous(), build_block_bias(0, P, 32), ka, va)
+    assert_within_bf16_noise(k[:, :, :P], kr[:, :, :P], ka[:, :, :P], "prefix k at P=4096")
+    assert_within_bf16_noise(v[:, :, :P], vr[:, :, :P], va[:, :, :P], "prefix v at P=4096")
     cached = eng.forward_cached(seq[:, P:].contiguous().to(_dev()), k, v, P, P)
-    assert_close_rel(cached, orc.forward_cached(seq[:, P:].contiguous(), kr, vr, P, P), 2e-2,
-                     "forward_cached at P=4096")
+    x = seq[:, P:].contiguous()
+    assert_within_bf16_noise(cached, orc.forward_cached(x, kr, vr, P, P), alt.forward_cached(x, ka, va, P, P),
+                             "forward_cached at P=4096")
     x8 = _act(8, 40)
     hp = eng.forward_block_partial(x8.to(_dev()), k, v, P + 16, P, 16)
-    assert_close_rel(hp, orc.forward_block_partial(x8, kr, vr, P + 16, P, 16), 2e-2, "rp16 at P=4096")
+    assert_within_bf16_noise(hp, orc.forward_block_partial(x8, kr, vr, P + 16, P, 16),
+                             alt.forward_block_partial(x8, ka, va, P + 16, P, 16), "rp16 at P=4096")
     dense = eng.forward_hidden(seq.to(_dev()), None)[:, P:]  # implicit block-causal mask
     assert_close_rel(cached, dense, 2e-2, "cached vs dense at P=4096")
     assert eng.device_error() == 0
 
 
+def _consistent(a, b, label):
+    """Two GPU plans of the same forward (different token tiles and split-K depths, so their fp32
+    sums run in another order): an occasional bf16 rounding flips and propagates through the next
+    layer, so this self-consistency check (not the parity criterion, which is against the oracle)
+    asks for 99.9% of the elements within the stated tolerance and the rest within twice its floor."""
+    a, b = a.float().cpu(), b.float().cpu()
+    floor = 2e-2 * float(b.pow(2).mean().sqrt())
+    err = (a - b).abs()
+    assert (err <= 2e-2 * b.abs() + floor).float().mean() >= 0.999, label
+    assert float(err.max()) <= 2 * floor, label
+
+
 @pytest.mark.parametrize("n_req,prefix", [(8, 1024), (32, 96)])
-def test_batched_requests_match_single(mid, n_req, prefix):
-    """configs[3] (batch 8, long prefixes) and configs[2] (32 requests = 1024 rows)."""
-    eng, orc = mid
-    reqs, xs, singles = [], [], []
+def test_batched_requests_match_oracle(mid, n_req, prefix):
+    """configs[3] (batch 8, long prefixes) and configs[2] (32 requests = 1024 rows): every request's
+    slice of one batched forward against the oracle (the stated tolerance), and against the same
+    request run alone on the GPU (self-consistency)."""
+    eng, orc, alt = mid
+    reqs, xs, singles, refs = [], [], [], []
     g = torch.Generator().manual_seed(n_req)
     for i in range(n_req):
         P = prefix + 32 * int(torch.randint(0, 3, (1,), generator=g))
         k, v = eng.new_cache(P + 32)
-        eng.build_prefix_cache(_act(P, 100 + i).to(_dev()), None, k, v)
-        x = _act(32, 200 + i).to(_dev())
+        pre, x = _act(P, 100 + i), _act(32, 200 + i)
+        eng.build_prefix_cache(pre.to(_dev()), None, k, v)
+        kr, vr = torch.zeros(k.shape, dtype=k.dtype), torch.zeros(v.shape, dtype=v.dtype)
+        ka, va = torch.zeros_like(kr), torch.zeros_like(vr)
+        orc.build_prefix_cache(pre, build_block_bias(0, P, 32), kr, vr)
+        alt.build_prefix_cache(pre, build_block_bias(0, P, 32), ka, va)
+        refs.append((orc.forward_cached(x, kr, vr, P, P)[0], kr, alt.forward_cached(x, ka, va, P, P)[0], ka))
         ks, vs = k.clone(), v.clone()
-        singles.append((eng.forward_cached(x, ks, vs, P, P)[0], ks, vs))
-        xs.append(x[0])
+        singles.append((eng.forward_cached(x.to(_dev()), ks, vs, P, P)[0], ks, vs))
+        xs.append(x[0].to(_dev()))
         reqs.append(dict(k=k, v=v, rows=32, prefix_len=P))
     out = eng.forward_cached_batch(torch.cat(xs), reqs)
-    # 32- and 1024-row calls use different token tiles and split-K plans, so their fp32 sums run in
-    # a different order and an occasional bf16 rounding flips, then propagates through the next
-    # layer: nearly all elements agree within the bf16 tolerance, the rest within two ulps.
-    for i, (r, (hs, ks, vs)) in enumerate(zip(reqs, singles)):
-        assert_close_rel(out[32 * i:32 * (i + 1)], hs, 2e-2, f"request {i}")
-        assert_close_rel(r["k"], ks, 2e-2, f"request {i} k")
+    for i, (r, (hs, ks, _), (hr, kr, ha, ka)) in enumerate(zip(reqs, singles, refs)):
+        assert_within_bf16_noise(out[32 * i:32 * (i + 1)], hr, ha, f"request {i} vs oracle")
+        assert_within_bf16_noise(r["k"], kr, ka, f"request {i} k vs oracle")
+        _consistent(out[32 * i:32 * (i + 1)], hs, f"request {i} batched vs alone")
     assert eng.device_error() == 0
 
 
 def test_batched_prefix_build_matches_single(mid):
     """fdllm_build_prefix_cache_batch == one build_prefix_cache per request (ragged prefixes, the
     block-causal mask inside each request), up to the bf16 rounding of the larger GEMM tiles."""
-    eng, _ = mid
+    eng, orc, alt = mid
     lens = [96, 160, 64, 224]
     xs = [_act(P, 300 + i).to(_dev()) for i, P in enumerate(lens)]
+    refs = []
+    for x, P in zip(xs, lens):  # the oracle's and the reordered oracle's caches of each prefix
+        shape = (MID.num_hidden_layers, 1, P + 32, MID.num_key_value_heads, MID.head_dim)
+        c = [torch.zeros(shape, dtype=torch.bfloat16) for _ in range(4)]
+        orc.build_prefix_cache(x.cpu(), build_block_bias(0, P, 32), c[0], c[1])
+        alt.build_prefix_cache(x.cpu(), build_block_bias(0, P, 32), c[2], c[3])
+        refs.append(c)
     batched = [eng.new_cache(P + 32) for P in lens]
     single = [eng.new_cache(P + 32) for P in lens]
     eng.build_prefix_cache_batch(torch.cat([x[0] for x in xs]), batched, lens)
     for x, (k, v) in zip(xs, single):
         eng.build_prefix_cache(x, None, k, v)
     for i, (P, (kb, vb), (ks, vs)) in enumerate(zip(lens, batched, single)):
-        for a, b, name in ((kb, ks, "k"), (vb, vs, "v")):
-            assert_close_rel(a[:, :, :P], b[:, :, :P], 2e-2, f"request {i} {name}")
+        for a, b, r, n, name in ((kb, ks, refs[i][0], refs[i][2], "k"), (vb, vs, refs[i][1], refs[i][3], "v")):
+            assert_within_bf16_noise(a[:, :, :P], r[:, :, :P], n[:, :, :P], f"request {i} {name} vs oracle")
+            _consistent(a[:, :, :P], b[:, :, :P], f"request {i} {name} batched vs alone")
     assert eng.device_error() == 0
 
 
 def test_masked_continuation_scoring(mid):
     """context 512, continuation 16 in a masked 32-row block (eos at row 16, pad
     masks after), log-softmax gathered on the device, batch 4."""
-    eng, orc = mid
+    eng, orc, alt = mid
     B, C, N = 4, 512, 16
     g = torch.Generator().manual_seed(5)
     reqs, xs, targets, refs = [], [], [], []

@@ -102,3 +102,27 @@ def test_tied_logits_equal_untied_with_the_same_array():
     mu = make_oracle(untied_cfg, untied, "float32")
     h = _rand(32, torch.float32, 6)
     assert torch.equal(mt.get_logits(h), mu.get_logits(h))
+
+
+def test_reordered_oracle_is_the_same_graph():
+    """The noise-floor model the bf16 GPU parity tests measure against (split-K sums,
+    flash-attention arithmetic) computes the same graph: in fp32 it equals the oracle within fp32
+    rounding (1e-5) on the dense, prefill and cached paths."""
+    import torch
+
+    from fast_dllm_relax_b200.config import TINY, TINY_MASK_ID, make_synthetic_params
+    from oracle.model import build_block_bias
+    from tests._oracle_util import make_oracle, make_reordered_oracle
+
+    params = make_synthetic_params(TINY, seed=0, dtype="float32", mask_id=TINY_MASK_ID)
+    a, b = make_oracle(TINY, params, "float32"), make_reordered_oracle(TINY, params, "float32")
+    x = torch.randn((1, 96, TINY.hidden_size), generator=torch.Generator().manual_seed(1))
+    bias = build_block_bias(0, 96, 32)
+    torch.testing.assert_close(b.forward_hidden(x, bias), a.forward_hidden(x, bias), rtol=1e-5, atol=1e-5)
+    shape = (TINY.num_hidden_layers, 1, 128, TINY.num_key_value_heads, TINY.head_dim)
+    (ka, va), (kb, vb) = [(torch.zeros(shape), torch.zeros(shape)) for _ in range(2)]
+    a.build_prefix_cache(x[:, :64], build_block_bias(0, 64, 32), ka, va)
+    b.build_prefix_cache(x[:, :64], build_block_bias(0, 64, 32), kb, vb)
+    torch.testing.assert_close(kb, ka, rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(b.forward_cached(x[:, 64:], kb, vb, 64, 64), a.forward_cached(x[:, 64:], ka, va, 64, 64),
+                               rtol=1e-5, atol=1e-5)
