@@ -22,7 +22,7 @@ FDLLM_ERR_DEVICE = -5
 DEVICE_ERRORS = {
     0: "none", 1: "TMA producer wait expired", 2: "MMA issuer wait expired", 3: "epilogue wait expired",
     4: "token id outside the vocabulary", 5: "RoPE position outside the table", 6: "KV write outside the cache",
-    7: "bounded-wait self test expired", 8: "layer-stack grid barrier or merge wait expired",
+    7: "bounded-wait self test expired", 8: "(no longer raised)",
     9: "device refinement loop exceeded its iteration limit",
 }
 
@@ -64,8 +64,6 @@ SIGNATURES: dict[str, tuple] = {
     "fdllm_confidence": (_I, [_P, _P, _I, _P, _P, _P]),
     "fdllm_confidence_from_logits": (_I, [_P, _P, _I, _P, _P, _P]),
     "fdllm_confidence_static": (_I, [_P, _P, _I, _P, _P, _P]),
-    "fdllm_stack_trace_enable": (_I, [_P, _I]),
-    "fdllm_stack_trace_read": (_I, [_P, _P, ctypes.c_longlong, ctypes.POINTER(_I), ctypes.POINTER(_I)]),
     "fdllm_kernel_trace_enable": (_I, [_P, _I]),
     "fdllm_kernel_trace_read": (_I, [_P, _P, _P, _I, ctypes.POINTER(_I)]),
     "fdllm_unmask": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, ctypes.c_double, _P, _P, _P, _P, _P]),

@@ -23,7 +23,7 @@ enum DeviceError : int {
   kErrPositionRange = 5,     // a RoPE position outside the precomputed table
   kErrCacheRange = 6,        // a KV write outside the cache capacity
   kErrTimeoutTest = 7,       // the bounded-wait self test expired (expected in that test)
-  kErrTimeoutBarrier = 8,    // the layer-stack kernel waited too long at a grid barrier or merge
+  kErrReserved8 = 8,         // no longer raised (kept so that codes keep their meaning)
   kErrLoopLimit = 9,         // a device-side refinement loop exceeded its iteration limit
 };
 

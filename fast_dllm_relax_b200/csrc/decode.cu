@@ -442,9 +442,8 @@ extern "C" int fdllm_generate(fdllm_handle* h, const int32_t* prompt, int prompt
   CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));  // the caller's prior work is done
   Driver d{h, nullptr, block_size, small_block_size, mask_id, stop_token, threshold, use_block_cache != 0};
   // device-side block loops: without a stop token (checked on the host between steps) and without
-  // per-launch profiling events; FDLLM_BLOCK_GRAPH=0 turns them off
-  const char* bgv = std::getenv("FDLLM_BLOCK_GRAPH");
-  const bool use_block_graph = stop_token < 0 && !h->prof && (bgv == nullptr || bgv[0] != '0');
+  // per-launch profiling events; tuning block_graph=0 turns them off
+  const bool use_block_graph = stop_token < 0 && !h->prof && h->tune.block_graph != 0;
   const int bs = block_size, sbs = small_block_size;
   std::vector<int> gen(prompt, prompt + prompt_len);
   const size_t n0 = gen.size();

@@ -14,14 +14,6 @@ static std::atomic<long long> g_launches{0};
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
-bool pdl_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("FDLLM_PDL");
-    return !(v != nullptr && v[0] == '0');
-  }();
-  return on;
-}
-
 // ---- embed (model/cuda.py:698-699) ----------------------------------------------------------
 template <typename T>
 __global__ void embed_kernel(const int* __restrict__ ids, const T* __restrict__ table, int vocab, int hidden,

@@ -277,7 +277,6 @@ __global__ void __launch_bounds__(128, 4)
   tc_fence_after_sync();
   __syncthreads();  // the producer's drain is complete before the ring is overwritten
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-  int row0 = lr0, row1 = lr1;  // rows of the last chunk this CTA finished (the only chunk when NT <= 64)
   for (int ch = 0; ch < NT / C::kChunk; ++ch) {
     const int cb = ch * C::kChunk;
     if (ch > 0) {  // the previous chunk is consumed (its epilogue, and the peers' reads of it)
@@ -340,92 +339,18 @@ __global__ void __launch_bounds__(128, 4)
       // only before leaving, so the closing barrier overlaps the epilogue.
       if (ch == NT / C::kChunk - 1) cluster_arrive();
     }
-    row0 = cb + lr0;
-    row1 = cb + lr1;
     // acc holds token columns [cb, cb + kChunk); the epilogue indexes it as the whole tile
-    gemm_epilogue<bf16>(g, acc - static_cast<size_t>(cb) * 128, NT, tok0, slab, S > 1 ? row0 : cb,
-                        S > 1 ? row1 : cb + C::kChunk, s_epi, static_cast<int>(threadIdx.x),
+    gemm_epilogue<bf16>(g, acc - static_cast<size_t>(cb) * 128, NT, tok0, slab, S > 1 ? cb + lr0 : cb,
+                        S > 1 ? cb + lr1 : cb + C::kChunk, s_epi, static_cast<int>(threadIdx.x),
                         static_cast<int>(blockDim.x), 0, NT <= 64 ? &pre : nullptr);
   }
   if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 5);
-  if (S == 1) {
-    row0 = 0;
-    row1 = NT;
-  }
 
-  // ---------------- post-norm: the next RMSNorm, by the last CTA of each token-row group ----------
-  // Every slab's cluster member of rank r owns the same rows [row0, row1) of this token tile, so
-  // the n_slabs CTAs of one (tile, rank) together complete those rows; the last to arrive
-  // normalises them (model/cuda.py:269-275) with the row statistics the residual epilogues left.
-  if (g.post_out != nullptr) {
-    __shared__ int s_last;
-    const int rank = g.splits > 1 ? static_cast<int>(cluster_ctarank()) : 0;
-    __syncthreads();  // this CTA's residual and statistics stores are issued
-    if (threadIdx.x == 0) {
-      __threadfence();
-      unsigned* ctr = g.post_ctr + tile * 16 + rank;
-      const unsigned old = atomicAdd(ctr, 1u);
-      s_last = (old == static_cast<unsigned>(g.n_slabs) - 1u) ? 1 : 0;
-      if (s_last) {
-        __threadfence();
-        *ctr = 0u;  // the last arrival: nobody else touches this counter in this launch
-      }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 6);
-    if (s_last) {
-      const int H = g.N;
-      const int n_ss = g.epi.ss_ld;
-      const bf16* hsrc = static_cast<const bf16*>(g.epi.resid);
-      const bf16* w = static_cast<const bf16*>(g.post_w);
-      bf16* out = static_cast<bf16*>(g.post_out);
-      float* rs = reinterpret_cast<float*>(s_epi);  // rows of this group
-      for (int t = row0 + threadIdx.x; t < row1; t += blockDim.x) {
-        const int tok = tok0 + t;
-        const float ss = tok < g.M ? sum_row_ss<true>(g.epi.ss_out + static_cast<size_t>(tok) * n_ss, n_ss) : 0.f;
-        rs[t - row0] = rsqrtf(ss / static_cast<float>(H) + g.norm_eps);
-      }
-      __syncthreads();
-      const int cpr = H / 8;
-      constexpr int kPB = 5;  // chunks per thread and batch: one batch for 3 rows of 1536 features
-      for (int c0 = threadIdx.x; c0 < (row1 - row0) * cpr; c0 += blockDim.x * kPB) {
-        uint4 xv[kPB], wv[kPB];
-#pragma unroll
-        for (int b = 0; b < kPB; ++b) {  // loads first
-          const int c = c0 + b * blockDim.x;
-          const int t = row0 + c / cpr, col = (c % cpr) * 8;
-          if (c < (row1 - row0) * cpr && tok0 + t < g.M) {
-            xv[b] = __ldcg(reinterpret_cast<const uint4*>(hsrc + static_cast<size_t>(tok0 + t) * H + col));
-            wv[b] = *reinterpret_cast<const uint4*>(w + col);
-          }
-        }
-#pragma unroll
-        for (int b = 0; b < kPB; ++b) {
-          const int c = c0 + b * blockDim.x;
-          const int t = row0 + c / cpr, col = (c % cpr) * 8;
-          if (c >= (row1 - row0) * cpr || tok0 + t >= g.M) continue;
-          const float r = rs[t - row0];
-          const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv[b]);
-          const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv[b]);
-          uint4 o;
-          __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const float2 xf = __bfloat1622float2(x2[v]);
-            const float2 wf = __bfloat1622float2(w2[v]);
-            const float2 xn = round2_bf16(xf.x * r, xf.y * r);
-            o2[v] = __floats2bfloat162_rn(wf.x * xn.x, wf.y * xn.y);
-          }
-          *reinterpret_cast<uint4*>(out + static_cast<size_t>(tok0 + t) * H + col) = o;
-        }
-      }
-    }
-  }
   if (S > 1) cluster_wait();  // no member leaves while another may still read its shared memory
   if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 7);
 }
 
-// ---- persistent variant for large token counts (M >= 256 rows, no split-K) ------------------------
+// ---- persistent variant for large token counts (prefill, batched serving) --------------------------
 // One CTA per SM walks its tiles (slab-major: neighbouring CTAs share a weight slab in L2) with
 // three roles: warp 0 issues TMA for every tile's k blocks through a 4-stage ring, warp 1 issues
 // tcgen05.mma into one of two TMEM accumulators (2 x 256 columns: the whole TMEM), warps 2-9 drain

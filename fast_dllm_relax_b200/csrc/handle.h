@@ -28,6 +28,23 @@ int fail(int code, const std::string& msg);
     if (_r != FDLLM_OK) return _r; \
   } while (0)
 
+// ---- tuning --------------------------------------------------------------------------------
+// Parameters of the kernel plans, fixed per handle at fdllm_create.  The defaults are the
+// measured best on B200; the environment variable FDLLM_TUNING ("key=value,...", read by
+// fdllm_create) overrides them for experiments without rebuilding.
+struct Tuning {
+  int nt_max = 256;            // largest token tile of the per-tile projection GEMM: 64, 128 or 256
+  int split_target = 0;        // CTAs per SM the split-K plan aims for (0: 2 at <= 16 rows, else 1)
+  int split_max = 16;          // largest split-K cluster of the per-tile GEMM
+  int gemm_tune = kGemmTunePrefetch | (2 << kGemmTuneL2Shift);  // kGemmTune* bits
+  int persist_min_rows = 256;  // token rows from which projections run on the persistent GEMM (0: never)
+  int persist_splitk = 0;      // split K inside the persistent GEMM while its tiles leave SMs idle
+  int attn_splits = 0;         // attention key splits of decode-sized calls (0: planned)
+  int gu_fused_rows = 16;      // gate_up normalises its own B tiles up to this many token rows
+  int block_graph = 1;         // fdllm_generate runs whole blocks as device-looped CUDA graphs
+};
+int parse_tuning(const char* spec, Tuning* t);
+
 // ---- handle ------------------------------------------------------------------------------
 struct Weight {
   const void* ptr = nullptr;
@@ -135,6 +152,7 @@ struct fdllm_handle {
   size_t esz = 2;
   int num_sms = 148;
   bool bound = false;
+  fdllm::Tuning tune;
   std::mutex mu;
 
   const void* embed = nullptr;
@@ -150,17 +168,8 @@ struct fdllm_handle {
   DevBuf<int> tok_req, tok_pos, tok_row, tmp_ids, targets;
   DevBuf<ReqDesc> reqs;
   DevBuf<float> conf_part, tmp_maxp, ss;  // ss: per-slab row sums of squares
-  DevBuf<unsigned> post_ctr;                // post-norm arrival counters (zero between launches)
   DevBuf<float> persist_part;               // persistent-GEMM split-K partial tiles
   DevBuf<unsigned> persist_ctr;             // persistent-GEMM per-tile split counters (zero between launches)
-  // persistent layer-stack kernel: weight maps and per-layer pointers (built at bind), partials,
-  // barrier / arrival counters (zeroed before every launch)
-  DevBuf<uint8_t> stack_maps, stack_layers;
-  DevBuf<float> stack_gpart, stack_apart, stack_alse;
-  DevBuf<unsigned> stack_sync;
-  bool stack_trace_on = false;            // fdllm_stack_trace_enable
-  DevBuf<unsigned long long> stack_trace; // per-CTA phase timeline of the last layer-stack launch
-  int stack_trace_grid = 0;
   // kernel trace (fdllm_kernel_trace_enable / _read): phase stamps of every projection and
   // attention launch issued outside stream capture while enabled, 8 per launch, and their kinds
   bool ktrace_on = false;
@@ -189,10 +198,6 @@ int check_handle(fdllm_handle* h);
 int forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDesc>& reqs, const float* bias, int ld_bias,
                  int causal_block, void* out, cudaStream_t s, int max_l_hint = 0);
 int reserve_workspace(fdllm_handle* h, int M, int nreq, int max_l);
-// The whole layer stack as one persistent launch when the call fits its envelope; *used is
-// FDLLM_OK when it ran, FDLLM_ERR_UNSUPPORTED when the caller must run the per-kernel loop.
-int stack_forward(fdllm_handle* h, const void* x, int M, const std::vector<ReqDesc>& reqs, int max_q, int max_l,
-                  void* out, cudaStream_t s, int* used);
 void release_step_graphs(fdllm_handle* h);
 int dense_forward(fdllm_handle* h, const void* x, const float* bias, int T, void* k, void* v, int cap, bool scratch,
                   void* out, cudaStream_t s);

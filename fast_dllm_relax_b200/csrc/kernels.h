@@ -97,13 +97,6 @@ struct GemmArgs {
   const float* norm_ss;     // [M, norm_ss_ld] per-128-feature sums of squares of norm_x rows
   int norm_ss_ld;
   float norm_eps;
-  // Post-norm (residual epilogue with ss_out, N = hidden): once every slab has written its part of a
-  // token row, the last CTA to finish those rows writes post_out = rmsnorm(row) * post_w, the next
-  // projection's normalised input.  post_ctr: [token tiles][16] arrival counters, zero between
-  // launches (the last arrival resets its counter).
-  const void* post_w;
-  void* post_out;
-  unsigned* post_ctr;
   // persistent GEMM split-K (splits <= 4): fp32 partial tiles [tiles][splits][NT][128] and per-tile
   // arrival counters (zero between launches; the last split resets its tile's counter)
   float* ppart;
@@ -132,61 +125,12 @@ struct AttnArgs {
   int* err;
 };
 
-// ---- persistent layer-stack kernel (stack.cu) -------------------------------------------------
-// One cooperative launch runs every layer of a cached decode-sized forward (M <= 32 token rows,
-// bf16): the projections on tcgen05 with weights streamed by TMA across phase boundaries, the
-// attention on mma.sync, split-K and key-split partials merged by the last-arriving CTA.
-constexpr int kStackRows = 32;          // MMA N (token rows, zero-padded)
-constexpr int kStackStages = 6;         // weight ring depth (16 KB stages)
-constexpr int kStackBBytes = 96 * 1024; // B operand / attention / accumulator region
-constexpr int kStackCtrPerLayer = 256;  // arrival counters per layer
-constexpr int kStackMaxSplits = 16;     // attention key splits per (request, q tile, kv head)
-
-struct StackLayer {
-  const void* qkv_b;  // [Nqkv]
-  const void* ln1;    // [H]
-  const void* ln2;    // [H]
-};
-
-struct StackArgs {
-  const CUtensorMap* wmaps;   // [L][4] weight maps (qkv, o, gate_up paired 64-row boxes, down), device memory
-  const StackLayer* layers;   // [L]
-  const void* final_norm;     // [H]
-  const void* x;              // [M, H] input embeddings
-  void* out;                  // [M, H] final-norm hidden states
-  void* h;                    // [M, H] residual stream
-  void* q;                    // [M, hq*hd]
-  void* attn;                 // [M, hq*hd]
-  void* act;                  // [M, I]
-  float* ss;                  // [M, H/128] per-slab sums of squares of h rows
-  float* gpart;               // split-K partial tiles [units][32][128]
-  float* apart;               // attention partial outputs [units][16*G][hd] (normalised)
-  float* alse;                // attention partial log-sum-exp [units][16*G]
-  unsigned* sync;             // [0] barrier arrivals, [1] abort flag, [64 + l*kStackCtrPerLayer + i] counters
-  const ReqDesc* reqs;
-  int n_reqs;
-  TokenMaps tok;
-  const void* rope_cos;
-  const void* rope_sin;
-  int max_pos;
-  int M, H, I, L, hq, hkv, hd;
-  float eps, scale;
-  int qkv_splits, o_splits, down_splits;  // split-K factors (slabs x splits <= grid)
-  int attn_groups, attn_splits;           // (request, q tile, kv head) groups x key splits <= grid
-  int* err;
-  // optional per-CTA timeline (globaltimer ns): [cta][kStackTraceHead + l * kStackTracePerLayer + event]
-  unsigned long long* trace;
-  int b_lsu;  // stage the B operand with cp.async by the compute warps instead of TMA
-};
-constexpr int kStackTraceHead = 4;
-constexpr int kStackTracePerLayer = 40;
-
 // ---- launch accounting / programmatic dependent launch -------------------------------------
 void count_launch(int n = 1);
 long long launch_count();
-bool pdl_enabled();  // FDLLM_PDL=0 in the environment disables programmatic dependent launch
 
-// Launch `kernel` with the programmatic-stream-serialization attribute (when enabled).
+// Launch `kernel` with the programmatic-stream-serialization attribute: it may start while its
+// predecessor in the stream drains (see pdl_wait / pdl_trigger).
 template <typename... KArgs, typename... Args>
 cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
   cudaLaunchConfig_t cfg{};
@@ -198,7 +142,7 @@ cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 1;
   count_launch();
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
@@ -214,11 +158,9 @@ cudaError_t launch_kc(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   int n = 0;
-  if (pdl_enabled()) {
-    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[n].val.programmaticStreamSerializationAllowed = 1;
-    ++n;
-  }
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
   if (cluster_z > 1) {
     attr[n].id = cudaLaunchAttributeClusterDimension;
     attr[n].val.clusterDim.x = 1;
@@ -257,10 +199,4 @@ int launch_unmask(const int* ids, const float* maxp, int rows, int* block, int s
                   int partial, int mask_id, double threshold, int* out_tok, float* out_conf, int* out_unmask,
                   int* status, cudaStream_t s);
 int launch_wait_test(int* flag, int* err, unsigned long long limit_ns, cudaStream_t s);
-// Persistent layer stack: activation maps (box 64 x 32 rows, 128-byte swizzle) of h, attn and act.
-int launch_stack(const StackArgs& a, const CUtensorMap& tm_h, const CUtensorMap& tm_attn, const CUtensorMap& tm_act,
-                 int grid, cudaStream_t s);
-int stack_smem_bytes();
-int init_stack_attributes();
-
 }  // namespace fdllm

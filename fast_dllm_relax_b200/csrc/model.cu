@@ -70,13 +70,40 @@ static int make_map(CUtensorMap* map, const void* base, int rows, int cols, int 
 
 size_t fdllm::round_up(size_t x, size_t m) { return (x + m - 1) / m * m; }
 
+// "key=value,key=value" over the Tuning fields; unknown keys or values out of range fail.
+int fdllm::parse_tuning(const char* spec, Tuning* t) {
+  if (spec == nullptr || spec[0] == '\0') return FDLLM_OK;
+  const std::string all(spec);
+  size_t pos = 0;
+  while (pos <= all.size()) {
+    const size_t end = std::min(all.find(',', pos), all.size());
+    const std::string item = all.substr(pos, end - pos);
+    pos = end + 1;
+    if (item.empty()) continue;
+    const size_t eq = item.find('=');
+    if (eq == std::string::npos) return fail(FDLLM_ERR_INVALID, "tuning item without '=': " + item);
+    const std::string key = item.substr(0, eq);
+    char* stop = nullptr;
+    const long v = std::strtol(item.c_str() + eq + 1, &stop, 0);
+    if (stop == item.c_str() + eq + 1 || *stop != '\0') return fail(FDLLM_ERR_INVALID, "bad tuning value: " + item);
+    const int x = static_cast<int>(v);
+    if (key == "nt_max" && (x == 64 || x == 128 || x == 256)) t->nt_max = x;
+    else if (key == "split_target" && x >= 0 && x <= 4) t->split_target = x;
+    else if (key == "split_max" && x >= 1 && x <= 16) t->split_max = x;
+    else if (key == "gemm_tune" && x >= 0) t->gemm_tune = x;
+    else if (key == "persist_min_rows" && x >= 0) t->persist_min_rows = x;
+    else if (key == "persist_splitk" && (x == 0 || x == 1)) t->persist_splitk = x;
+    else if (key == "attn_splits" && x >= 0 && x <= kMaxAttnSplits) t->attn_splits = x;
+    else if (key == "gu_fused_rows" && x >= 0 && x <= 64) t->gu_fused_rows = x;
+    else if (key == "block_graph" && (x == 0 || x == 1)) t->block_graph = x;
+    else return fail(FDLLM_ERR_INVALID, "unknown tuning key or value out of range: " + item);
+  }
+  return FDLLM_OK;
+}
+
 // ---- GEMM dispatch -------------------------------------------------------------------------
-static int pick_nt(int M) {
-  static const int nt_max = [] {  // tuning override of the largest token tile
-    const char* v = std::getenv("FDLLM_NT_MAX");
-    const int x = v ? std::atoi(v) : 256;
-    return (x == 64 || x == 128 || x == 256) ? x : 256;
-  }();
+static int pick_nt(const fdllm_handle* h, int M) {
+  const int nt_max = h->tune.nt_max;
   if (M <= 16) return 16;
   if (M <= 32) return 32;
   if (M <= 64 || nt_max == 64) return 64;
@@ -152,13 +179,9 @@ static int launch_persist_thunk(const GemmArgs& g, const void* a, const void* b,
                                 s);
 }
 
-// The persistent large-tile GEMM for >= 256 token rows (FDLLM_PERSIST=0 turns it off).
+// The persistent large-tile GEMM from tune.persist_min_rows token rows (prefill, batched serving).
 static bool use_persist(const fdllm_handle* h, int M) {
-  static const bool on = [] {
-    const char* v = std::getenv("FDLLM_PERSIST");
-    return v == nullptr || v[0] != '0';
-  }();
-  return on && h->dtype == FDLLM_BFLOAT16 && M >= 256;
+  return h->tune.persist_min_rows > 0 && h->dtype == FDLLM_BFLOAT16 && M >= h->tune.persist_min_rows;
 }
 
 static int launch_simt_thunk(const GemmArgs& g, const void* w, const void* x, int, cudaStream_t s) {
@@ -178,7 +201,7 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
     g->kb_per_split = 0;
     return 32;
   }
-  const int nt = pick_nt(M);
+  const int nt = pick_nt(h, M);
   g->n_tok_tiles = (M + nt - 1) / nt;
   g->n_slabs = w.paired ? (g->N / 2) / 64 : g->N / 128;
   const int kblocks = g->K / 64;
@@ -186,17 +209,8 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
   int splits = 1;
   // CTAs per SM the split-K plan aims for: 2 at <= 16 token rows (the 8-row partial step: 1.348 ->
   // 1.329 ms at prefix 384; 32 rows unchanged, 3 or 4 slower at both), else 1.
-  static const int target_override = [] {  // tuning override
-    const char* v = std::getenv("FDLLM_SPLIT_TARGET");
-    const int x = v ? std::atoi(v) : 0;
-    return x >= 1 && x <= 4 ? x : 0;
-  }();
-  const int target = target_override > 0 ? target_override : (M <= 16 ? 2 : 1);
-  static const int split_max = [] {  // tuning override: largest split-K cluster
-    const char* v = std::getenv("FDLLM_SPLIT_MAX");
-    const int x = v ? std::atoi(v) : 16;
-    return x >= 1 && x <= 16 ? x : 16;
-  }();
+  const int target = h->tune.split_target > 0 ? h->tune.split_target : (M <= 16 ? 2 : 1);
+  const int split_max = h->tune.split_max;
   if (tiles < target * h->num_sms) {  // split K over a cluster of at most 16 CTAs
     splits = std::max(1, std::min({kblocks, target * h->num_sms / tiles, split_max}));
     const int kpb = (kblocks + splits - 1) / splits;
@@ -205,17 +219,6 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
   g->splits = splits;
   g->kb_per_split = (kblocks + splits - 1) / splits;
   return nt;
-}
-
-// kGemmTune* bits of every tcgen05 projection launch.  Default: epilogue prefetch, 2 weight k
-// blocks into L2 ahead of the ring (measured per 32-row step: 2 -1.3 %; 4 / 8 / 16 slower, their
-// traffic delays the latency-bound kernels before them).
-static int gemm_tune() {
-  static const int tune = [] {  // tuning override of the kGemmTune* bits
-    const char* v = std::getenv("FDLLM_GEMM_TUNE");
-    return v != nullptr ? std::atoi(v) : (kGemmTunePrefetch | (2 << kGemmTuneL2Shift));
-  }();
-  return tune;
 }
 
 // Kernel trace slot of the next launch (null when tracing is off, capturing, or full): one
@@ -239,18 +242,12 @@ static int ktrace_reset(fdllm_handle* h) {
 // norm_w set (tcgen05 path only): X is the un-normalized input and the kernel applies RMSNorm
 // with weight norm_w while building its B operand.
 static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epilogue epi, cudaStream_t s,
-                    const void* norm_w = nullptr, const void* post_w = nullptr, void* post_out = nullptr) {
+                    const void* norm_w = nullptr) {
   if (M <= 0) return FDLLM_OK;
   GemmArgs g{};
   const int nt = plan_gemm(h, w, M, &g);
   g.err = h->err.p;
   g.epi = epi;
-  if (post_out != nullptr) {  // residual epilogue (with row statistics) followed by the next RMSNorm
-    g.post_w = post_w;
-    g.post_out = post_out;
-    g.post_ctr = h->post_ctr.p;
-    g.norm_eps = h->cfg.rms_norm_eps;
-  }
   if (norm_w != nullptr) {
     g.norm_x = X;
     g.norm_w = norm_w;
@@ -259,9 +256,9 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
     g.norm_eps = h->cfg.rms_norm_eps;
   }
   if (h->dtype == FDLLM_FLOAT32) return timed_launch(h, g, s, launch_simt_thunk, w.ptr, X, 0);
-  g.ktrace = ktrace_slot(h, 100 + epi.kind + (post_out ? 1000 : 0) + (norm_w ? 2000 : 0));
-  g.tune = gemm_tune();
-  if (norm_w == nullptr && post_out == nullptr && use_persist(h, M)) {
+  g.ktrace = ktrace_slot(h, 100 + epi.kind + (norm_w ? 2000 : 0));
+  g.tune = h->tune.gemm_tune;
+  if (norm_w == nullptr && use_persist(h, M)) {
     g.n_slabs = w.paired ? (g.N / 2) / 64 : g.N / 128;
     // 256-token tiles when they cover half the SMs, else 128 (twice the tiles for few-slab weights)
     const int pnt = 2 * g.n_slabs * ((M + 255) / 256) >= h->num_sms ? 256 : 128;
@@ -269,13 +266,10 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
     const int tiles = g.n_slabs * g.n_tok_tiles;
     const int kblocks = g.K / 64;
     // split K (<= 4 ways, >= 8 k blocks each) while the tiles alone leave SMs idle -- off unless
-    // FDLLM_PERSIST_SPLITK=1: measured slower (the last split's serial merge outweighs the idle SMs)
-    static const bool splitk = [] {
-      const char* v = std::getenv("FDLLM_PERSIST_SPLITK");
-      return v != nullptr && v[0] == '1';
-    }();
+    // tune.persist_splitk: measured slower (the last split's serial merge outweighs the idle SMs)
     int splits = 1;
-    while (splitk && splits < 4 && tiles * splits < h->num_sms && kblocks / (2 * splits) >= 8) splits *= 2;
+    while (h->tune.persist_splitk && splits < 4 && tiles * splits < h->num_sms && kblocks / (2 * splits) >= 8)
+      splits *= 2;
     g.splits = splits;
     g.kb_per_split = (kblocks + splits - 1) / splits;
     if (splits > 1) {
@@ -309,8 +303,7 @@ static void plan_attention(const fdllm_handle* h, int max_q, int max_l, int nreq
     // per layer: 32 requests x 768 keys 32 µs unsplit vs 47 µs with 3 splits; 8 x 4096 keys 44 µs
     // with 4 splits vs 59 µs with 8)
     int want = std::min({h->num_sms / base_ctas, (max_l + 63) / 64, kMaxAttnSplits});
-    const char* ev = std::getenv("FDLLM_ATTN_SPLITS");  // tuning override
-    if (ev != nullptr && std::atoi(ev) > 0) want = std::min(std::atoi(ev), kMaxAttnSplits);
+    if (h->tune.attn_splits > 0) want = std::min(h->tune.attn_splits, kMaxAttnSplits);
     if (want > 1) {
       *n_splits = want;
       *split_len = 64;  // the kernel divides each request's own key range evenly
@@ -323,7 +316,6 @@ static int ensure_ws(fdllm_handle* h, int M, int nreq) {
   const fdllm_config& c = h->cfg;
   const size_t m = round_up(static_cast<size_t>(std::max(M, 1)), 64);
   const size_t qd = static_cast<size_t>(c.num_attention_heads) * c.head_dim;
-  FDLLM_TRY(h->post_ctr.ensure(4 * 16, true));  // zeroed once; every launch leaves it zero
   FDLLM_TRY(h->h.ensure(m * c.hidden_size * h->esz));
   FDLLM_TRY(h->xn.ensure(m * std::max<size_t>(c.hidden_size, c.intermediate_size) * h->esz));
   FDLLM_TRY(h->q.ensure(m * qd * h->esz));
@@ -343,13 +335,9 @@ static int ensure_ws(fdllm_handle* h, int M, int nreq) {
 static TokenMaps token_maps(fdllm_handle* h) { return TokenMaps{h->tok_req.p, h->tok_pos.p, h->tok_row.p}; }
 
 // ---- the layer stack ----------------------------------------------------------------------
-// x: [M, hidden] input embeddings; reqs: host descriptors (q_tok0 / n_q filled); bias: dense fp32
-// bias of request 0 (or null), causal_block: implicit block-causal mask when bias is null.
-static int stack_reserve(fdllm_handle* h);
 
 int fdllm::reserve_workspace(fdllm_handle* h, int M, int nreq, int max_l) {
   FDLLM_TRY(ensure_ws(h, M, nreq));
-  if (M <= kStackRows) FDLLM_TRY(stack_reserve(h));
   const fdllm_config& c = h->cfg;
   int n_splits, split_len;
   plan_attention(h, M, max_l, nreq, false, &n_splits, &split_len);
@@ -357,140 +345,9 @@ int fdllm::reserve_workspace(fdllm_handle* h, int M, int nreq, int max_l) {
   return FDLLM_OK;
 }
 
-// ---- persistent layer stack ------------------------------------------------------------------
-// FDLLM_STACK=1 selects the persistent layer-stack kernel for eligible calls.
-static bool stack_disabled() {
-  const char* v = std::getenv("FDLLM_STACK");
-  return v == nullptr || v[0] != '1';
-}
-
-// Tuning override "qkv,o,down,attn" of the layer-stack split factors (0 = planned value).
-static void stack_split_override(int* q, int* o, int* d, int* at) {
-  const char* v = std::getenv("FDLLM_STACK_SPLITS");
-  if (v == nullptr) return;
-  int x[4] = {0, 0, 0, 0};
-  if (std::sscanf(v, "%d,%d,%d,%d", &x[0], &x[1], &x[2], &x[3]) < 1) return;
-  if (x[0] > 0) *q = x[0];
-  if (x[1] > 0) *o = x[1];
-  if (x[2] > 0) *d = x[2];
-  if (x[3] > 0) *at = x[3];
-}
-
-// Plan of the layer-stack kernel for this call, or false when the call is outside its envelope
-// (then the per-kernel layer loop runs).
-static bool stack_plan(const fdllm_handle* h, int M, const std::vector<ReqDesc>& reqs, int max_l, StackArgs* a) {
-  const fdllm_config& c = h->cfg;
-  if (h->dtype != FDLLM_BFLOAT16 || stack_disabled() || M <= 0 || M > kStackRows) return false;
-  const int grid = h->num_sms;
-  const int H = c.hidden_size, I = c.intermediate_size, hq = c.num_attention_heads, hkv = c.num_key_value_heads;
-  const int hd = c.head_dim;
-  if ((hd != 64 && hd != 128) || hkv <= 0 || hq % hkv != 0 || hq / hkv > 6) return false;
-  const int nqkv = (hq + 2 * hkv) * hd, qd = hq * hd;
-  if (H % 128 != 0 || nqkv % 128 != 0 || qd % 64 != 0 || I % 64 != 0 || H / 8 > 384) return false;
-  const int s_qkv = nqkv / 128, s_o = H / 128, s_gu = I / 64, s_down = H / 128;
-  if (s_qkv > 64 || s_o > 64 || s_down > 64 || s_gu > grid || s_qkv > grid || s_o > grid) return false;
-  // Split-K: the fewest splits whose units fit the weight ring (prefetched whole while the
-  // previous phase runs), within the grid and the merge limit.
-  auto splits_for = [&](int slabs, int kbt) {
-    const int fit = (kbt + kStackStages - 1) / kStackStages;
-    return std::max(1, std::min({fit, grid / slabs, kStackMaxSplits, kbt}));
-  };
-  a->qkv_splits = splits_for(s_qkv, H / 64);
-  a->o_splits = splits_for(s_o, qd / 64);
-  a->down_splits = splits_for(s_down, I / 64);
-  int groups = 0;
-  for (const ReqDesc& r : reqs) groups += (r.n_q + 15) / 16 * hkv;
-  if (groups <= 0 || groups > 64) return false;
-  a->attn_groups = groups;
-  a->attn_splits = std::max(1, std::min({grid / groups, kStackMaxSplits, (std::max(max_l, 1) + 63) / 64}));
-  stack_split_override(&a->qkv_splits, &a->o_splits, &a->down_splits, &a->attn_splits);
-  auto ok_split = [&](int slabs, int kbt, int sp) { return sp >= 1 && sp <= kStackMaxSplits && sp <= kbt && slabs * sp <= grid; };
-  if (!ok_split(s_qkv, H / 64, a->qkv_splits) || !ok_split(s_o, qd / 64, a->o_splits) ||
-      !ok_split(s_down, I / 64, a->down_splits) || a->attn_splits < 1 || a->attn_splits > kStackMaxSplits ||
-      groups * a->attn_splits > grid)
-    return false;
-  auto max_nk = [](int kbt, int splits) { return (kbt + splits - 1) / splits; };
-  const int bmax = kStackBBytes / (kStackRows * 64 * 2);
-  if (max_nk(H / 64, a->qkv_splits) > bmax || max_nk(qd / 64, a->o_splits) > bmax || H / 64 > bmax ||
-      max_nk(I / 64, a->down_splits) > bmax)
-    return false;
-  return true;
-}
-
-// Partial and counter buffers at their largest sizes (units <= grid), so that no later call,
-// in particular none inside a stream capture, has to grow them.
-static int stack_reserve(fdllm_handle* h) {
-  const fdllm_config& c = h->cfg;
-  if (h->dtype != FDLLM_BFLOAT16 || c.num_key_value_heads <= 0) return FDLLM_OK;
-  const size_t grid = static_cast<size_t>(h->num_sms);
-  const size_t rows = 16 * static_cast<size_t>(c.num_attention_heads / c.num_key_value_heads);
-  FDLLM_TRY(h->stack_gpart.ensure(grid * kStackRows * 128));
-  FDLLM_TRY(h->stack_apart.ensure(grid * rows * c.head_dim));
-  FDLLM_TRY(h->stack_alse.ensure(grid * rows));
-  FDLLM_TRY(h->stack_sync.ensure(64 + static_cast<size_t>(c.num_hidden_layers) * kStackCtrPerLayer));
-  return FDLLM_OK;
-}
-
-int fdllm::stack_forward(fdllm_handle* h, const void* x, int M, const std::vector<ReqDesc>& reqs, int max_q,
-                         int max_l, void* out, cudaStream_t s, int* used) {
-  (void)max_q;
-  *used = FDLLM_ERR_UNSUPPORTED;
-  StackArgs a{};
-  if (!stack_plan(h, M, reqs, max_l, &a)) return FDLLM_OK;
-  const fdllm_config& c = h->cfg;
-  const int grid = h->num_sms;
-  FDLLM_TRY(stack_reserve(h));
-  const size_t n_sync = 64 + static_cast<size_t>(c.num_hidden_layers) * kStackCtrPerLayer;
-  CUtensorMap tm_h, tm_attn, tm_act;
-  FDLLM_TRY(make_map(&tm_h, h->h.p, M, c.hidden_size, kStackRows));
-  FDLLM_TRY(make_map(&tm_attn, h->attn.p, M, c.num_attention_heads * c.head_dim, kStackRows));
-  FDLLM_TRY(make_map(&tm_act, h->act.p, M, c.intermediate_size, kStackRows));
-  a.wmaps = reinterpret_cast<const CUtensorMap*>(h->stack_maps.p);
-  a.layers = reinterpret_cast<const StackLayer*>(h->stack_layers.p);
-  a.final_norm = h->final_norm;
-  a.x = x;
-  a.out = out ? out : h->xn.p;
-  a.h = h->h.p;
-  a.q = h->q.p;
-  a.attn = h->attn.p;
-  a.act = h->act.p;
-  a.ss = h->ss.p;
-  a.gpart = h->stack_gpart.p;
-  a.apart = h->stack_apart.p;
-  a.alse = h->stack_alse.p;
-  a.sync = h->stack_sync.p;
-  a.reqs = h->reqs.p;
-  a.n_reqs = static_cast<int>(reqs.size());
-  a.tok = token_maps(h);
-  a.rope_cos = h->rope_cos.p;
-  a.rope_sin = h->rope_sin.p;
-  a.max_pos = c.max_positions;
-  a.M = M;
-  a.H = c.hidden_size;
-  a.I = c.intermediate_size;
-  a.L = c.num_hidden_layers;
-  a.hq = c.num_attention_heads;
-  a.hkv = c.num_key_value_heads;
-  a.hd = c.head_dim;
-  a.eps = c.rms_norm_eps;
-  a.scale = 1.0f / std::sqrt(static_cast<float>(c.head_dim));
-  a.err = h->err.p;
-  a.trace = nullptr;
-  const char* bl = std::getenv("FDLLM_STACK_BLSU");
-  a.b_lsu = (bl != nullptr && bl[0] == '1') ? 1 : 0;
-  if (h->stack_trace_on) {
-    const size_t n = static_cast<size_t>(grid) * (kStackTraceHead + static_cast<size_t>(c.num_hidden_layers) * kStackTracePerLayer);
-    FDLLM_TRY(h->stack_trace.ensure(n));
-    CUDA_TRY(cudaMemsetAsync(h->stack_trace.p, 0, n * sizeof(unsigned long long), s));
-    a.trace = h->stack_trace.p;
-    h->stack_trace_grid = grid;
-  }
-  CUDA_TRY(cudaMemsetAsync(h->stack_sync.p, 0, n_sync * sizeof(unsigned), s));
-  CUDA_TRY(launch_stack(a, tm_h, tm_attn, tm_act, grid, s));
-  *used = FDLLM_OK;
-  return FDLLM_OK;
-}
-
+// ---- the layer stack ----------------------------------------------------------------------
+// x: [M, hidden] input embeddings; reqs: host descriptors (q_tok0 / n_q filled); bias: dense fp32
+// bias of request 0 (or null), causal_block: implicit block-causal mask when bias is null.
 int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDesc>& reqs, const float* bias,
                         int ld_bias, int causal_block, void* out, cudaStream_t s, int max_l_hint) {
   const fdllm_config& c = h->cfg;
@@ -513,12 +370,6 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
   int n_splits, split_len;
   plan_attention(h, max_q, max_l, nreq, bias != nullptr || causal_block != 0, &n_splits, &split_len);
 
-  if (bias == nullptr && causal_block == 0) {
-    int rc = FDLLM_ERR_UNSUPPORTED;
-    FDLLM_TRY(stack_forward(h, x, M, reqs, max_q, max_l, out, s, &rc));
-    if (rc == FDLLM_OK) return FDLLM_OK;  // else: not eligible, run the per-kernel layer loop
-  }
-
   Epilogue base{};
   base.hq = c.num_attention_heads;
   base.hkv = c.num_key_value_heads;
@@ -531,23 +382,11 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
 
   // Decode-sized calls fold each layer's input RMSNorm into the qkv projection (its CTAs normalize
   // their B tiles in place, with row statistics left by the previous down projection); large calls
-  // normalize once in a separate kernel.
+  // normalize once in a separate kernel.  The post-attention RMSNorm is folded into gate_up the
+  // same way up to tune.gu_fused_rows token rows (a stage's normalisation is short there); above,
+  // a separate vectorized rmsnorm kernel is faster (32 rows: 1.41 ms per step against 1.52).
   const bool fuse_norm = h->dtype == FDLLM_BFLOAT16 && M <= 64 && c.hidden_size <= 2560;
-  // post-attention RMSNorm: "fused" = gate_up normalises its B tiles (fastest for <= 16 rows, where
-  // a stage's normalisation is short); "kernel" = a separate rmsnorm kernel (fastest above: at 32
-  // rows 1.41 ms per step vs 1.46 for "post" and 1.52 for "fused"); "post" = the o projection's
-  // last CTAs normalise each finished row group.  FDLLM_GU_NORM overrides the choice.
-  const char* gn = std::getenv("FDLLM_GU_NORM");
-  const std::string gu_norm =
-      gn != nullptr ? std::string(gn) : std::string(!fuse_norm ? "kernel" : (M <= 16 ? "fused" : "kernel"));
-  const bool fuse_norm_gu = fuse_norm && gu_norm == "fused";
-  const bool post_norm_gu = fuse_norm && gu_norm == "post" && M <= 64;
-  // The next layer's input RMSNorm (and the final norm): "fused" = the qkv projection normalises
-  // its B tiles with the statistics the down projection left; "post" = the down projection's last
-  // CTAs write the normalised rows; "kernel" = a separate rmsnorm kernel (FDLLM_QKV_NORM overrides).
-  const char* qn = std::getenv("FDLLM_QKV_NORM");
-  const bool post_norm_qkv = fuse_norm && M <= 64 && qn != nullptr && std::string(qn) == "post";
-  const bool kernel_norm_qkv = qn != nullptr && std::string(qn) == "kernel";
+  const bool fuse_norm_gu = fuse_norm && M <= h->tune.gu_fused_rows;
 
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const LayerW& L = h->layers[l];
@@ -557,9 +396,7 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     e.layer = l;
     e.bias = L.qkv_b;
     e.qout = h->q.p;
-    if (post_norm_qkv && l > 0) {  // the previous down projection wrote the normalised input
-      FDLLM_TRY(run_gemm(h, L.qkv, h->xn.p, M, e, s));
-    } else if (fuse_norm && l > 0 && !kernel_norm_qkv) {  // layer 0's input has no producer epilogue
+    if (fuse_norm && l > 0) {  // layer 0's input has no producer epilogue
       FDLLM_TRY(run_gemm(h, L.qkv, layer_in, M, e, s, L.ln1));
     } else {
       // layer 0 reads the input embeddings and starts the residual stream h as their copy
@@ -592,23 +429,17 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     e.kind = kEpiResidual;
     e.resid = h->h.p;
     e.ld_resid = c.hidden_size;
-    if (fuse_norm_gu || post_norm_gu) {  // leave the statistics of the post-attention RMSNorm
+    if (fuse_norm_gu) {  // leave the statistics of the post-attention RMSNorm
       e.ss_out = h->ss.p;
       e.ss_ld = c.hidden_size / 128;
     }
-    if (post_norm_gu) {
-      FDLLM_TRY(run_gemm(h, L.o, h->attn.p, M, e, s, nullptr, L.ln2, h->xn.p));
-    } else {
-      FDLLM_TRY(run_gemm(h, L.o, h->attn.p, M, e, s));
-    }
+    FDLLM_TRY(run_gemm(h, L.o, h->attn.p, M, e, s));
 
     e = base;
     e.kind = kEpiSiluMul;
     e.out = h->act.p;
     e.ld_out = c.intermediate_size;
-    if (post_norm_gu) {
-      FDLLM_TRY(run_gemm(h, L.gu, h->xn.p, M, e, s));
-    } else if (fuse_norm_gu) {
+    if (fuse_norm_gu) {
       FDLLM_TRY(run_gemm(h, L.gu, h->h.p, M, e, s, L.ln2));
     } else {
       CUDA_TRY(launch_rmsnorm(h->h.p, L.ln2, h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s));
@@ -623,15 +454,8 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
       e.ss_out = h->ss.p;
       e.ss_ld = c.hidden_size / 128;
     }
-    if (post_norm_qkv) {
-      const bool last = l + 1 == c.num_hidden_layers;
-      FDLLM_TRY(run_gemm(h, L.down, h->act.p, M, e, s, nullptr, last ? h->final_norm : h->layers[l + 1].ln1,
-                         last ? (out ? out : h->xn.p) : h->xn.p));
-    } else {
-      FDLLM_TRY(run_gemm(h, L.down, h->act.p, M, e, s));
-    }
+    FDLLM_TRY(run_gemm(h, L.down, h->act.p, M, e, s));
   }
-  if (post_norm_qkv) return FDLLM_OK;  // the last down projection wrote the final norm
   // out == null (build_prefix_cache): the final hidden states are not needed; xn is free by now.
   CUDA_TRY(launch_rmsnorm(h->h.p, h->final_norm, out ? out : h->xn.p, M, c.hidden_size, c.rms_norm_eps, h->dtype, s));
   return FDLLM_OK;
@@ -710,9 +534,12 @@ int fdllm_create(const fdllm_config* cfg, int device, fdllm_handle** out) {
              qkv % 128 || 128 % c.head_dim) {
     return fail(FDLLM_ERR_UNSUPPORTED, "fp32 path needs sizes divisible by 32, qkv by 128, head_dim dividing 128");
   }
+  Tuning tune;
+  FDLLM_TRY(parse_tuning(std::getenv("FDLLM_TUNING"), &tune));
   CUDA_TRY(cudaSetDevice(device));
   CUDA_TRY(init_kernel_attributes());
   fdllm_handle* h = new fdllm_handle();
+  h->tune = tune;
   h->cfg = c;
   h->device = device;
   h->dtype = c.dtype;
@@ -747,15 +574,9 @@ int fdllm_destroy(fdllm_handle* h) {
   for (auto* b : {&h->err, &h->tok_req, &h->tok_pos, &h->tok_row, &h->tmp_ids, &h->targets, &h->dec.ids,
                   &h->dec.block, &h->dec.cids, &h->dec.out})
     b->release();
-  for (auto* b : {&h->conf_part, &h->tmp_maxp, &h->ss, &h->dec.cmax, &h->stack_gpart, &h->stack_apart, &h->stack_alse})
-    b->release();
-  h->stack_maps.release();
-  h->stack_layers.release();
-  h->stack_sync.release();
-  h->post_ctr.release();
+  for (auto* b : {&h->conf_part, &h->tmp_maxp, &h->ss, &h->dec.cmax}) b->release();
   h->persist_part.release();
   h->persist_ctr.release();
-  h->stack_trace.release();
   h->ktrace.release();
   h->reqs.release();
   if (h->dec.host) cudaFreeHost(h->dec.host);
@@ -805,21 +626,6 @@ int fdllm_bind_params(fdllm_handle* h, const void* const* ptrs, int n) {
       FDLLM_TRY(make_map(&L.down.map, L.down.ptr, L.down.rows, L.down.cols, 128));
     }
     FDLLM_TRY(make_map(&h->lm.map, h->lm.ptr, h->lm.rows, h->lm.cols, 128));
-    // the layer-stack kernel reads every layer's weight maps and small pointers from device memory
-    std::vector<CUtensorMap> maps(static_cast<size_t>(c.num_hidden_layers) * 4);
-    std::vector<StackLayer> sl(c.num_hidden_layers);
-    for (int l = 0; l < c.num_hidden_layers; ++l) {
-      const LayerW& L = h->layers[l];
-      maps[l * 4 + 0] = L.qkv.map;
-      maps[l * 4 + 1] = L.o.map;
-      maps[l * 4 + 2] = L.gu.map;
-      maps[l * 4 + 3] = L.down.map;
-      sl[l] = StackLayer{L.qkv_b, L.ln1, L.ln2};
-    }
-    FDLLM_TRY(h->stack_maps.ensure(maps.size() * sizeof(CUtensorMap)));
-    FDLLM_TRY(h->stack_layers.ensure(sl.size() * sizeof(StackLayer)));
-    CUDA_TRY(cudaMemcpy(h->stack_maps.p, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
-    CUDA_TRY(cudaMemcpy(h->stack_layers.p, sl.data(), sl.size() * sizeof(StackLayer), cudaMemcpyHostToDevice));
   }
   h->bound = true;
   return FDLLM_OK;
@@ -1065,28 +871,6 @@ int fdllm_profile_read(fdllm_handle* h, double* out4) {
   return FDLLM_OK;
 }
 
-int fdllm_stack_trace_enable(fdllm_handle* h, int enable) {
-  if (h == nullptr) return fail(FDLLM_ERR_INVALID, "null handle");
-  std::lock_guard<std::mutex> lock(h->mu);
-  h->stack_trace_on = enable != 0;
-  return FDLLM_OK;
-}
-
-int fdllm_stack_trace_read(fdllm_handle* h, uint64_t* out, long long cap, int32_t* n_cta, int32_t* per_cta) {
-  if (h == nullptr || n_cta == nullptr || per_cta == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
-  std::lock_guard<std::mutex> lock(h->mu);
-  const int per = kStackTraceHead + h->cfg.num_hidden_layers * kStackTracePerLayer;
-  *n_cta = h->stack_trace_grid;
-  *per_cta = per;
-  const long long n = static_cast<long long>(h->stack_trace_grid) * per;
-  if (out == nullptr || n == 0) return FDLLM_OK;
-  if (cap < n) return fail(FDLLM_ERR_INVALID, "trace buffer too small");
-  CUDA_TRY(cudaSetDevice(h->device));
-  CUDA_TRY(cudaDeviceSynchronize());
-  CUDA_TRY(cudaMemcpy(out, h->stack_trace.p, static_cast<size_t>(n) * sizeof(uint64_t), cudaMemcpyDeviceToHost));
-  return FDLLM_OK;
-}
-
 int fdllm_kernel_trace_enable(fdllm_handle* h, int enable) {
   if (h == nullptr) return fail(FDLLM_ERR_INVALID, "null handle");
 #ifndef FDLLM_KTRACE
@@ -1216,7 +1000,7 @@ extern "C" int fdllm_confidence_static(fdllm_handle* h, const void* hidden, int 
     FDLLM_TRY(timed_launch(h, g, s, launch_simt_thunk, h->lm.ptr, hidden, 0));
   } else {
     g.ktrace = ktrace_slot(h, 100 + e.kind);
-    g.tune = gemm_tune();
+    g.tune = h->tune.gemm_tune;
     CUtensorMap tmB;
     FDLLM_TRY(make_map(&tmB, hidden, rows, g.K, nt));
     FDLLM_TRY(timed_launch(h, g, s, launch_tc_thunk, &h->lm.map, &tmB, nt));

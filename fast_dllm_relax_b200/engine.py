@@ -309,21 +309,6 @@ class Engine:
         _lib.check(self.lib.fdllm_wait_selftest(self._h, int(limit_ns), ctypes.byref(code)))
         return code.value
 
-    def stack_trace_enable(self, enable: bool = True) -> None:
-        """Record a per-CTA phase timeline in every later layer-stack launch (diagnostics)."""
-        _lib.check(self.lib.fdllm_stack_trace_enable(self._h, int(bool(enable))))
-
-    def stack_trace_read(self):
-        """The last layer-stack launch's timeline: uint64 ns [n_cta, per_cta] (slots in the header)."""
-        import numpy as np  # noqa: PLC0415
-        n_cta, per = ctypes.c_int(0), ctypes.c_int(0)
-        _lib.check(self.lib.fdllm_stack_trace_read(self._h, None, 0, ctypes.byref(n_cta), ctypes.byref(per)))
-        out = np.zeros((n_cta.value, per.value), dtype=np.uint64)
-        if out.size:
-            _lib.check(self.lib.fdllm_stack_trace_read(self._h, out.ctypes.data, out.size, ctypes.byref(n_cta),
-                                                       ctypes.byref(per)))
-        return out
-
     def kernel_trace_enable(self, enable: bool = True) -> None:
         """Record per-launch phase stamps of later eager projection / attention launches
         (diagnostics; clears the record)."""

@@ -176,21 +176,6 @@ FDLLM_API int fdllm_profile_read(fdllm_handle* h, double* out4);
 /* Bytes of device workspace the handle currently holds. */
 FDLLM_API long long fdllm_workspace_bytes(fdllm_handle* h);
 
-/* Diagnostics of the persistent layer-stack kernel (no counterpart in the reference; the
- * reference profiles per compiled function, docs/notebooks/07_profiling.ipynb).  While enabled,
- * every layer-stack launch issued afterwards records %globaltimer stamps (ns) per CTA;
- * fdllm_stack_trace_read copies the last record (synchronises): out[cta * per_cta + slot] with
- * slots 0 start, 1 layer-0 statistics done, 2 first grid barrier passed, 3 end, and per layer l
- * at 4 + 40*l: qkv 0-4 (start, first B group landed, B released, accumulator ready, epilogue
- * done), 5 barrier; attention 6 start, 7 done, 8 barrier; o 9-13, 14 barrier; gate_up 15-19,
- * 20 barrier; down 21-25, 26 barrier; attention detail 27 first K/V tile, 28 partial written,
- * 29 splits gathered; qkv split-K 30 partial published, 31 splits gathered.  0 = not reached
- * (a CTA without a unit in that phase).  With
- * out == NULL only *n_cta and *per_cta are written.  A CUDA graph captured while disabled keeps
- * recording nothing. */
-FDLLM_API int fdllm_stack_trace_enable(fdllm_handle* h, int enable);
-FDLLM_API int fdllm_stack_trace_read(fdllm_handle* h, uint64_t* out, long long cap, int32_t* n_cta, int32_t* per_cta);
-
 /* Kernel trace (diagnostics; no counterpart in the reference).  While enabled, every projection
  * GEMM and attention launch issued outside stream capture records the earliest and latest
  * %globaltimer value (ns) at which any of its CTAs reached phase p: out[24*i + 2p] and

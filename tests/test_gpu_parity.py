@@ -208,41 +208,11 @@ def _batched_vs_single(setup, cases, seed0):
         o += r["rows"]
 
 
-def test_batched_forward_matches_single_requests(setup, monkeypatch):
-    """Batched rows run the per-kernel layer loop; the single requests are forced onto the same
-    path (FDLLM_STACK=0): 80 mixed rows, and 16 rows of partial steps (the <= 16-row plan)."""
-    monkeypatch.setenv("FDLLM_STACK", "0")
+def test_batched_forward_matches_single_requests(setup):
+    """80 mixed rows in one batched forward, and 16 rows of partial steps (the <= 16-row plan),
+    against the same requests run one at a time."""
     _batched_vs_single(setup, ((32, 32, 0), (64, 8, 8), (96, 32, 0), (32, 8, 24)), 40)
     _batched_vs_single(setup, ((64, 8, 8), (32, 8, 24)), 70)
-
-
-def test_batched_requests_in_the_layer_stack_kernel(setup, monkeypatch):
-    """Several requests sharing one persistent layer-stack launch (<= 32 rows in all) match the
-    same requests run one at a time."""
-    cfg, dtype, eng, orc = setup
-    monkeypatch.setenv("FDLLM_STACK", "1")
-    reqs, xs, singles = [], [], []
-    for i, (P, rows, rp) in enumerate(((32, 8, 8), (64, 16, 0), (96, 8, 24))):
-        k, v = eng.new_cache(P + 32)
-        eng.build_prefix_cache(_rand_act(cfg, P, dtype, 70 + i).to(_dev()), None, k, v)
-        eng.forward_cached(_rand_act(cfg, 32, dtype, 80 + i).to(_dev()), k, v, P, P)
-        x = _rand_act(cfg, rows, dtype, 90 + i).to(_dev())
-        attend = 32 if rp else rows
-        ks, vs = k.clone(), v.clone()
-        singles.append((eng.forward_cached(x, ks, vs, P + rp, P, rp, attend)[0], ks, vs))
-        xs.append(x[0])
-        reqs.append(dict(k=k, v=v, rows=rows, prefix_len=P, write_rel=rp, attend_rel=attend))
-    n0 = eng.kernel_launches()
-    out = eng.forward_cached_batch(torch.cat(xs), reqs)
-    torch.cuda.synchronize()
-    if dtype == "bfloat16":
-        assert eng.kernel_launches() - n0 == 2  # prepare + the layer-stack kernel
-    o = 0
-    for r, (hs, ks, vs) in zip(reqs, singles):
-        _close(out[o:o + r["rows"]], hs, dtype, "batched rows")
-        _close(r["k"], ks, dtype, "k")
-        _close(r["v"], vs, dtype, "v")
-        o += r["rows"]
 
 
 def test_invalid_windows_raise_value_error(setup):
@@ -332,54 +302,3 @@ def test_out_of_range_token_sets_device_error_not_fault():
     assert eng.device_error() == 4
     assert torch.equal(out[1].cpu(), torch.zeros(TINY.hidden_size))
     assert eng.device_error() == 0
-
-
-def test_layer_stack_kernel_matches_per_kernel_path(setup, monkeypatch):
-    """With FDLLM_STACK=1, decode-sized bf16 cached forwards (<= 32 rows) run as one persistent
-    layer-stack launch; with FDLLM_STACK=0 the same call runs the per-kernel layer loop.  Both must agree with each
-    other and with the oracle, and the persistent path must really be the one taken."""
-    cfg, dtype, eng, orc = setup
-    if dtype != "bfloat16":
-        pytest.skip("the layer-stack kernel is the bf16 decode path")
-    P = 96
-    prefix = _rand_act(cfg, P, dtype, 40)
-    k, v = eng.new_cache(P + 64)
-    k.zero_()
-    v.zero_()
-    eng.build_prefix_cache(prefix.to(_dev()), None, k, v)
-    kr, vr = torch.zeros(k.shape, dtype=k.dtype), torch.zeros(v.shape, dtype=v.dtype)
-    orc.build_prefix_cache(prefix, build_block_bias(0, P, 32), kr, vr)
-    for rows, rp in ((32, None), (8, 8), (17, None), (1, None)):
-        x = _rand_act(cfg, rows, dtype, 50 + rows).to(_dev())
-        off = P + (rp or 0)
-        k0, v0 = k.clone(), v.clone()
-        monkeypatch.setenv("FDLLM_STACK", "1")
-        n0 = eng.kernel_launches()
-        if rp is None:
-            h_stack = eng.forward_cached(x, k, v, off, P)
-        else:
-            h_stack = eng.forward_block_partial(x, k, v, off, P, rp)
-        torch.cuda.synchronize()
-        n_stack = eng.kernel_launches() - n0
-        k_stack = k.clone()
-        k.copy_(k0)
-        v.copy_(v0)
-        monkeypatch.setenv("FDLLM_STACK", "0")
-        n0 = eng.kernel_launches()
-        if rp is None:
-            h_loop = eng.forward_cached(x, k, v, off, P)
-        else:
-            h_loop = eng.forward_block_partial(x, k, v, off, P, rp)
-        torch.cuda.synchronize()
-        n_loop = eng.kernel_launches() - n0
-        monkeypatch.delenv("FDLLM_STACK")
-        assert n_stack == 2, f"rows={rows}: expected prepare + one layer-stack launch, saw {n_stack}"
-        assert n_loop > 4 * cfg.num_hidden_layers
-        _close(h_stack, h_loop, dtype, f"rows={rows} stack vs loop")
-        _close(k_stack, k, dtype, f"rows={rows} cache rows")
-        if rp is None:  # the oracle's cache takes the same writes, in the same order
-            ref = orc.forward_cached(x.cpu(), kr, vr, off, P)
-        else:
-            ref = orc.forward_block_partial(x.cpu(), kr, vr, off, P, rp)
-        _close(h_stack.cpu(), ref, dtype, f"rows={rows} stack vs oracle")
-        assert eng.device_error() == 0

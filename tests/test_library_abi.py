@@ -101,3 +101,22 @@ def test_create_without_a_device_returns_a_cuda_error(lib):
     assert lib.fdllm_last_error()
     with pytest.raises(_lib.FdllmError):
         _lib.check(_lib.FDLLM_ERR_CUDA)
+
+
+def test_tuning_overrides_are_parsed_before_any_device_use(monkeypatch):
+    """FDLLM_TUNING ("key=value,...") sets the per-handle kernel-plan parameters at fdllm_create;
+    an unknown key or a value out of range is refused with FDLLM_ERR_INVALID before the device is
+    touched, so it fails the same way with or without a GPU."""
+    lib = _lib.load()
+    c = _lib.FdllmConfig(1024, 256, 512, 2, 4, 2, 64, 1e-6, 1e6, 1, 32, 4096, 1)
+    h = ctypes.c_void_p()
+    for spec, needle in (("bogus=1", "unknown tuning key"), ("nt_max=96", "out of range"),
+                         ("split_max", "without '='"), ("attn_splits=x", "bad tuning value")):
+        monkeypatch.setenv("FDLLM_TUNING", spec)
+        assert lib.fdllm_create(ctypes.byref(c), 0, ctypes.byref(h)) == _lib.FDLLM_ERR_INVALID, spec
+        assert needle in lib.fdllm_last_error().decode(), spec
+    monkeypatch.setenv("FDLLM_TUNING", "nt_max=128,split_max=8,persist_min_rows=0,block_graph=0")
+    rc = lib.fdllm_create(ctypes.byref(c), 0, ctypes.byref(h))
+    assert rc != _lib.FDLLM_ERR_INVALID  # a valid spec passes parsing (then needs a device)
+    if rc == _lib.FDLLM_OK:
+        lib.fdllm_destroy(h)
