@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple] = {
     "fdllm_profile_enable": (_I, [_P, _I]),
     "fdllm_profile_read": (_I, [_P, ctypes.POINTER(ctypes.c_double)]),
     "fdllm_device_error": (_I, [_P, ctypes.POINTER(_I)]),
+    "fdllm_device_error_detail": (_I, [_P, _P]),
     "fdllm_wait_selftest": (_I, [_P, ctypes.c_ulonglong, ctypes.POINTER(_I)]),
     "fdllm_workspace_bytes": (ctypes.c_longlong, [_P]),
 }

@@ -31,6 +31,17 @@ __device__ __forceinline__ void report_error(int* err, int code) {
   if (err != nullptr) atomicCAS(err, 0, code);
 }
 
+// report_error for an expired wait, with where it gave up: the first error also leaves err[1] =
+// the wait site, err[2] = the call's token rows, err[3] = block index | split count << 16.
+__device__ __forceinline__ void report_wait(int* err, int code, int site, int rows, int splits) {
+  if (err == nullptr) return;
+  if (atomicCAS(err, 0, code) == 0) {
+    err[1] = site;
+    err[2] = rows;
+    err[3] = static_cast<int>(blockIdx.x) | (splits << 16);
+  }
+}
+
 // ---- element conversions ------------------------------------------------------------------
 template <typename T> __device__ __forceinline__ float to_f(T v);
 template <> __device__ __forceinline__ float to_f<float>(float v) { return v; }

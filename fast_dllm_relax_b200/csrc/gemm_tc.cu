@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(128, 4)
       const int s = i % C::kStages;
       const uint32_t ph = (i / C::kStages) & 1u;
       if (!mbar_wait(&empty[s], ph ^ 1u)) {
-        report_error(g.err, kErrTimeoutProducer);
+        report_wait(g.err, kErrTimeoutProducer, 1, g.M, g.splits);
         break;
       }
       mbar_arrive_expect_tx(&full[s], C::kStage);
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(128, 4)
     // Drain: every copy this thread issued must have landed before shared memory is reused.
     for (int i = max(0, issued - C::kStages); i < issued; ++i) {
       if (!mbar_wait(&full[i % C::kStages], (i / C::kStages) & 1u)) {
-        report_error(g.err, kErrTimeoutProducer);
+        report_wait(g.err, kErrTimeoutProducer, 2, g.M, g.splits);
         break;
       }
     }
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(128, 4)
       const int s = i % C::kStages;
       const uint32_t ph = (i / C::kStages) & 1u;
       if (!mbar_wait(&full[s], ph)) {
-        report_error(g.err, kErrTimeoutMma);
+        report_wait(g.err, kErrTimeoutMma, 3, g.M, g.splits);
         break;
       }
       const uint4 wu = reinterpret_cast<const uint4*>(s_w)[(kb0 + i) * 8 + cc];
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(128, 4)
       const int s = i % C::kStages;
       const uint32_t ph = (i / C::kStages) & 1u;
       if (!mbar_wait(g.norm_x ? &ready[s] : &full[s], ph)) {
-        report_error(g.err, kErrTimeoutMma);
+        report_wait(g.err, kErrTimeoutMma, 4, g.M, g.splits);
         break;
       }
       tc_fence_after_sync();
@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(128, 4)
   EpiPre<bf16> pre;
   if (NT <= 64 && (g.tune & kGemmTunePrefetch))
     epi_prefetch<bf16>(g, tok0, slab, S > 1 ? lr0 : 0, S > 1 ? lr1 : NT, threadIdx.x, blockDim.x, pre);
-  if (!mbar_wait(accf, 0)) report_error(g.err, kErrTimeoutEpilogue);
+  if (!mbar_wait(accf, 0)) report_wait(g.err, kErrTimeoutEpilogue, 5, g.M, g.splits);
   if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 2);
   tc_fence_after_sync();
   __syncthreads();  // the producer's drain is complete before the ring is overwritten
@@ -435,7 +435,7 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kPStages;
           if (!mbar_wait(&empty[s], ((it / kPStages) & 1u) ^ 1u)) {
-            report_error(g.err, kErrTimeoutProducer);
+            report_wait(g.err, kErrTimeoutProducer, 11, g.M, g.splits);
             ok = false;
             break;
           }
@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
         int kb0, kb1;
         kb_range(u, &kb0, &kb1);
         if (!mbar_wait(&tempty[buf], ((ti >> 1) & 1u) ^ 1u)) {  // the epilogue released this accumulator
-          report_error(g.err, kErrTimeoutMma);
+          report_wait(g.err, kErrTimeoutMma, 13, g.M, g.splits);
           break;
         }
         tc_fence_after_sync();
@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kPStages;
           if (!mbar_wait(&full[s], (it / kPStages) & 1u)) {
-            report_error(g.err, kErrTimeoutMma);
+            report_wait(g.err, kErrTimeoutMma, 14, g.M, g.splits);
             ok = false;
             break;
           }
@@ -499,7 +499,7 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
       const int slab = t / g.n_tok_tiles, tok0 = (t % g.n_tok_tiles) * kPNT;
       const uint32_t buf = ti & 1u;
       if (!mbar_wait(&tfull[buf], (ti >> 1) & 1u)) {
-        report_error(g.err, kErrTimeoutEpilogue);
+        report_wait(g.err, kErrTimeoutEpilogue, 15, g.M, g.splits);
         break;
       }
       tc_fence_after_sync();

@@ -88,6 +88,7 @@ struct GemmArgs {
   int paired;               // gate/up pairing (N = 2*I; slab s covers rows [64s, 64s+64) and I + same)
   int n_slabs;              // N / 128 (or I / 64 when paired)
   int n_tok_tiles;
+  int tile_n;               // persistent GEMM: token rows per tile (128 or 256; the B map's box height)
   int splits;               // split-K factor = cluster size (<= 16)
   int kb_per_split;         // 64-wide k blocks per split
   // Fused RMSNorm of the activations (tcgen05 path): when norm_x is set the B operand is

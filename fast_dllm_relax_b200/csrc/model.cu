@@ -174,9 +174,9 @@ static int launch_tc_thunk(const GemmArgs& g, const void* a, const void* b, int 
 }
 
 static int launch_persist_thunk(const GemmArgs& g, const void* a, const void* b, int grid, cudaStream_t s) {
-  const int nt = g.n_tok_tiles * 256 >= g.M + 256 ? 128 : 256;  // recover the tile from the plan
-  return launch_gemm_tc_persist(g, *static_cast<const CUtensorMap*>(a), *static_cast<const CUtensorMap*>(b), nt, grid,
-                                s);
+  // the token tile is the one the B tensor map was encoded with (its box height)
+  return launch_gemm_tc_persist(g, *static_cast<const CUtensorMap*>(a), *static_cast<const CUtensorMap*>(b), g.tile_n,
+                                grid, s);
 }
 
 // The persistent large-tile GEMM from tune.persist_min_rows token rows (prefill, batched serving).
@@ -263,13 +263,15 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
     // 256-token tiles when they cover half the SMs, else 128 (twice the tiles for few-slab weights)
     const int pnt = 2 * g.n_slabs * ((M + 255) / 256) >= h->num_sms ? 256 : 128;
     g.n_tok_tiles = (M + pnt - 1) / pnt;
+    g.tile_n = pnt;
     const int tiles = g.n_slabs * g.n_tok_tiles;
     const int kblocks = g.K / 64;
-    // split K (<= 4 ways, >= 8 k blocks each) while the tiles alone leave SMs idle -- off unless
-    // tune.persist_splitk: measured slower (the last split's serial merge outweighs the idle SMs)
+    // Split K (<= 4 ways, >= 8 k blocks each) only when the tiles cover at most half the SMs (a
+    // few-slab projection of a short prefill); with more tiles the last split's serial merge costs
+    // more than the idle SMs (1024 rows: +30% per step).
     int splits = 1;
-    while (h->tune.persist_splitk && splits < 4 && tiles * splits < h->num_sms && kblocks / (2 * splits) >= 8)
-      splits *= 2;
+    if (h->tune.persist_splitk && tiles * 2 <= h->num_sms)
+      while (splits < 4 && tiles * splits < h->num_sms && kblocks / (2 * splits) >= 8) splits *= 2;
     g.splits = splits;
     g.kb_per_split = (kblocks + splits - 1) / splits;
     if (splits > 1) {
@@ -821,10 +823,18 @@ int fdllm_unmask(fdllm_handle* h, const int32_t* ids, const float* maxp, int row
 
 int fdllm_device_error(fdllm_handle* h, int* code) {
   if (h == nullptr || code == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
+  int w[4] = {0, 0, 0, 0};
+  FDLLM_TRY(fdllm_device_error_detail(h, w));
+  *code = w[0];
+  return FDLLM_OK;
+}
+
+int fdllm_device_error_detail(fdllm_handle* h, int32_t* out4) {
+  if (h == nullptr || out4 == nullptr) return fail(FDLLM_ERR_INVALID, "null argument");
   CUDA_TRY(cudaSetDevice(h->device));
   CUDA_TRY(cudaDeviceSynchronize());
-  CUDA_TRY(cudaMemcpy(code, h->err.p, sizeof(int), cudaMemcpyDeviceToHost));
-  CUDA_TRY(cudaMemset(h->err.p, 0, sizeof(int)));
+  CUDA_TRY(cudaMemcpy(out4, h->err.p, 4 * sizeof(int), cudaMemcpyDeviceToHost));
+  CUDA_TRY(cudaMemset(h->err.p, 0, 4 * sizeof(int)));
   return FDLLM_OK;
 }
 

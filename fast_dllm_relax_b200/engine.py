@@ -304,6 +304,13 @@ class Engine:
         _lib.check(self.lib.fdllm_device_error(self._h, ctypes.byref(code)))
         return code.value
 
+    def device_error_detail(self) -> list[int]:
+        """[code, wait site, token rows, block | splits << 16] of the first recorded device error
+        (zeros when none); clears the record."""
+        buf = (ctypes.c_int32 * 4)()
+        _lib.check(self.lib.fdllm_device_error_detail(self._h, buf))
+        return [int(x) for x in buf]
+
     def wait_selftest(self, limit_ns: int = 200_000_000) -> int:
         code = ctypes.c_int(0)
         _lib.check(self.lib.fdllm_wait_selftest(self._h, int(limit_ns), ctypes.byref(code)))

@@ -160,6 +160,13 @@ FDLLM_API int fdllm_generate(fdllm_handle* h, const int32_t* prompt, int prompt_
 /* Read and clear the handle's device error word (synchronises the device).  *code = 0 if none. */
 FDLLM_API int fdllm_device_error(fdllm_handle* h, int* code);
 
+/* fdllm_device_error with where an expired wait gave up (diagnostics; no counterpart in the
+ * reference): out[0] the code, and for a wait timeout out[1] the wait site (1-5 the per-tile
+ * projection GEMM's producer, drain, normaliser, MMA issuer and epilogue; 11-15 the persistent
+ * GEMM's producer, drain, MMA accumulator, MMA operand and epilogue waits), out[2] the call's token
+ * rows, out[3] the CTA's block index | split count << 16.  Clears all four words. */
+FDLLM_API int fdllm_device_error_detail(fdllm_handle* h, int32_t* out4);
+
 /* Failure-detection self test: launch a kernel that waits on a flag nothing sets, with a bounded
  * wait of limit_ns; it must give up, record its error code and leave the context usable. */
 FDLLM_API int fdllm_wait_selftest(fdllm_handle* h, unsigned long long limit_ns, int* code);
