@@ -405,6 +405,7 @@ int init_kernel_attributes() {
   if (e == cudaSuccess) e = attn_attrs<64, 1>();
   if (e == cudaSuccess) e = attn_attrs<64, 2>();
   if (e == cudaSuccess) e = static_cast<cudaError_t>(init_gemm_tc_attributes());
+  if (e == cudaSuccess) e = static_cast<cudaError_t>(init_attention_tc_attributes());
   return e;
 }
 

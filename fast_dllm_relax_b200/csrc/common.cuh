@@ -60,6 +60,12 @@ __device__ __forceinline__ float2 round2_bf16(float a, float b) {
   return __bfloat1622float2(__floats2bfloat162_rn(a, b));
 }
 
+// Two fp32 values rounded to bf16 and packed (lo in the low half).
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
 // ---- time / addresses ---------------------------------------------------------------------
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
@@ -70,19 +76,19 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // Kernel trace: tr[cta * kKtracePhases + p] = the %globaltimer value (ns) at which CTA `cta` (linear
 // block index) of one launch reached phase p (0 entry, 1 dependency wait passed, 2 main loop done,
 // 7 exit, the others kernel-specific); 0 = not reached.  Plain stores to distinct words: atomics
-// on one per-launch word serialise in L2 and delay the stamping thread.  Compiled in only with
-// FDLLM_KTRACE: even an untaken stamp costs the decode step about 1.5%.
+// on one per-launch word serialise in L2 and delay the stamping thread.  Phases 1 and 7 are always
+// compiled in (a null check when tracing is off): the span from the first CTA passing its
+// dependency wait to the last CTA leaving is the launch's share of the critical path.  The other
+// phases only with FDLLM_KTRACE: compiled in, even untaken, they cost the decode step about 1.5%.
 constexpr int kKtracePhases = 12;
 constexpr int kKtraceMaxCta = 1280;  // CTAs of one launch recorded
 __device__ __forceinline__ void ktrace_stamp(unsigned long long* tr, int phase) {
-#ifdef FDLLM_KTRACE
+#ifndef FDLLM_KTRACE
+  if (phase != 1 && phase != 7) return;
+#endif
   if (tr == nullptr) return;
   const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
   if (cta < static_cast<unsigned>(kKtraceMaxCta)) tr[cta * kKtracePhases + phase] = global_timer_ns();
-#else
-  (void)tr;
-  (void)phase;
-#endif
 }
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -232,6 +238,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 3D tiled load of box (c0 inner, c1, c2) into shared memory, completion on `bar` (CTA-local).
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(policy)
+      : "memory");
+}
+
 // ---- tcgen05: TMEM allocation, MMA, commit, loads ------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {  // whole warp
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)),
@@ -313,11 +329,28 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(const void* tile) {
   return d;
 }
 
+// UMMA shared-memory descriptor for an MN-major bf16 operand written by TMA with 128-byte swizzling:
+// rows of 64 MN-consecutive elements (128 B) along K, 8-row (K) groups `sbo` bytes apart, and the
+// next 64 MN elements `lbo` bytes further (the next 64-column TMA box).  Base 1024-byte aligned.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(const void* tile, uint32_t lbo, uint32_t sbo) {
+  const uint32_t a = smem_addr(tile);
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((a >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major, shape M x N.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
 }
+
+// Instruction descriptor as umma_idesc_bf16 with the B operand MN-major (transposed).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int m, int n) { return umma_idesc_bf16(m, n) | (1u << 16); }
 
 // ---- cp.async (Ampere-style 16-byte async copies, used by the attention kernel) -------------
 __device__ __forceinline__ void cp_async_16(void* dst, const void* src, bool valid) {

@@ -90,7 +90,10 @@ __global__ void __launch_bounds__(128, 4)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int slab = blockIdx.x, tile = blockIdx.y, split = blockIdx.z;
+  // tile-major grids (several token tiles, no split): the token tiles of one weight slab are
+  // neighbouring CTAs, so the slab streams from HBM once and the other tiles read it from L2
+  const int slab = g.tile_major ? blockIdx.y : blockIdx.x, tile = g.tile_major ? blockIdx.x : blockIdx.y;
+  const int split = blockIdx.z;
   const int tok0 = tile * NT;
   const int kb_total = g.K / 64;
   const int kb0 = split * g.kb_per_split;
@@ -587,7 +590,7 @@ int launch_gemm_tc_persist(const GemmArgs& a, const CUtensorMap& tmA, const CUte
 template <int NT>
 static int launch_nt(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, cudaStream_t s) {
   using C = TcCfg<NT>;
-  dim3 grid(a.n_slabs, a.n_tok_tiles, a.splits);
+  dim3 grid = a.tile_major ? dim3(a.n_tok_tiles, a.n_slabs, a.splits) : dim3(a.n_slabs, a.n_tok_tiles, a.splits);
   return launch_kc(gemm_tc_kernel<NT>, grid, dim3(128), C::kSmem, s, a.splits, tmA, tmB, a);
 }
 

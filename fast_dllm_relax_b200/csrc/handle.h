@@ -33,7 +33,8 @@ int fail(int code, const std::string& msg);
 // measured best on B200; the environment variable FDLLM_TUNING ("key=value,...", read by
 // fdllm_create) overrides them for experiments without rebuilding.
 struct Tuning {
-  int nt_max = 256;            // largest token tile of the per-tile projection GEMM: 64, 128 or 256
+  int nt_max = 128;            // largest token tile of the per-tile projection GEMM: 64, 128 or 256
+                               // (224-row prefill: 2.62 ms at 128 against 3.71 at 256)
   int split_target = 0;        // CTAs per SM the split-K plan aims for (0: 2 at <= 16 rows, else 1)
   int split_max = 16;          // largest split-K cluster of the per-tile GEMM
   int gemm_tune = kGemmTunePrefetch | (2 << kGemmTuneL2Shift);  // kGemmTune* bits
@@ -42,6 +43,7 @@ struct Tuning {
   int attn_splits = 0;         // attention key splits of decode-sized calls (0: planned)
   int gu_fused_rows = 16;      // gate_up normalises its own B tiles up to this many token rows
   int block_graph = 1;         // fdllm_generate runs whole blocks as device-looped CUDA graphs
+  int attn_tc_min_q = 64;      // tcgen05 attention from this many query tokens per request (0: never)
 };
 int parse_tuning(const char* spec, Tuning* t);
 
@@ -168,6 +170,7 @@ struct fdllm_handle {
   DevBuf<int> tok_req, tok_pos, tok_row, tmp_ids, targets;
   DevBuf<ReqDesc> reqs;
   DevBuf<float> conf_part, tmp_maxp, ss;  // ss: per-slab row sums of squares
+  DevBuf<CUtensorMap> attn_maps;            // tcgen05 attention: K and V tensor maps per request
   DevBuf<float> persist_part;               // persistent-GEMM split-K partial tiles
   DevBuf<unsigned> persist_ctr;             // persistent-GEMM per-tile split counters (zero between launches)
   // kernel trace (fdllm_kernel_trace_enable / _read): phase stamps of every projection and

@@ -89,6 +89,7 @@ struct GemmArgs {
   int n_slabs;              // N / 128 (or I / 64 when paired)
   int n_tok_tiles;
   int tile_n;               // persistent GEMM: token rows per tile (128 or 256; the B map's box height)
+  int tile_major;           // per-tile GEMM: grid (token tiles, slabs, splits) instead of (slabs, tiles, splits)
   int splits;               // split-K factor = cluster size (<= 16)
   int kb_per_split;         // 64-wide k blocks per split
   // Fused RMSNorm of the activations (tcgen05 path): when norm_x is set the B operand is
@@ -185,6 +186,10 @@ int gemm_tc_smem_bytes(int nt);
 int gemm_tc_stages(int nt);
 
 int launch_attention(const AttnArgs& a, int max_q, int dtype, cudaStream_t s);
+// tcgen05 attention (bf16, head_dim 128, no explicit bias): maps_dev holds two 3D tensor maps per
+// request (K then V: {kv_heads * head_dim, attended keys, layers}, box {64, 64, 1}, 128-byte swizzle).
+int launch_attention_tc(const AttnArgs& a, const CUtensorMap* maps_dev, int max_q, cudaStream_t s);
+int init_attention_tc_attributes();
 int init_kernel_attributes();  // opt-in shared memory sizes; once per device, before any capture
 
 int launch_embed(const int* ids, int n, const void* table, int vocab, int hidden, void* out, int dtype, int* err,

@@ -68,6 +68,25 @@ static int make_map(CUtensorMap* map, const void* base, int rows, int cols, int 
   return FDLLM_OK;
 }
 
+// K or V cache of one request as a 3D bf16 tensor {kv_heads * head_dim, keys, layers} (row stride
+// row_bytes, layer stride layer_bytes), box {64, 64, 1}, 128-byte swizzle.  `keys` is the attended
+// length, so keys past it read as zeros whatever the cache rows beyond it hold.
+static int make_kv_map(CUtensorMap* map, const void* base, int cols, int keys, int layers, size_t row_bytes,
+                       size_t layer_bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(FDLLM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return fail(FDLLM_ERR_INVALID, "KV cache must be 16-byte aligned");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(keys), static_cast<cuuint64_t>(layers)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(layer_bytes)};
+  cuuint32_t box[3] = {64, 64, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FDLLM_ERR_CUDA, "cuTensorMapEncodeTiled (KV) failed (" + std::to_string(r) + ")");
+  return FDLLM_OK;
+}
+
 size_t fdllm::round_up(size_t x, size_t m) { return (x + m - 1) / m * m; }
 
 // "key=value,key=value" over the Tuning fields; unknown keys or values out of range fail.
@@ -96,6 +115,7 @@ int fdllm::parse_tuning(const char* spec, Tuning* t) {
     else if (key == "attn_splits" && x >= 0 && x <= kMaxAttnSplits) t->attn_splits = x;
     else if (key == "gu_fused_rows" && x >= 0 && x <= 64) t->gu_fused_rows = x;
     else if (key == "block_graph" && (x == 0 || x == 1)) t->block_graph = x;
+    else if (key == "attn_tc_min_q" && x >= 0) t->attn_tc_min_q = x;
     else return fail(FDLLM_ERR_INVALID, "unknown tuning key or value out of range: " + item);
   }
   return FDLLM_OK;
@@ -218,6 +238,7 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
   }
   g->splits = splits;
   g->kb_per_split = (kblocks + splits - 1) / splits;
+  g->tile_major = (splits == 1 && g->n_tok_tiles > 1) ? 1 : 0;
   return nt;
 }
 
@@ -372,6 +393,29 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
   int n_splits, split_len;
   plan_attention(h, max_q, max_l, nreq, bias != nullptr || causal_block != 0, &n_splits, &split_len);
 
+  // tcgen05 attention for calls with many query tokens per request (prefill, batched steps): its
+  // per-request K/V tensor maps are encoded here and uploaded once for all layers.  Not inside a
+  // stream capture, and not for device-side prefix lengths (the maps carry the attended length).
+  bool attn_tc = h->dtype == FDLLM_BFLOAT16 && c.head_dim == 128 && bias == nullptr && !h->capturing &&
+                 h->tune.attn_tc_min_q > 0 && max_q >= h->tune.attn_tc_min_q &&
+                 c.num_attention_heads / c.num_key_value_heads <= 16;
+  for (const ReqDesc& r : reqs) attn_tc = attn_tc && r.plen_dev == nullptr && r.attend_len > 0;
+  if (attn_tc) {
+    std::vector<CUtensorMap> maps(2 * static_cast<size_t>(nreq));
+    const size_t row_bytes = static_cast<size_t>(c.num_key_value_heads) * c.head_dim * h->esz;
+    for (int i = 0; i < nreq; ++i) {
+      const ReqDesc& r = reqs[i];
+      const int layers = r.layer_stride != 0 ? c.num_hidden_layers : 1;
+      const size_t layer_bytes = static_cast<size_t>(r.cap) * row_bytes;
+      FDLLM_TRY(make_kv_map(&maps[2 * i], r.k, c.num_key_value_heads * c.head_dim, r.attend_len, layers, row_bytes,
+                            layer_bytes));
+      FDLLM_TRY(make_kv_map(&maps[2 * i + 1], r.v, c.num_key_value_heads * c.head_dim, r.attend_len, layers, row_bytes,
+                            layer_bytes));
+    }
+    FDLLM_TRY(h->attn_maps.ensure(maps.size()));
+    CUDA_TRY(cudaMemcpyAsync(h->attn_maps.p, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, s));
+  }
+
   Epilogue base{};
   base.hq = c.num_attention_heads;
   base.hkv = c.num_key_value_heads;
@@ -424,8 +468,12 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     a.split_len = split_len;
     a.m_total = M;
     a.err = h->err.p;
-    a.ktrace = h->dtype == FDLLM_BFLOAT16 ? ktrace_slot(h, 1) : nullptr;
-    CUDA_TRY(launch_attention(a, max_q, h->dtype, s));
+    a.ktrace = h->dtype == FDLLM_BFLOAT16 ? ktrace_slot(h, attn_tc ? 2 : 1) : nullptr;
+    if (attn_tc) {
+      CUDA_TRY(launch_attention_tc(a, h->attn_maps.p, max_q, s));
+    } else {
+      CUDA_TRY(launch_attention(a, max_q, h->dtype, s));
+    }
 
     e = base;
     e.kind = kEpiResidual;
@@ -580,6 +628,7 @@ int fdllm_destroy(fdllm_handle* h) {
   h->persist_part.release();
   h->persist_ctr.release();
   h->ktrace.release();
+  h->attn_maps.release();
   h->reqs.release();
   if (h->dec.host) cudaFreeHost(h->dec.host);
   if (h->dec.host_params) cudaFreeHost(h->dec.host_params);
@@ -883,9 +932,6 @@ int fdllm_profile_read(fdllm_handle* h, double* out4) {
 
 int fdllm_kernel_trace_enable(fdllm_handle* h, int enable) {
   if (h == nullptr) return fail(FDLLM_ERR_INVALID, "null handle");
-#ifndef FDLLM_KTRACE
-  if (enable != 0) return fail(FDLLM_ERR_UNSUPPORTED, "kernel trace not compiled in (build with FDLLM_KTRACE=1)");
-#endif
   std::lock_guard<std::mutex> lock(h->mu);
   CUDA_TRY(cudaSetDevice(h->device));
   CUDA_TRY(cudaDeviceSynchronize());

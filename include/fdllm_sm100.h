@@ -187,14 +187,16 @@ FDLLM_API long long fdllm_workspace_bytes(fdllm_handle* h);
  * GEMM and attention launch issued outside stream capture records the earliest and latest
  * %globaltimer value (ns) at which any of its CTAs reached phase p: out[24*i + 2p] and
  * out[24*i + 2p + 1] for launch i and p = 0..11 (UINT64_MAX / 0: not reached; the large-tile
- * persistent GEMM records nothing).  Phases: 0 entry, 1 dependency wait passed, 2 main loop done,
- * 7 exit; projection 3 accumulator drained from TMEM, 4 split-K partials summed, 5 epilogue done,
- * 6 post-norm arrival counted, 8 TMEM released; attention 3 partials published, 4 merge weights,
- * 5 merge done; 9-11 unused.  The stamps are compiled in only by `python -m fast_dllm_relax_b200.build --ktrace`
- * (they slow every launch); otherwise enabling returns FDLLM_ERR_UNSUPPORTED.
- * kinds[i]: 1 attention; 100 + epilogue kind for a projection, +1000 with the post-norm, +2000
- * with the fused input norm.  Enabling, and every read, clears the record; at most 512
- * launches (1280 CTAs each) are kept.  Both calls synchronise the device.  With out == NULL only *n is written. */
+ * persistent GEMM records nothing).  Always recorded: phase 1 (dependency wait passed) and 7 (exit);
+ * the span from the earliest phase-1 stamp to the latest exit is the launch's share of the step's
+ * critical path under programmatic dependent launch.  A build with
+ * `python -m fast_dllm_relax_b200.build --ktrace` also records 0 entry, 2 main loop done;
+ * projection 3 accumulator drained from TMEM, 4 split-K partials summed, 5 epilogue done,
+ * 8 TMEM released; attention 3 partials published, 4 merge weights, 5 merge done (those stamps
+ * slow every launch).  kinds[i]: 1 attention (mma.sync), 2 attention (tcgen05); 100 + epilogue kind
+ * for a projection, +2000 with the fused input norm.  Enabling, and every read, clears the
+ * record; at most 512 launches (1280 CTAs each) are kept.  Both calls synchronise the device.
+ * With out == NULL only *n is written. */
 FDLLM_API int fdllm_kernel_trace_enable(fdllm_handle* h, int enable);
 FDLLM_API int fdllm_kernel_trace_read(fdllm_handle* h, uint64_t* out, int32_t* kinds, int cap, int32_t* n);
 

@@ -1,0 +1,116 @@
+"""The tcgen05 attention (csrc/attention_tc.cu) against the oracle and against the mma.sync
+attention it replaces for calls with many query tokens.
+
+Two engines share one set of MID weights (the 1.5B layer shapes, 2 layers): the default one runs
+attention on the tensor cores from 64 query tokens per request; the other has it turned off
+(FDLLM_TUNING=attn_tc_min_q=0) and runs the legacy kernel everywhere.  Prefix builds (single and
+batched, ragged lengths that leave partial 21-token tiles and partial 64-key tiles), a dense
+forward_hidden and a batched cached forward must agree with the oracle at the bf16 noise floor
+(tests/_oracle_util.assert_within_bf16_noise) and with each other as two GPU plans of the same
+arithmetic.
+"""
+
+import pytest
+import torch
+
+from fast_dllm_relax_b200.config import ModelConfig, make_synthetic_params
+from oracle.model import build_block_bias
+from tests._oracle_util import assert_within_bf16_noise, bf16_discrepancy, make_oracle, make_reordered_oracle
+
+pytestmark = pytest.mark.gpu
+
+MID = ModelConfig(vocab_size=4096, hidden_size=1536, intermediate_size=8960, num_hidden_layers=2,
+                  num_attention_heads=12, num_key_value_heads=2, head_dim=128, context_window_size=8192)
+
+
+def _dev():
+    return torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module")
+def engines():
+    import os
+
+    from fast_dllm_relax_b200.engine import Engine
+    params = make_synthetic_params(MID, seed=21, dtype="bfloat16", mask_id=4095)
+    dev_params = [p.to(_dev()) for p in params]
+    old = os.environ.get("FDLLM_TUNING")
+    try:
+        os.environ["FDLLM_TUNING"] = ""
+        tc = Engine(MID, dev_params, dtype="bfloat16")
+        os.environ["FDLLM_TUNING"] = "attn_tc_min_q=0"
+        legacy = Engine(MID, dev_params, dtype="bfloat16")
+    finally:
+        if old is None:
+            os.environ.pop("FDLLM_TUNING", None)
+        else:
+            os.environ["FDLLM_TUNING"] = old
+    return tc, legacy, make_oracle(MID, params, "bfloat16"), make_reordered_oracle(MID, params, "bfloat16")
+
+
+def _act(n, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn((1, n, MID.hidden_size), generator=g).to(torch.bfloat16)
+
+
+def _consistent(a, b, label):
+    d = bf16_discrepancy(a, b)
+    assert d["out"] <= 1e-3 and d["rel"] <= 1e-2, f"{label}: {d}"
+
+
+@pytest.mark.parametrize("P", [64, 96, 200, 1000])
+def test_prefix_build_matches_oracle_and_legacy(engines, P):
+    tc, legacy, orc, alt = engines
+    x = _act(P, P)
+    caches = []
+    for eng in (tc, legacy):
+        k, v = eng.new_cache(P + 32)
+        eng.build_prefix_cache(x.to(_dev()), None, k, v)
+        caches.append((k[:, :, :P].cpu(), v[:, :, :P].cpu()))
+    ref = [torch.zeros((2, 1, P + 32, 2, 128), dtype=torch.bfloat16) for _ in range(4)]
+    orc.build_prefix_cache(x, build_block_bias(0, P, 32), ref[0], ref[1])
+    alt.build_prefix_cache(x, build_block_bias(0, P, 32), ref[2], ref[3])
+    for i, name in ((0, "k"), (1, "v")):
+        assert_within_bf16_noise(caches[0][i], ref[i][:, :, :P], ref[2 + i][:, :, :P], f"P={P} {name} vs oracle")
+        _consistent(caches[0][i], caches[1][i], f"P={P} {name} tcgen05 vs legacy")
+    assert tc.device_error() == 0 and legacy.device_error() == 0
+
+
+def test_forward_hidden_matches_oracle(engines):
+    tc, legacy, orc, alt = engines
+    T = 160
+    x = _act(T, 7)
+    bias = build_block_bias(0, T, 32)
+    got = tc.forward_hidden(x.to(_dev()), None)
+    assert_within_bf16_noise(got, orc.forward_hidden(x, bias), alt.forward_hidden(x, bias), "forward_hidden")
+    _consistent(got, legacy.forward_hidden(x.to(_dev()), None), "forward_hidden tcgen05 vs legacy")
+    assert tc.device_error() == 0
+
+
+def test_batched_ragged_prefix_and_cached_forward(engines):
+    """Ragged prefixes in one batched build, then one batched cached forward of 96 rows per
+    request (the cached path: every row attends the whole window)."""
+    tc, legacy, orc, alt = engines
+    lens = [70, 130, 64, 200]
+    xs = [_act(P, 100 + i) for i, P in enumerate(lens)]
+    out = {}
+    for name, eng in (("tc", tc), ("legacy", legacy)):
+        caches = [eng.new_cache(P + 96) for P in lens]
+        eng.build_prefix_cache_batch(torch.cat([x[0] for x in xs]).to(_dev()), caches, lens)
+        blocks = [_act(96, 200 + i) for i in range(len(lens))]
+        reqs = [dict(k=k, v=v, rows=96, prefix_len=P) for (k, v), P in zip(caches, lens)]
+        h = eng.forward_cached_batch(torch.cat([b[0] for b in blocks]).to(_dev()), reqs)
+        out[name] = (h.cpu(), [(k.cpu(), v.cpu()) for k, v in caches], blocks)
+    h_tc, caches_tc, blocks = out["tc"]
+    _consistent(h_tc, out["legacy"][0], "batched cached forward tcgen05 vs legacy")
+    o = 0
+    for i, P in enumerate(lens):
+        kr, vr, ka, va = [torch.zeros((2, 1, P + 96, 2, 128), dtype=torch.bfloat16) for _ in range(4)]
+        orc.build_prefix_cache(xs[i], build_block_bias(0, P, 32), kr, vr)
+        alt.build_prefix_cache(xs[i], build_block_bias(0, P, 32), ka, va)
+        assert_within_bf16_noise(caches_tc[i][0][:, :, :P], kr[:, :, :P], ka[:, :, :P], f"request {i} prefix k")
+        hr = orc.forward_cached(blocks[i], kr, vr, P, P)
+        ha = alt.forward_cached(blocks[i], ka, va, P, P)
+        assert_within_bf16_noise(h_tc[o:o + 96], hr[0], ha[0], f"request {i} cached forward")
+        o += 96
+    assert tc.device_error() == 0 and legacy.device_error() == 0
