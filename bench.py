@@ -14,8 +14,15 @@ value: decode tokens/s over all ranks = generated tokens / (generation time - pr
 reference's definition (fast_dllm_relax/runners.py:748-750), with device time from CUDA events
 inside the native driver (the max over ranks).  e2e: the same metric through the public call
 (Engine.generate: host prompt in, host tokens out, per-step host reads) on the host clock.
-roofline: the projection GEMM (tcgen05) -- algorithmic bytes (weights + activations + outputs) per
-launch over its CUDA-event duration, against the measured HBM copy bandwidth.
+roofline: the projection GEMM (tcgen05) in situ -- every projection launch of an eager 32-row
+refinement step at prefix 384 carries its dependency-wait and exit stamps (%globaltimer, programmatic
+launch kept); a launch's time is the span from its first CTA passing the wait (its predecessor done)
+to its last CTA leaving, so the spans partition the step's critical path and their sum stays under
+the step's CUDA-event time.  achieved = algorithmic bytes (weights + activations + outputs) over
+that time, against the measured HBM copy bandwidth; per projection and for the attention too.
+workloads: BASELINE configs[2] (32 requests per GPU, prompt 512, generate 512), configs[3] (8
+requests of prompt 4096, generate 256, split over the GPUs) and configs[4] (1024 sequences of a
+512-token context + 16-token continuation scored, batch 64 per GPU) at the same N.
 step_roofline: one whole 32-row (and 8-row partial) refinement step at prefix 384 -- the slower of
 (weights + KV bytes) / HBM and FLOPs / bf16 tensor peak, over the step's CUDA-event time, against
 the measured peaks and the nominal 8 TB/s and 2.25 PFLOP/s.
@@ -82,6 +89,92 @@ def step_roofline(rows: int, prefix: int, ms: float, hbm_gbs: float, tensor_tflo
         floor_ms = max(nbytes / (bw * 1e9), flops / (tf * 1e12)) * 1e3
         out[tag] = {"hbm_gbs": bw, "bf16_tflops": tf, "floor_ms": floor_ms,
                     "frac": floor_ms / ms if ms > 0 else None}
+    return out
+
+
+# Algorithmic bytes of one projection launch over `rows` token rows (bf16): weights + activations in
+# + outputs, as the library counts them (csrc/model.cu gemm_bytes).
+H, I, HQKV, V_SLABS = 1536, 8960, 2048, 1187
+
+
+def _proj_bytes(name: str, rows: int) -> float:
+    n, k, out = {"qkv": (HQKV, H, rows * HQKV * 2), "o": (H, H, 2 * rows * H * 2),
+                 "gate_up": (2 * I, H, rows * I * 2), "down": (H, I, 2 * rows * H * 2),
+                 "lm_head": (151936, H, 16 * rows * V_SLABS)}[name]
+    return n * k * 2 + rows * k * 2 + out
+
+
+def in_situ_step(eng, torch, dev, peak_gbs: float, rows: int = 32, prefix: int = 384, steps: int = 3) -> dict:
+    """Critical-path attribution of the eager refinement step (embed, forward_cached, fused lm_head
+    + confidence, unmask) at `prefix`, from the always-on launch stamps of the projection and
+    attention kernels (fdllm_kernel_trace_*): each launch's span runs from its first CTA past the
+    dependency wait to its last CTA's exit.  Median over `steps` steps."""
+    from fast_dllm_relax_b200.config import QWEN_MASK_ID
+    k, v = eng.new_cache(prefix + BLOCK)
+    k.normal_(0, 0.5)
+    v.normal_(0, 0.5)
+    block = torch.randint(0, 151000, (BLOCK,), device=dev, dtype=torch.int32)
+    block[8:] = QWEN_MASK_ID
+
+    def step():
+        if rows == BLOCK:
+            h = eng.forward_cached(eng.embed(block)[None], k, v, prefix, prefix)
+        else:
+            h = eng.forward_block_partial(eng.embed(block[8:16])[None], k, v, prefix + 8, prefix, 8)
+        i, m = eng.confidence(h)
+        eng.unmask(i, m, block.clone(), 8, 8, rows != BLOCK, QWEN_MASK_ID, THRESHOLD)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    eng.kernel_trace_enable(True)
+    recs = []
+    for _ in range(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        torch.cuda.synchronize()
+        stamps, kinds = eng.kernel_trace_read()
+        spans = [(int(kd), (int(st[7, 1]) - int(st[1, 0])) / 1e6) for st, kd in zip(stamps, kinds)
+                 if st[1, 0] != 0xFFFFFFFFFFFFFFFF and st[7, 1] != 0]
+        recs.append((e0.elapsed_time(e1), spans))
+    eng.kernel_trace_enable(False)
+    step_ms, spans = sorted(recs, key=lambda r: r[0])[len(recs) // 2]
+    groups: dict[str, list[float]] = {n: [] for n in ("qkv", "attention", "o", "gate_up", "down", "lm_head")}
+    seen_o = False
+    for kd, ms in spans:
+        base = kd % 1000
+        if kd in (1, 2):
+            groups["attention"].append(ms)
+            seen_o = False
+        elif base == 101:
+            groups["qkv"].append(ms)
+        elif base == 102:
+            groups["down" if seen_o else "o"].append(ms)
+            seen_o = not seen_o
+        elif base == 103:
+            groups["gate_up"].append(ms)
+        elif base == 105:
+            groups["lm_head"].append(ms)
+    out: dict = {"rows": rows, "prefix": prefix, "step_ms": step_ms,
+                 "stamped_ms": sum(ms for _, ms in spans), "launches": len(spans), "per_kernel": {}}
+    gemm_bytes = gemm_ms = 0.0
+    for name, ms_list in groups.items():
+        if not ms_list:
+            continue
+        tot = sum(ms_list)
+        if name == "attention":
+            nbytes = len(ms_list) * ((prefix + BLOCK) * 1024 + 2 * rows * H * 2)
+        else:
+            nbytes = len(ms_list) * _proj_bytes(name, rows)
+            gemm_bytes += nbytes
+            gemm_ms += tot
+        gbs = nbytes / (tot / 1e3) / 1e9
+        out["per_kernel"][name] = {"launches": len(ms_list), "ms": tot, "us_per_launch": 1e3 * tot / len(ms_list),
+                                   "gbs": gbs, "frac": gbs / peak_gbs}
+    out["gemm"] = {"launches": sum(len(groups[n]) for n in groups if n != "attention"), "ms": gemm_ms,
+                   "bytes": gemm_bytes, "gbs": gemm_bytes / (gemm_ms / 1e3) / 1e9 if gemm_ms else None}
     return out
 
 
@@ -266,6 +359,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--block-cache", action="store_true", help="use_block_cache=True (partial 8-row steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--headline-only", action="store_true", help="skip the configs[2]-[4] workloads")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -319,17 +413,6 @@ def main() -> None:
             dist.barrier()
     launches = Engine.kernel_launches() - launches0
 
-    # Roofline of the dominant kernel: one more generation with a CUDA-event pair around every
-    # projection-GEMM launch (captured as event nodes of the step graphs).  Timed apart from the
-    # headline run because the event nodes break the programmatic overlap between kernels.
-    eng.profile_enable(True)
-    eng.generate(prompt, **gen_kw)  # captures the profiled step graphs
-    eng.profile_read()
-    eng.generate(prompt, **gen_kw)
-    torch.cuda.synchronize()
-    eng.profile_enable(False)
-    prof = eng.profile_read()
-
     # e2e: the same generations through the public call on the host clock (pinned-free host lists)
     torch.cuda.synchronize()
     e2e_tokens, e2e_dec_s, e2e_pref_ms = 0, 0.0, 0.0
@@ -352,14 +435,18 @@ def main() -> None:
         alt_dec_ms += t["total_ms"] - t["prefill_ms"]
     # ms per 32-token block step (embed + forward_cached(32) + fused confidence + unmask) at P = 384
     blk = block_step_ms(eng, torch, dev)
+    peak, peak_kind = _peaks()
+    situ = in_situ_step(eng, torch, dev, peak)
+    situ_partial = in_situ_step(eng, torch, dev, peak, rows=SUB_BLOCK)
+    # BASELINE configs[2]-[4] at this N (every rank runs them; collectives in the same order)
+    loads = {} if args.headline_only else workloads(eng, torch, dev, world, rank)
 
     # off the decode path: max over ranks of the device-timed durations, sum of the work
     (dec_ms, tot_ms, e2e_dec_s, alt_dec_ms), (tokens, launches, e2e_tokens, alt_tokens) = dp.reduce_max_sum(
         [dec_ms, tot_ms, e2e_dec_s, alt_dec_ms], [tokens, launches, e2e_tokens, alt_tokens], device=dev)
 
     if rank == 0:
-        peak, peak_kind = _peaks()
-        achieved = prof["bytes"] / (prof["ms"] / 1e3) / 1e9 if prof["ms"] > 0 else 0.0
+        achieved = situ["gemm"]["gbs"] or 0.0
         tr = _traffic()
         steps_per_gen = stats_acc["block_recomputes"] if stats_acc else 0
         n_blocks = (stats_acc["block_appends"] + 1) if stats_acc else 0
@@ -380,19 +467,23 @@ def main() -> None:
             "prefill_ms": (tot_ms - dec_ms) / args.steps,
             "e2e": {"value": e2e_tokens / e2e_dec_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "path": "Engine.generate -> fdllm_generate (host buffers)"},
-            "roofline": {"bound": "hbm", "kernel": "gemm_tc_kernel (tcgen05 projection GEMM)",
+            "roofline": {"bound": "hbm", "kernel": "gemm_tc_kernel (tcgen05 projection GEMM, in situ)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak if peak else None, "peak_kind": peak_kind,
                          "traffic": tr.get("bytes_per_launch") if tr else None,
-                         "algorithmic_bytes_per_launch": prof["bytes"] / max(1, prof["launches"]),
-                         "avg_launch_us": 1e3 * prof["ms"] / max(1, prof["launches"]),
-                         "launches": prof["launches"]},
+                         "algorithmic_bytes_per_launch": situ["gemm"]["bytes"] / max(1, situ["gemm"]["launches"]),
+                         "avg_launch_us": 1e3 * situ["gemm"]["ms"] / max(1, situ["gemm"]["launches"]),
+                         "launches": situ["gemm"]["launches"],
+                         "timing": "launch stamps inside the eager 32-row step at prefix 384 (programmatic "
+                                   "launch kept): first CTA past the dependency wait to last CTA exit",
+                         "in_situ": situ, "in_situ_partial": situ_partial},
             "step_roofline": {
                 "full": step_roofline(BLOCK, 384, blk["full_ms"], peak, _tensor_peak()[0]),
                 "partial": step_roofline(SUB_BLOCK, 384, blk["partial_ms"], peak, _tensor_peak()[0]),
                 "bound": "hbm", "peak_kind": f"{peak_kind} / nominal 8 TB/s, 2.25 PFLOP/s"},
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
+            "workloads": loads,
         }
         if world == 1 and not args.no_cpu_baseline:
             params_cpu = [p.cpu() for p in params]
@@ -401,6 +492,77 @@ def main() -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def workloads(eng, torch, dev, world: int, rank: int) -> dict:
+    """BASELINE configs[2]-[4] on this engine, data-parallel by request over the ranks (no
+    collective while decoding; the max over ranks of the device time and the sum of the work are
+    reduced after each).  Device time from CUDA events; decode tokens/s excludes the prefix-cache
+    builds (runners.py:748-750)."""
+    import numpy as np
+
+    from fast_dllm_relax_b200 import dp
+    from fast_dllm_relax_b200.batch_decode import generate_batch
+    from fast_dllm_relax_b200.config import QWEN_MASK_ID
+    from fast_dllm_relax_b200.scorebench import EOS_ID, score_batch
+
+    out = {}
+    kw = dict(mask_id=QWEN_MASK_ID, use_block_cache=False)
+
+    def serve(name, n_total, per_gpu, prompt_len, gen, desc):
+        mine = dp.request_range(n_total, world, rank) if per_gpu is None else range(rank * per_gpu, (rank + 1) * per_gpu)
+        prompts = [np.random.default_rng(1000 + i).integers(0, 151000, prompt_len).tolist() for i in mine]
+        if prompts:
+            generate_batch(eng, prompts, max_new_tokens=32, **kw)  # warm-up: allocations, kernels
+        torch.cuda.synchronize()
+        t = {}
+        toks = generate_batch(eng, prompts, max_new_tokens=gen, timing=t, **kw)[0] if prompts else []
+        dec = (t["total_ms"] - t["prefill_ms"]) if prompts else 0.0
+        (dec_ms, tot_ms, pre_ms), (n_tok, n_req) = dp.reduce_max_sum(
+            [dec, t.get("total_ms", 0.0), t.get("prefill_ms", 0.0)], [sum(len(x) for x in toks), len(prompts)],
+            device=dev)
+        out[name] = {"workload": desc, "metric": "decode tokens/s", "value": n_tok / (dec_ms / 1e3) if dec_ms else None,
+                     "unit": "tokens/s", "requests": int(n_req), "tokens": int(n_tok), "decode_ms": dec_ms,
+                     "prefill_ms": pre_ms, "total_ms": tot_ms}
+
+    serve("serving", None, 32, 512, 512,
+          "BASELINE configs[2]: 1.5B bf16, 32 requests per GPU (prompt 512, generate 512), block 32, threshold 0.9")
+    serve("long_prefix", 8, None, 4096, 256,
+          "BASELINE configs[3]: 1.5B bf16, 8 requests (prompt 4096, generate 256) split over the GPUs")
+
+    # configs[4]: masked-continuation scoring, 1024 sequences split over the GPUs, batch 64 per GPU
+    n_seq, C, N, B = 1024, 512, 16, 64
+    mine = list(dp.request_range(n_seq, world, rank))
+    n = len(mine)
+    g = torch.Generator().manual_seed(2000 + (mine[0] if mine else 0))
+    ctx = torch.randint(0, 151000, (n, C), generator=g, dtype=torch.int32).to(dev)
+    cont = torch.randint(0, 151000, (n, N), generator=g, dtype=torch.int32)
+    blocks = torch.full((n, 32), QWEN_MASK_ID, dtype=torch.int32)
+    blocks[:, N] = EOS_ID
+    targets = torch.zeros((n, 32), dtype=torch.int32)
+    targets[:, :N] = cont
+    blocks, targets = blocks.to(dev), targets.to(dev)
+    caches = [eng.new_cache(C + 32) for _ in range(min(B, max(n, 1)))]
+
+    def run(lo, hi):
+        return [score_batch(eng, caches, ctx[s0:min(s0 + B, hi)], blocks[s0:min(s0 + B, hi)],
+                            targets[s0:min(s0 + B, hi)], N) for s0 in range(lo, hi, B)]
+
+    if n:
+        run(0, min(n, B))
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    scores = run(0, n)
+    e1.record()
+    e1.synchronize()
+    finite = float(bool(torch.cat(scores).isfinite().all())) if scores else 1.0
+    (ms,), (n_all, fin) = dp.reduce_max_sum([e0.elapsed_time(e1)], [n, finite], device=dev)
+    out["scoring"] = {"workload": "BASELINE configs[4]: 1.5B bf16, 1024 sequences (context 512 + continuation "
+                                  "16) split over the GPUs, batch 64 per GPU, device log-softmax gather",
+                      "metric": "scored sequences/s", "value": n_all / (ms / 1e3), "unit": "sequences/s",
+                      "sequences": int(n_all), "ms": ms, "scores_finite": fin == world}
+    return out
 
 
 def block_step_ms(eng, torch, dev, iters: int = 20) -> dict:

@@ -59,12 +59,12 @@ __device__ __forceinline__ uint32_t tile_off(int key, int c) {
 
 // At most 6 query heads per KV head (192 threads).  MINB = 2 (two CTAs per SM, <= 170 registers)
 // for launches with more CTAs than SMs; MINB = 1 keeps every accumulator in registers.
-template <int HD, int MINB>
+template <int HD, int MINB, bool KT>
 __global__ void __launch_bounds__(192, MINB) attn_mma_kernel(const AttnArgs a) {
-  if (threadIdx.x == 0) ktrace_stamp(a.ktrace, 0);
+  if (threadIdx.x == 0) ktrace_stamp<KT>(a.ktrace, 0);
   pdl_trigger();
   pdl_wait();
-  if (threadIdx.x == 0) ktrace_stamp(a.ktrace, 1);
+  if (threadIdx.x == 0) ktrace_stamp<KT>(a.ktrace, 1);
   constexpr int kChunks = HD / 8;          // 16-byte chunks per key row
   constexpr int kTileBytes = kKT * HD * 2;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(192, MINB) attn_mma_kernel(const AttnArgs a) {
     l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
     l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
   }
-  if (threadIdx.x == 0) ktrace_stamp(a.ktrace, 2);
+  if (threadIdx.x == 0) ktrace_stamp<KT>(a.ktrace, 2);
   if (a.n_splits == 1) {
     bf16* out = static_cast<bf16*>(a.out);
 #pragma unroll
@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(192, MINB) attn_mma_kernel(const AttnArgs a) {
       if (t4 == 0) s_lse[rr] = (valid_row[h] && l_run[h] > 0.f) ? m_run[h] + logf(l_run[h]) : -INFINITY;
     }
     cluster_sync();  // every member's partial is in its shared memory
-    if (threadIdx.x == 0) ktrace_stamp(a.ktrace, 3);
+    if (threadIdx.x == 0) ktrace_stamp<KT>(a.ktrace, 3);
     constexpr int kMaxS = kMaxAttnSplits;
     const uint32_t S = static_cast<uint32_t>(a.n_splits);
     const uint32_t rank = cluster_ctarank();
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(192, MINB) attn_mma_kernel(const AttnArgs a) {
       s_w[rr - r0][kMaxS] = den > 0.f ? 1.f / den : 0.f;
     }
     __syncthreads();
-    if (threadIdx.x == 0) ktrace_stamp(a.ktrace, 4);
+    if (threadIdx.x == 0) ktrace_stamp<KT>(a.ktrace, 4);
     bf16* out = static_cast<bf16*>(a.out);
     for (int idx = threadIdx.x; idx < (r1 - r0) * (HD / 4); idx += blockDim.x) {
       const int rr = r0 + idx / (HD / 4), c4 = idx % (HD / 4);
@@ -322,10 +322,10 @@ __global__ void __launch_bounds__(192, MINB) attn_mma_kernel(const AttnArgs a) {
       *reinterpret_cast<__nv_bfloat162*>(op) = __floats2bfloat162_rn(num.x * inv, num.y * inv);
       *reinterpret_cast<__nv_bfloat162*>(op + 2) = __floats2bfloat162_rn(num.z * inv, num.w * inv);
     }
-    if (threadIdx.x == 0) ktrace_stamp(a.ktrace, 5);
+    if (threadIdx.x == 0) ktrace_stamp<KT>(a.ktrace, 5);
     cluster_sync();  // no member leaves while another may still read its shared memory
   }
-  if (threadIdx.x == 0) ktrace_stamp(a.ktrace, 7);
+  if (threadIdx.x == 0) ktrace_stamp<KT>(a.ktrace, 7);
 }
 
 // CUDA-core attention: one warp per (token, query head); dims split over lanes (hd <= 128).
@@ -382,20 +382,30 @@ static int launch_mma(const AttnArgs& a, int max_q, cudaStream_t s) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (static_cast<long long>(grid.x) * grid.y * grid.z > sms)
-    e = launch_kc(attn_mma_kernel<HD, 2>, grid, dim3(G * 32), smem, s, a.n_splits, a);
+  const bool many = static_cast<long long>(grid.x) * grid.y * grid.z > sms;
+  if (a.ktrace != nullptr)
+    e = many ? launch_kc(attn_mma_kernel<HD, 2, true>, grid, dim3(G * 32), smem, s, a.n_splits, a)
+             : launch_kc(attn_mma_kernel<HD, 1, true>, grid, dim3(G * 32), smem, s, a.n_splits, a);
   else
-    e = launch_kc(attn_mma_kernel<HD, 1>, grid, dim3(G * 32), smem, s, a.n_splits, a);
+    e = many ? launch_kc(attn_mma_kernel<HD, 2, false>, grid, dim3(G * 32), smem, s, a.n_splits, a)
+             : launch_kc(attn_mma_kernel<HD, 1, false>, grid, dim3(G * 32), smem, s, a.n_splits, a);
   return e;
 }
 
 int init_gemm_tc_attributes();
 
+template <int HD, int MINB, bool KT>
+static cudaError_t attn_attrs1() {
+  cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<HD, MINB, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       2 * kKV * kKT * HD * 2);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_mma_kernel<HD, MINB, KT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
+}
+
 template <int HD, int MINB>
 static cudaError_t attn_attrs() {
-  cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<HD, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       2 * kKV * kKT * HD * 2);
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_mma_kernel<HD, MINB>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t e = attn_attrs1<HD, MINB, false>();
+  if (e == cudaSuccess) e = attn_attrs1<HD, MINB, true>();
   return e;
 }
 

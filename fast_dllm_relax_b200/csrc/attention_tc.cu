@@ -94,12 +94,13 @@ __device__ __forceinline__ bool fold_o(float (&o)[128], int i, float alpha, TcBa
 
 }  // namespace
 
+template <bool KT>
 __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const AttnArgs a, const CUtensorMap* maps, int tq) {
   // The request table, Q and this layer's K/V rows come from kernels earlier in the stream (the
   // per-call prepare kernel among them): wait for them before reading anything.
   pdl_wait();
   pdl_trigger();
-  if (threadIdx.x == 0) ktrace_stamp(a.ktrace, 1);
+  if (threadIdx.x == 0) ktrace_stamp<KT>(a.ktrace, 1);
   const int G = a.hq / a.hkv;
   const int qtile = blockIdx.x, kvh = blockIdx.y, req = blockIdx.z;
   const ReqDesc r = a.reqs[req];
@@ -340,13 +341,15 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const AttnArgs a, const
     tc_fence_after_sync();
     tmem_dealloc(tmem, 512);
   }
-  if (threadIdx.x == 0) ktrace_stamp(a.ktrace, 7);
+  if (threadIdx.x == 0) ktrace_stamp<KT>(a.ktrace, 7);
 }
 
 int attention_tc_smem_bytes() { return kSmem; }
 
 int init_attention_tc_attributes() {
-  return cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  return e;
 }
 
 int launch_attention_tc(const AttnArgs& a, const CUtensorMap* maps_dev, int max_q, cudaStream_t s) {
@@ -354,7 +357,8 @@ int launch_attention_tc(const AttnArgs& a, const CUtensorMap* maps_dev, int max_
   if (a.hd != 128 || G < 1 || G > kRows / 8) return cudaErrorInvalidValue;
   const int tq = kRows / G;
   dim3 grid((max_q + tq - 1) / tq, a.hkv, a.n_reqs);
-  return launch_k(attn_tc_kernel, grid, dim3(192), kSmem, s, a, maps_dev, tq);
+  if (a.ktrace != nullptr) return launch_k(attn_tc_kernel<true>, grid, dim3(192), kSmem, s, a, maps_dev, tq);
+  return launch_k(attn_tc_kernel<false>, grid, dim3(192), kSmem, s, a, maps_dev, tq);
 }
 
 }  // namespace fdllm

@@ -79,10 +79,14 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 // on one per-launch word serialise in L2 and delay the stamping thread.  Phases 1 and 7 are always
 // compiled in (a null check when tracing is off): the span from the first CTA passing its
 // dependency wait to the last CTA leaving is the launch's share of the critical path.  The other
-// phases only with FDLLM_KTRACE: compiled in, even untaken, they cost the decode step about 1.5%.
+// phases only with FDLLM_KTRACE (compiled in, they slow every traced launch).
+// Kernels that stamp come in two instantiations (kOn): the launch takes the stamping one only when
+// a trace slot is attached, so an untraced launch carries no stamp code at all.
 constexpr int kKtracePhases = 12;
 constexpr int kKtraceMaxCta = 1280;  // CTAs of one launch recorded
+template <bool kOn>
 __device__ __forceinline__ void ktrace_stamp(unsigned long long* tr, int phase) {
+  if constexpr (!kOn) return;
 #ifndef FDLLM_KTRACE
   if (phase != 1 && phase != 7) return;
 #endif

@@ -71,7 +71,7 @@ struct TcCfg {
 
 // At most 128 registers a thread (min 4 blocks): a CTA must fit beside a 192-thread attention CTA
 // of up to 256 registers a thread in one SM's 64K registers for programmatic launch to overlap them.
-template <int NT>
+template <int NT, bool KT>
 __global__ void __launch_bounds__(128, 4)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmArgs g) {
@@ -101,7 +101,7 @@ __global__ void __launch_bounds__(128, 4)
   const int nk = max(kb1 - kb0, 0);
 
   if (threadIdx.x == 0) {
-    ktrace_stamp(g.ktrace, 0);
+    ktrace_stamp<KT>(g.ktrace, 0);
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&ready[s], 2);  // one arrival per normalizing warp
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(128, 4)
     }
     for (int i = pre; i < pre + l2_ahead; ++i) prefetch_a(i);  // and a few more into L2
     pdl_wait();
-    ktrace_stamp(g.ktrace, 1);
+    ktrace_stamp<KT>(g.ktrace, 1);
     for (int i = 0; i < pre; ++i) load_b(i);
     int issued = pre;
     for (int i = pre; i < nk; ++i) {
@@ -276,7 +276,7 @@ __global__ void __launch_bounds__(128, 4)
   if (NT <= 64 && (g.tune & kGemmTunePrefetch))
     epi_prefetch<bf16>(g, tok0, slab, S > 1 ? lr0 : 0, S > 1 ? lr1 : NT, threadIdx.x, blockDim.x, pre);
   if (!mbar_wait(accf, 0)) report_wait(g.err, kErrTimeoutEpilogue, 5, g.M, g.splits);
-  if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 2);
+  if (threadIdx.x == 0) ktrace_stamp<KT>(g.ktrace, 2);
   tc_fence_after_sync();
   __syncthreads();  // the producer's drain is complete before the ring is overwritten
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
@@ -304,11 +304,11 @@ __global__ void __launch_bounds__(128, 4)
     if (ch == NT / C::kChunk - 1) {  // every column drained: free TMEM
       tc_fence_before_sync();
       __syncthreads();
-      if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 3);
+      if (threadIdx.x == 0) ktrace_stamp<KT>(g.ktrace, 3);
       if (warp == 0) {
         tc_fence_after_sync();
         tmem_dealloc(tmem, C::kTmemCols);
-        if (lane == 0) ktrace_stamp(g.ktrace, 8);
+        if (lane == 0) ktrace_stamp<KT>(g.ktrace, 8);
       }
     } else {
       __syncthreads();
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(128, 4)
         acc4[c] = sum;  // only this member reads or writes its own rows from here on
       }
       __syncthreads();
-      if (threadIdx.x == 0 && ch == NT / C::kChunk - 1) ktrace_stamp(g.ktrace, 4);
+      if (threadIdx.x == 0 && ch == NT / C::kChunk - 1) ktrace_stamp<KT>(g.ktrace, 4);
       // Last chunk: this member's reads of its peers' partials are done.  Arrive now and wait
       // only before leaving, so the closing barrier overlaps the epilogue.
       if (ch == NT / C::kChunk - 1) cluster_arrive();
@@ -347,10 +347,10 @@ __global__ void __launch_bounds__(128, 4)
                         S > 1 ? cb + lr1 : cb + C::kChunk, s_epi, static_cast<int>(threadIdx.x),
                         static_cast<int>(blockDim.x), 0, NT <= 64 ? &pre : nullptr);
   }
-  if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 5);
+  if (threadIdx.x == 0) ktrace_stamp<KT>(g.ktrace, 5);
 
   if (S > 1) cluster_wait();  // no member leaves while another may still read its shared memory
-  if (threadIdx.x == 0) ktrace_stamp(g.ktrace, 7);
+  if (threadIdx.x == 0) ktrace_stamp<KT>(g.ktrace, 7);
 }
 
 // ---- persistent variant for large token counts (prefill, batched serving) --------------------------
@@ -591,14 +591,22 @@ template <int NT>
 static int launch_nt(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, cudaStream_t s) {
   using C = TcCfg<NT>;
   dim3 grid = a.tile_major ? dim3(a.n_tok_tiles, a.n_slabs, a.splits) : dim3(a.n_slabs, a.n_tok_tiles, a.splits);
-  return launch_kc(gemm_tc_kernel<NT>, grid, dim3(128), C::kSmem, s, a.splits, tmA, tmB, a);
+  if (a.ktrace != nullptr) return launch_kc(gemm_tc_kernel<NT, true>, grid, dim3(128), C::kSmem, s, a.splits, tmA, tmB, a);
+  return launch_kc(gemm_tc_kernel<NT, false>, grid, dim3(128), C::kSmem, s, a.splits, tmA, tmB, a);
+}
+
+template <int NT, bool KT>
+static cudaError_t set_attr1() {
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<NT, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<NT>::kSmem);
+  // split-K clusters of up to 16 CTAs (above the portable 8)
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_tc_kernel<NT, KT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
 }
 
 template <int NT>
 static cudaError_t set_attr() {
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<NT>::kSmem);
-  // split-K clusters of up to 16 CTAs (above the portable 8)
-  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_tc_kernel<NT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaError_t e = set_attr1<NT, false>();
+  if (e == cudaSuccess) e = set_attr1<NT, true>();
   return e;
 }
 

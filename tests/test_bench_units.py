@@ -41,3 +41,17 @@ def test_peaks_fall_back_per_key(tmp_path):
     p.write_text('{"hbm_gbs": null, "bf16_tflops": 1618.1}')
     assert bench._peak("hbm_gbs", p) == (6650.0, "fallback")
     assert bench._peak("bf16_tflops", p) == (1618.1, "measured")
+
+
+def test_projection_bytes_cover_the_step_weights():
+    """bench.py's in-situ roofline counts, per projection launch, weights + activations in +
+    outputs; over one step's launches the weight part is every matrix once (the step's weight
+    bytes less the qkv biases and the norm weights)."""
+    from fast_dllm_relax_b200.config import QWEN_1_5B as c
+    names = ("qkv", "o", "gate_up", "down")
+    w0 = sum(bench._proj_bytes(n, 0) for n in names) * c.num_hidden_layers + bench._proj_bytes("lm_head", 0)
+    extra = c.num_hidden_layers * ((c.num_attention_heads + 2 * c.num_key_value_heads) * c.head_dim
+                                   + 2 * c.hidden_size) + c.hidden_size
+    assert w0 == bench.STEP_WEIGHT_BYTES - 2 * extra
+    # 32 rows: activations in (rows x K) and outputs on top of the weights
+    assert bench._proj_bytes("o", 32) - bench._proj_bytes("o", 0) == 32 * c.hidden_size * 2 * 3
