@@ -68,6 +68,7 @@ SIGNATURES: dict[str, tuple] = {
     "fdllm_kernel_trace_read": (_I, [_P, _P, _P, _I, ctypes.POINTER(_I)]),
     "fdllm_unmask": (_I, [_P, _P, _P, _I, _P, _I, _I, _I, _I, ctypes.c_double, _P, _P, _P, _P, _P]),
     "fdllm_token_logprob": (_I, [_P, _P, _I, _P, _P, _P]),
+    "fdllm_unmask_batch": (_I, [_P, _P, _P, _P, _I, ctypes.c_double, _P, _P]),
     "fdllm_generate": (_I, [_P, _P, _I, _I, _I, _I, ctypes.c_double, _I, _I, _I, _P, ctypes.POINTER(_I), _P, _P, _P]),
     "fdllm_kernel_launches": (ctypes.c_longlong, []),
     "fdllm_profile_enable": (_I, [_P, _I]),

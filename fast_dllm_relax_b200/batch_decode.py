@@ -13,8 +13,10 @@ needs next; the scheduler gathers the pending work of all requests and runs it t
   plus ONE fused lm_head + confidence launch over all rows;
 * every pending prefix-cache build is ONE batched forward (fdllm_build_prefix_cache_batch, the
   implicit block-causal mask inside each request, no O(P^2) bias);
-* the unmask decision (runtime.py:158-181 shift, 794-805 rule) runs on the host from the
-  per-row (argmax, max-probability) pairs, 8 bytes per row read back per step.
+* the unmask decision (runtime.py:158-181 shift, 794-805 rule) of every request runs on the
+  device in the same step (fdllm_unmask_batch, one warp per request) from the fused confidence
+  results; the host reads back, per request, the bit mask of the rows to unmask, their tokens and
+  the token after the block (136 bytes), and applies them to its block.
 
 Requests are independent: batching changes which kernels run together, not what any request
 computes, up to the bf16 rounding of the larger token tiles.
@@ -45,7 +47,10 @@ class _Cache:
 
 # Work items a request program yields (and what it receives back):
 #   ("prefill", cache, ids)                      -> None; rows [0, len(ids)) of `cache` written
-#   ("step", cache, ids, write_rel, attend_rel)  -> (ids, maxp): lists of rows ints / floats, unshifted
+#   ("step", cache, ids, write_rel, attend_rel, base, win, masked_bits)
+#                                                -> (unmasked_bits, last_id, window_tokens): the device
+#                                                   decision for window rows [0, win) (window row r takes
+#                                                   shifted row base + r); win 0 for a block append
 #   ("dense", seq_ids)                           -> float32 logits [len(seq_ids), vocab] (stateless path)
 
 def _id_tensor(seqs, n: int, dev) -> torch.Tensor:
@@ -54,20 +59,6 @@ def _id_tensor(seqs, n: int, dev) -> torch.Tensor:
     return torch.from_numpy(flat).to(dev)
 
 
-def _shifted(vals, row: int):
-    """runtime.py:169-174: row i takes row i-1's prediction, row 0 its own."""
-    return vals[row - 1] if row > 0 else vals[0]
-
-
-def _unmask_rows(masked: list[int], prob, threshold: float) -> list[int]:
-    """runtime.py:796-805: masked rows above the threshold, else the first most confident one.
-    `prob(r)` is the shifted confidence of window row r."""
-    conf = [prob(r) for r in masked]
-    rows = [r for r, c in zip(masked, conf) if c > threshold]
-    if not rows:
-        best = max(range(len(conf)), key=lambda j: (conf[j], -j))  # first index on ties, as argmax
-        rows = [masked[best]]
-    return rows
 
 
 def request_program(engine: Engine, prompt_ids: Sequence[int], *, max_new_tokens: int, block_size: int,
@@ -106,11 +97,10 @@ def request_program(engine: Engine, prompt_ids: Sequence[int], *, max_new_tokens
         if lb > 0:
             yield ("prefill", cache, gen[:lb])
             cache.prefix_len = lb
-        ids, _ = yield ("step", cache, gen[lb:], 0, bs)
+        _, nxt, _ = yield ("step", cache, gen[lb:], 0, bs, 0, 0, 0)
         cache.prefix_len += bs
         stats["block_recomputes"] += 1
         stats["block_appends"] += 1
-        nxt = int(ids[-1])
         gen.append(nxt)
         if stop_token is not None and nxt == int(stop_token):
             return continuation(gen)
@@ -135,19 +125,18 @@ def request_program(engine: Engine, prompt_ids: Sequence[int], *, max_new_tokens
                     return continuation(x)
                 if use_cache:
                     partial = use_block_cache and kv_valid and x[a0 + s0] != mask_id
+                    bits = sum(1 << r for r in masked)
                     if partial:  # the step's rows are the window itself
-                        ids, maxp = yield ("step", cache, x[a0 + s0:a0 + s1], s0, bs)
-                        base = 0
+                        taken, _, toks = yield ("step", cache, x[a0 + s0:a0 + s1], s0, bs, 0, s1 - s0, bits)
                     else:  # the step's rows are the whole block; the window starts at row s0
-                        ids, maxp = yield ("step", cache, x[a0:], 0, bs)
-                        base = s0
+                        taken, _, toks = yield ("step", cache, x[a0:], 0, bs, s0, s1 - s0, bits)
                         kv_valid = use_block_cache
                     stats["block_recomputes"] += 1
                     stats["partial_recomputes"] += int(partial)
-                    rows = _unmask_rows(masked, lambda r: float(_shifted(maxp, base + r)), threshold)
-                    for r in rows:
-                        x[a0 + s0 + r] = int(_shifted(ids, base + r))
-                    stats["unmask_updates"] += len(rows)
+                    for r in range(s1 - s0):
+                        if taken >> r & 1:
+                            x[a0 + s0 + r] = toks[r]
+                            stats["unmask_updates"] += 1
                 else:  # stateless first block (runtime.py:806-837): dense forward over the sequence
                     logits = yield ("dense", x)
                     stats["block_recomputes"] += 1
@@ -171,10 +160,9 @@ def request_program(engine: Engine, prompt_ids: Sequence[int], *, max_new_tokens
         if len(gen) - n0 >= max_new_tokens or done_stop(gen, n0):
             break
         if use_cache:  # block-append: the committing forward
-            ids, _ = yield ("step", cache, gen[a0:], 0, bs)
+            _, nxt, _ = yield ("step", cache, gen[a0:], 0, bs, 0, 0, 0)
             cache.prefix_len += bs
             kv_valid = False
-            nxt = int(ids[-1])
         else:
             logits = yield ("dense", gen)
             nxt = int(np.argmax(logits[-1]))
@@ -240,24 +228,24 @@ def generate_batch(engine: Engine, prompts: Sequence[Sequence[int]], *, max_new_
         steps = [(i, op) for i, op in pending.items() if op[0] == "step"]
         if not steps:
             continue
-        # every pending cached step in one batched forward + one fused confidence launch
-        ids_all = _id_tensor([op[2] for _, op in steps], sum(len(op[2]) for _, op in steps), dev)
-        x = engine.embed(ids_all)
-        reqs = []
-        for _, (_, cache, ids, write_rel, attend_rel) in steps:
+        # every pending cached step in one batched forward, one fused confidence launch and one
+        # unmask launch; the token ids and the unmask descriptors go up in one copy
+        n_ids = sum(len(op[2]) for _, op in steps)
+        buf = np.empty(n_ids + 5 * len(steps), dtype=np.int32)
+        reqs, o = [], 0
+        for j, (_, (_, cache, ids, write_rel, attend_rel, base, win, bits)) in enumerate(steps):
             rows = len(ids)
+            buf[o:o + rows] = ids
+            buf[n_ids + 5 * j:n_ids + 5 * j + 5] = (o, rows, base, win, bits)
             reqs.append(dict(k=cache.k, v=cache.v, rows=rows, prefix_len=cache.prefix_len, write_rel=write_rel,
                              attend_rel=attend_rel))
-        hidden = engine.forward_cached_batch(x, reqs)
-        cid, cmax = engine.confidence(hidden)
-        both = torch.cat([cid.view(torch.float32), cmax]).cpu().numpy()  # one device-to-host copy
-        # Python lists: each request reads a few of its rows one by one, which lists serve faster
-        cid, cmax = both[:len(cid)].view(np.int32).tolist(), both[len(cid):].tolist()
-        o = 0
-        for i, op in steps:
-            rows = len(op[2])
-            advance(i, (cid[o:o + rows], cmax[o:o + rows]))
             o += rows
+        up = torch.from_numpy(buf).to(dev)
+        hidden = engine.forward_cached_batch(engine.embed(up[:n_ids]), reqs)
+        cid, cmax = engine.confidence(hidden)
+        dec = engine.unmask_batch(cid, cmax, up[n_ids:].view(len(steps), 5), threshold).cpu().numpy()
+        for j, (i, op) in enumerate(steps):
+            advance(i, (int(dec[j, 0]), int(dec[j, 1]), dec[j, 2:2 + op[6]].tolist()))
     if timing is not None:
         t1 = torch.cuda.Event(enable_timing=True)
         t1.record()

@@ -420,6 +420,65 @@ int launch_unmask(const int* ids, const float* maxp, int rows, int* block, int s
                   threshold, out_tok, out_conf, out_unmask, status);
 }
 
+// ---- unmask decisions of a batched step, one warp per request ---------------------------------
+// The rule of unmask_kernel for many requests whose rows share one ids / maxp array.  desc[5 i ..]:
+// row0, rows (the request's rows in ids / maxp), base (window row 0 takes shifted row `base`: 0 for
+// a partial step, the sub-block start for a full one), win (window length, 0 = no decision: a block
+// append) and the bit mask of the window rows still masked.  out[34 i ..]: the bit mask of the rows
+// unmasked, the last row's unshifted argmax (the token after the block, runtime.py:181), then the
+// shifted token of each window row.  The block itself stays on the host, which applies the bits.
+__global__ void unmask_batch_kernel(const int* __restrict__ ids, const float* __restrict__ maxp,
+                                    const int* __restrict__ desc, int n, double threshold, int* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int j = threadIdx.x & 31;
+  if (i >= n) return;
+  const int row0 = desc[5 * i], rows = desc[5 * i + 1], base = desc[5 * i + 2], win = desc[5 * i + 3];
+  const unsigned bits = static_cast<unsigned>(desc[5 * i + 4]);
+  int tok = 0;
+  float conf = -INFINITY;
+  bool masked = false;
+  if (j < win) {
+    const int src_row = base + j;
+    const int row = src_row > 0 ? src_row - 1 : 0;
+    if (row < rows) {
+      tok = ids[row0 + row];
+      conf = maxp[row0 + row];
+    }
+    masked = (bits >> j) & 1u;
+  }
+  const bool above = masked && static_cast<double>(conf) > threshold;
+  bool take = above;
+  if (__ballot_sync(0xffffffffu, above) == 0u) {
+    float best = masked ? conf : -INFINITY;
+    int best_j = masked ? j : 0x7fffffff;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+      const int oj = __shfl_xor_sync(0xffffffffu, best_j, off);
+      if (ob > best || (ob == best && oj < best_j)) {
+        best = ob;
+        best_j = oj;
+      }
+    }
+    take = masked && j == best_j;
+  }
+  const unsigned took = __ballot_sync(0xffffffffu, take);
+  int* o = out + 34 * i;
+  if (j == 0) {
+    o[0] = static_cast<int>(took);
+    o[1] = rows > 0 ? ids[row0 + rows - 1] : 0;
+  }
+  if (j < win) o[2 + j] = tok;
+}
+
+int launch_unmask_batch(const int* ids, const float* maxp, const int* desc, int n, double threshold, int* out,
+                        cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  return launch_k(unmask_batch_kernel, dim3((n + 7) / 8), dim3(256), 0, s, ids, maxp, desc, n, threshold, out);
+}
+
 // ---- bounded-wait self test: spin on a flag that nothing sets; give up and report ----------
 __global__ void wait_test_kernel(const volatile int* flag, int* err, unsigned long long limit_ns) {
   const uint64_t t0 = global_timer_ns();

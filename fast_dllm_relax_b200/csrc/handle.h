@@ -44,6 +44,7 @@ struct Tuning {
   int gu_fused_rows = 16;      // gate_up normalises its own B tiles up to this many token rows
   int block_graph = 1;         // fdllm_generate runs whole blocks as device-looped CUDA graphs
   int attn_tc_min_q = 64;      // tcgen05 attention from this many query tokens per request (0: never)
+  int attn_tc_min_ctas = 64;   // ... or from this many (request, KV head, query tile) CTAs
 };
 int parse_tuning(const char* spec, Tuning* t);
 

@@ -204,5 +204,7 @@ int launch_lse_combine(const float* part, int rows, int n_slabs, float* logprob,
 int launch_unmask(const int* ids, const float* maxp, int rows, int* block, int sub_start, int sub_len,
                   int partial, int mask_id, double threshold, int* out_tok, float* out_conf, int* out_unmask,
                   int* status, cudaStream_t s);
+int launch_unmask_batch(const int* ids, const float* maxp, const int* desc, int n, double threshold, int* out,
+                        cudaStream_t s);
 int launch_wait_test(int* flag, int* err, unsigned long long limit_ns, cudaStream_t s);
 }  // namespace fdllm

@@ -116,6 +116,7 @@ int fdllm::parse_tuning(const char* spec, Tuning* t) {
     else if (key == "gu_fused_rows" && x >= 0 && x <= 64) t->gu_fused_rows = x;
     else if (key == "block_graph" && (x == 0 || x == 1)) t->block_graph = x;
     else if (key == "attn_tc_min_q" && x >= 0) t->attn_tc_min_q = x;
+    else if (key == "attn_tc_min_ctas" && x >= 0) t->attn_tc_min_ctas = x;
     else return fail(FDLLM_ERR_INVALID, "unknown tuning key or value out of range: " + item);
   }
   return FDLLM_OK;
@@ -396,9 +397,14 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
   // tcgen05 attention for calls with many query tokens per request (prefill, batched steps): its
   // per-request K/V tensor maps are encoded here and uploaded once for all layers.  Not inside a
   // stream capture, and not for device-side prefix lengths (the maps carry the attended length).
-  bool attn_tc = h->dtype == FDLLM_BFLOAT16 && c.head_dim == 128 && bias == nullptr && !h->capturing &&
-                 h->tune.attn_tc_min_q > 0 && max_q >= h->tune.attn_tc_min_q &&
-                 c.num_attention_heads / c.num_key_value_heads <= 16;
+  // It runs one CTA per (request, KV head, query tile) without key splits, so it takes the call when
+  // a request has attn_tc_min_q query tokens or the tiles alone cover attn_tc_min_ctas CTAs (a
+  // batched step); a lone decode-sized request keeps the key-split mma.sync kernel (32 rows at
+  // prefix 384: 1.41 ms per step against 1.55; 32 requests x 32 rows: 4.68 ms against 4.96).
+  const int gqa = c.num_attention_heads / c.num_key_value_heads;
+  const int tc_ctas = nreq * c.num_key_value_heads * ((max_q + 128 / gqa - 1) / (128 / gqa));
+  bool attn_tc = h->dtype == FDLLM_BFLOAT16 && c.head_dim == 128 && bias == nullptr && !h->capturing && gqa <= 16 &&
+                 h->tune.attn_tc_min_q > 0 && (max_q >= h->tune.attn_tc_min_q || tc_ctas >= h->tune.attn_tc_min_ctas);
   for (const ReqDesc& r : reqs) attn_tc = attn_tc && r.plen_dev == nullptr && r.attend_len > 0;
   if (attn_tc) {
     std::vector<CUtensorMap> maps(2 * static_cast<size_t>(nreq));
@@ -867,6 +873,15 @@ int fdllm_unmask(fdllm_handle* h, const int32_t* ids, const float* maxp, int row
   if (partial ? rows != sub_len : rows < sub_start + sub_len) return fail(FDLLM_ERR_INVALID, "rows do not cover the window");
   CUDA_TRY(launch_unmask(ids, maxp, rows, block_tokens, sub_start, sub_len, partial, mask_id, threshold, out_tokens,
                          out_conf, out_unmask, status, static_cast<cudaStream_t>(stream)));
+  return FDLLM_OK;
+}
+
+int fdllm_unmask_batch(fdllm_handle* h, const int32_t* ids, const float* maxp, const int32_t* desc, int n,
+                       double threshold, int32_t* out, void* stream) {
+  FDLLM_TRY(check_handle(h));
+  if (n < 0 || (n > 0 && (ids == nullptr || maxp == nullptr || desc == nullptr || out == nullptr)))
+    return fail(FDLLM_ERR_INVALID, "bad unmask batch arguments");
+  CUDA_TRY(launch_unmask_batch(ids, maxp, desc, n, threshold, out, static_cast<cudaStream_t>(stream)));
   return FDLLM_OK;
 }
 

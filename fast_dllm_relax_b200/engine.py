@@ -255,6 +255,19 @@ class Engine:
                                          self._stream()))
         return tok, conf, flag, status
 
+    def unmask_batch(self, ids: torch.Tensor, maxp: torch.Tensor, desc: torch.Tensor, threshold: float) -> torch.Tensor:
+        """Unmask decisions of a batched step on the device (fdllm_unmask_batch): ids / maxp the
+        step's confidence results, desc int32 [n, 5] (row0, rows, base, win, masked bits) on the
+        device.  Returns int32 [n, 34]: unmasked bits, last-row argmax, window tokens."""
+        n = int(desc.shape[0])
+        for t, dt, name in ((ids, torch.int32, "ids"), (maxp, torch.float32, "maxp"), (desc, torch.int32, "desc")):
+            if t.device != self.device or t.dtype != dt or not t.is_contiguous():
+                raise ValueError(f"unmask_batch: {name} must be a contiguous {dt} tensor on {self.device}")
+        out = torch.empty((n, 34), dtype=torch.int32, device=self.device)
+        _lib.check(self.lib.fdllm_unmask_batch(self._h, ids.data_ptr(), maxp.data_ptr(), desc.data_ptr(), n,
+                                               float(threshold), out.data_ptr(), self._stream()))
+        return out
+
     def token_logprob(self, hidden: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         h2 = self._act(hidden, "token_logprob")
         n = h2.shape[0]

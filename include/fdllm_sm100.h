@@ -140,6 +140,17 @@ FDLLM_API int fdllm_unmask(fdllm_handle* h, const int32_t* ids, const float* max
                  int sub_start, int sub_len, int partial, int mask_id, double threshold, int32_t* out_tokens,
                  float* out_conf, int32_t* out_unmask, int32_t* status, void* stream);
 
+/* fdllm_unmask for every request of a batched step at once (runtime.py:158-181 shift, 794-805
+ * rule, per request; the reference decides one request at a time on the host).  ids / maxp: the
+ * unshifted fdllm_confidence results of all rows of the step.  desc int32[5 n] (device), per
+ * request: row0, rows (its rows in ids / maxp), base (window row 0 takes shifted row `base`: 0 for
+ * a partial step, the sub-block start for a full one), win (window length <= 32; 0: no decision,
+ * a block append) and the bit mask of the window rows still masked.  out int32[34 n] (device), per
+ * request: the bit mask of the window rows unmasked, the last row's unshifted argmax (the token
+ * after the block), then win shifted tokens.  The caller applies the bits to its block. */
+FDLLM_API int fdllm_unmask_batch(fdllm_handle* h, const int32_t* ids, const float* maxp, const int32_t* desc, int n,
+                                 double threshold, int32_t* out, void* stream);
+
 /* log_softmax(get_logits(hidden))[row, target[row]] per row, fused with the lm_head
  * (the host reduction of runners.py:877-881).  targets int32[rows] -> logprob fp32[rows]. */
 FDLLM_API int fdllm_token_logprob(fdllm_handle* h, const void* hidden, int rows, const int32_t* targets, float* logprob,

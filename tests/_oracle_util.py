@@ -191,3 +191,23 @@ def assert_within_bf16_noise(got, ref, noise, msg: str = "", rtol: float = 2e-2,
     assert a["out"] <= slack * b["out"] + 1e-3, line
     assert a["max"] <= slack * b["max"] + rtol * a["rms"], line
     return {"gpu": a, "floor": b}
+
+
+def unmask_batch_rule(ids, maxp, desc, threshold: float):
+    """fdllm_unmask_batch's rule restated on the host (runtime.py:158-181 shift, 796-805 rule): per
+    request (desc row: row0, rows, base, win, masked bits), window row j takes shifted row base + j;
+    the masked rows above the threshold are unmasked, else the first most confident masked row.
+    Returns int32 [n, 34]: unmasked bits, the last row's unshifted id, the window's tokens."""
+    ids, maxp = ids.cpu(), maxp.cpu()
+    out = torch.zeros((desc.shape[0], 34), dtype=torch.int32)
+    for i, (row0, rows, base, win, bits) in enumerate(desc.cpu().tolist()):
+        src = [row0 + (base + j - 1 if base + j > 0 else 0) for j in range(win)]
+        toks, conf = [int(ids[r]) for r in src], [float(maxp[r]) for r in src]
+        masked = [j for j in range(win) if bits >> j & 1]
+        take = [j for j in masked if conf[j] > threshold]
+        if not take and masked:
+            take = [max(masked, key=lambda j: (conf[j], -j))]
+        out[i, 0] = sum(1 << j for j in take)
+        out[i, 1] = int(ids[row0 + rows - 1])
+        out[i, 2:2 + win] = torch.tensor(toks, dtype=torch.int32)
+    return out

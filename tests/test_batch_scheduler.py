@@ -1,9 +1,10 @@
 """The batched-serving scheduler (fast_dllm_relax_b200.batch_decode) on the CPU: an engine stand-in
 backed by the oracle (test infrastructure) runs the tiny fp32 model, and every request must
 reproduce the reference runtime's tokens and statistics (tests/golden/tiny_decode.json), alone
-and batched with requests in other states.  This pins the scheduler's host logic -- the shift of
-the confidences, the unmask rule, block appends, the stateless first block, batched prefix
-builds -- independently of the CUDA kernels."""
+and batched with requests in other states.  This pins the scheduler's host logic -- the window
+descriptors it hands to the device unmask (shift base, window, masked rows), how it applies the
+decisions, block appends, the stateless first block, batched prefix builds -- independently of
+the CUDA kernels; the stand-in's unmask_batch restates the device kernel's rule."""
 
 import json
 
@@ -13,7 +14,7 @@ import torch
 from fast_dllm_relax_b200.batch_decode import generate_batch
 from fast_dllm_relax_b200.config import TINY, TINY_MASK_ID, make_synthetic_params
 from oracle.model import build_block_bias, confidence
-from tests._oracle_util import make_oracle
+from tests._oracle_util import make_oracle, unmask_batch_rule
 
 CASES = ["cfg0_nocache", "cfg0_blockcache", "short_prompt_stateless", "one_block_prompt", "unaligned_prompt",
          "low_threshold", "stop_token"]
@@ -55,6 +56,9 @@ class OracleEngine:
 
     def confidence(self, hidden):
         return confidence(self.m.get_logits(hidden[None])[0])
+
+    def unmask_batch(self, ids, maxp, desc, threshold):
+        return unmask_batch_rule(ids, maxp, desc, threshold)
 
     def forward_hidden(self, x, bias):
         assert bias is None  # the scheduler relies on the implicit block-causal mask

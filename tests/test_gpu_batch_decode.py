@@ -74,3 +74,32 @@ def test_bf16_batch_runs_and_is_deterministic():
     assert a == b and sa == sb
     assert all(len(t) > 0 and 4095 not in t for t in a)
     assert eng.device_error() == 0
+
+
+def test_unmask_batch_kernel_is_bit_exact():
+    """fdllm_unmask_batch against the host restatement of the rule on 200 random batched steps:
+    full and partial windows, append rows (win 0), ties, confidences at and around the threshold."""
+    from fast_dllm_relax_b200.config import TINY, make_synthetic_params
+    from fast_dllm_relax_b200.engine import Engine
+    from tests._oracle_util import unmask_batch_rule
+    eng = Engine(TINY, [p.cuda() for p in make_synthetic_params(TINY, 0, "float32")], dtype="float32")
+    g = torch.Generator().manual_seed(5)
+    for case in range(200):
+        n = int(torch.randint(1, 40, (1,), generator=g))
+        desc, o = [], 0
+        for _ in range(n):
+            rows = [8, 32][int(torch.randint(0, 2, (1,), generator=g))]
+            win = 0 if int(torch.randint(0, 6, (1,), generator=g)) == 0 else 8
+            base = 0 if rows == 8 else 8 * int(torch.randint(0, 4, (1,), generator=g))
+            bits = int(torch.randint(0, 256, (1,), generator=g)) if win else 0
+            desc.append((o, rows, base, win, bits))
+            o += rows
+        ids = torch.randint(0, 1000, (o,), generator=g, dtype=torch.int32)
+        levels = torch.tensor([0.1, 0.5, 0.9, 0.9000001, 0.95, 0.3], dtype=torch.float32)
+        maxp = levels[torch.randint(0, len(levels), (o,), generator=g)]
+        d = torch.tensor(desc, dtype=torch.int32)
+        got = eng.unmask_batch(ids.cuda(), maxp.cuda(), d.cuda(), 0.9).cpu()
+        ref = unmask_batch_rule(ids, maxp, d, 0.9)
+        for i, (_, _, _, win, _) in enumerate(desc):
+            assert torch.equal(got[i, :2 + win], ref[i, :2 + win]), (case, i)
+    assert eng.device_error() == 0
