@@ -22,7 +22,7 @@
 //                   S_j from TMEM, mask, online softmax, write P_j (bf16, swizzled) to shared
 //                   memory, and fold O_{j-1} from TMEM into fp32 registers with the rescale.
 // Every wait is bounded (kWaitLimitNs): on expiry the thread records an error with its wait site
-// and the CTA drains and leaves.  No cluster and no multicast: every TMA load reads this GPU's
+// and the CTA drains and leaves.  No thread-block cluster: every TMA load reads this GPU's
 // own memory into this CTA only.
 #include "common.cuh"
 #include "kernels.h"
