@@ -35,7 +35,7 @@ int fail(int code, const std::string& msg);
 struct Tuning {
   int nt_max = 128;            // largest token tile of the per-tile projection GEMM: 64, 128 or 256
                                // (224-row prefill: 2.62 ms at 128 against 3.71 at 256)
-  int split_target = 0;        // CTAs per SM the split-K plan aims for (0: 2 at <= 16 rows, else 1)
+  int split_target = 0;        // CTAs per SM the split-K plan aims for (0: 2 at <= 32 rows, else 1)
   int split_max = 16;          // largest split-K cluster of the per-tile GEMM
   int gemm_tune = kGemmTunePrefetch | (2 << kGemmTuneL2Shift);  // kGemmTune* bits
   int persist_min_rows = 256;  // token rows from which projections run on the persistent GEMM (0: never)

@@ -228,9 +228,10 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
   const int kblocks = g->K / 64;
   const int tiles = g->n_slabs * g->n_tok_tiles;
   int splits = 1;
-  // CTAs per SM the split-K plan aims for: 2 at <= 16 token rows (the 8-row partial step: 1.348 ->
-  // 1.329 ms at prefix 384; 32 rows unchanged, 3 or 4 slower at both), else 1.
-  const int target = h->tune.split_target > 0 ? h->tune.split_target : (M <= 16 ? 2 : 1);
+  // CTAs per SM the split-K plan aims for: 2 at <= 32 token rows (the 8-row partial step: 1.348 ->
+  // 1.329 ms at prefix 384; the 32-row block step 1.517 -> 1.511 ms, 700 -> 707 tokens/s; 3 or 4
+  // slower at both), else 1.
+  const int target = h->tune.split_target > 0 ? h->tune.split_target : (M <= 32 ? 2 : 1);
   const int split_max = h->tune.split_max;
   if (tiles < target * h->num_sms) {  // split K over a cluster of at most 16 CTAs
     splits = std::max(1, std::min({kblocks, target * h->num_sms / tiles, split_max}));

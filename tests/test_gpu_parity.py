@@ -180,8 +180,9 @@ def test_token_logprob_matches_log_softmax(setup):
 def _batched_vs_single(setup, cases, seed0):
     """Run `cases` (prefix, rows, write_rel) one by one and as one batch; compare outputs and caches.
     The caches must be bit-identical where the batch and the single request get the same split-K
-    plan: K is split over twice as many CTAs at <= 16 token rows, so an 8-row request alone sums
-    its fp32 partials in another order than inside a batch of more rows, and agrees to rounding."""
+    plan: K is split over twice as many CTAs at <= 32 token rows, so a request of up to 32 rows
+    alone sums its fp32 partials in another order than inside a batch of more rows, and agrees to
+    rounding."""
     cfg, dtype, eng, orc = setup
     reqs, xs, singles = [], [], []
     for i, (P, rows, rp) in enumerate(cases):
@@ -200,7 +201,7 @@ def _batched_vs_single(setup, cases, seed0):
     o = 0
     for r, (hs, ks, vs) in zip(reqs, singles):
         _close(out[o:o + r["rows"]], hs, dtype, "batched rows")
-        if dtype == "float32" or (total <= 16) == (r["rows"] <= 16):
+        if dtype == "float32" or (total <= 32) == (r["rows"] <= 32):
             assert torch.equal(r["k"], ks) and torch.equal(r["v"], vs)
         else:
             _close(r["k"], ks, dtype, "batched K cache")
@@ -209,7 +210,7 @@ def _batched_vs_single(setup, cases, seed0):
 
 
 def test_batched_forward_matches_single_requests(setup):
-    """80 mixed rows in one batched forward, and 16 rows of partial steps (the <= 16-row plan),
+    """80 mixed rows in one batched forward, and 16 rows of partial steps (the <= 32-row plan),
     against the same requests run one at a time."""
     _batched_vs_single(setup, ((32, 32, 0), (64, 8, 8), (96, 32, 0), (32, 8, 24)), 40)
     _batched_vs_single(setup, ((64, 8, 8), (32, 8, 24)), 70)
