@@ -362,7 +362,10 @@ __global__ void __launch_bounds__(128, 4)
 // The epilogue of tile i therefore overlaps the mainloop of tile i + 1.
 template <int NT>
 struct PCfg {
+  static_assert(NT == 96 || NT == 128 || NT == 256, "persistent token tiles: 96, 128 or 256");
   static constexpr int kStages = NT == 256 ? 4 : 6;
+  static constexpr uint32_t kTmemCols = 2 * NT <= 256 ? 256 : 512;  // a power of two >= 2 NT
+  static constexpr uint32_t kAccStride = kTmemCols / 2;                // accumulator 1's first column
   static constexpr int kStage = 128 * 64 * 2 + NT * 64 * 2;  // A + B of one k block
   static constexpr int kChunk = 32;
   static constexpr int kSmem = 1024 + kStages * kStage + kChunk * 128 * 4 + 256;
@@ -370,7 +373,7 @@ struct PCfg {
 };
 constexpr int kPEpi = 256;  // epilogue threads (warps 2-9)
 
-template <int NT>
+template <int NT, bool KT>
 __global__ void __launch_bounds__(64 + kPEpi, 1)
     gemm_tc_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const GemmArgs g) {
@@ -413,7 +416,7 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
     tma_prefetch_map(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * kPNT);
+    tmem_alloc(tmem_slot, PCfg<NT>::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before_sync();
@@ -428,6 +431,7 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
       pdl_wait();
+      ktrace_stamp<KT>(g.ktrace, 1);
       uint32_t it = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
@@ -471,7 +475,7 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
           break;
         }
         tc_fence_after_sync();
-        const uint32_t d = tmem + buf * kPNT;
+        const uint32_t d = tmem + buf * PCfg<NT>::kAccStride;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kPStages;
           if (!mbar_wait(&full[s], (it / kPStages) & 1u)) {
@@ -510,7 +514,7 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
       float4* mine = S > 1 ? reinterpret_cast<float4*>(g.ppart + (static_cast<size_t>(t) * S + sp) * kPNT * 128) : nullptr;
       for (int cb = 0; cb < kPNT && tok0 + cb < g.M; cb += kPChunk) {
         uint32_t r[16];
-        tmem_ld_32x32b_x16(tmem + buf * kPNT + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(cb + half * 16),
+        tmem_ld_32x32b_x16(tmem + buf * PCfg<NT>::kAccStride + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(cb + half * 16),
                            r);
         tmem_ld_wait();
 #pragma unroll
@@ -574,16 +578,23 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after_sync();
-    tmem_dealloc(tmem, 2 * kPNT);
+    tmem_dealloc(tmem, PCfg<NT>::kTmemCols);
   }
+  if (threadIdx.x == 0) ktrace_stamp<KT>(g.ktrace, 7);
 }
 
 int launch_gemm_tc_persist(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int nt, int grid,
                            cudaStream_t s) {
+  const bool kt = a.ktrace != nullptr;
   if (nt == 256)
-    return launch_k(gemm_tc_persist_kernel<256>, dim3(grid), dim3(64 + kPEpi), PCfg<256>::kSmem, s, tmA, tmB, a);
+    return kt ? launch_k(gemm_tc_persist_kernel<256, true>, dim3(grid), dim3(64 + kPEpi), PCfg<256>::kSmem, s, tmA, tmB, a)
+              : launch_k(gemm_tc_persist_kernel<256, false>, dim3(grid), dim3(64 + kPEpi), PCfg<256>::kSmem, s, tmA, tmB, a);
   if (nt == 128)
-    return launch_k(gemm_tc_persist_kernel<128>, dim3(grid), dim3(64 + kPEpi), PCfg<128>::kSmem, s, tmA, tmB, a);
+    return kt ? launch_k(gemm_tc_persist_kernel<128, true>, dim3(grid), dim3(64 + kPEpi), PCfg<128>::kSmem, s, tmA, tmB, a)
+              : launch_k(gemm_tc_persist_kernel<128, false>, dim3(grid), dim3(64 + kPEpi), PCfg<128>::kSmem, s, tmA, tmB, a);
+  if (nt == 96)
+    return kt ? launch_k(gemm_tc_persist_kernel<96, true>, dim3(grid), dim3(64 + kPEpi), PCfg<96>::kSmem, s, tmA, tmB, a)
+              : launch_k(gemm_tc_persist_kernel<96, false>, dim3(grid), dim3(64 + kPEpi), PCfg<96>::kSmem, s, tmA, tmB, a);
   return cudaErrorInvalidValue;
 }
 
@@ -611,10 +622,18 @@ static cudaError_t set_attr() {
 }
 
 int init_gemm_tc_attributes() {
-  cudaError_t e =
-      cudaFuncSetAttribute(gemm_tc_persist_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<256>::kSmem);
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_persist_kernel<256, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       PCfg<256>::kSmem);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(gemm_tc_persist_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<128>::kSmem);
+    e = cudaFuncSetAttribute(gemm_tc_persist_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<256>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc_persist_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<128>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc_persist_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<128>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc_persist_kernel<96, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<96>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc_persist_kernel<96, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<96>::kSmem);
   if (e == cudaSuccess) e = set_attr<16>();
   if (e == cudaSuccess) e = set_attr<32>();
   if (e == cudaSuccess) e = set_attr<64>();

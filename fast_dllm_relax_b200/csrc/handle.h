@@ -40,6 +40,7 @@ struct Tuning {
   int gemm_tune = kGemmTunePrefetch | (2 << kGemmTuneL2Shift);  // kGemmTune* bits
   int persist_min_rows = 256;  // token rows from which projections run on the persistent GEMM (0: never)
   int persist_splitk = 0;      // split K inside the persistent GEMM while its tiles leave SMs idle
+  int persist_nt96 = 0;        // 96-token persistent tiles where they balance the SMs better
   int attn_splits = 0;         // attention key splits of decode-sized calls (0: planned)
   int gu_fused_rows = 16;      // gate_up normalises its own B tiles up to this many token rows
   int block_graph = 1;         // fdllm_generate runs whole blocks as device-looped CUDA graphs

@@ -117,6 +117,7 @@ int fdllm::parse_tuning(const char* spec, Tuning* t) {
     else if (key == "block_graph" && (x == 0 || x == 1)) t->block_graph = x;
     else if (key == "attn_tc_min_q" && x >= 0) t->attn_tc_min_q = x;
     else if (key == "attn_tc_min_ctas" && x >= 0) t->attn_tc_min_ctas = x;
+    else if (key == "persist_nt96" && (x == 0 || x == 1)) t->persist_nt96 = x;
     else return fail(FDLLM_ERR_INVALID, "unknown tuning key or value out of range: " + item);
   }
   return FDLLM_OK;
@@ -283,8 +284,16 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
   g.tune = h->tune.gemm_tune;
   if (norm_w == nullptr && use_persist(h, M)) {
     g.n_slabs = w.paired ? (g.N / 2) / 64 : g.N / 128;
-    // 256-token tiles when they cover half the SMs, else 128 (twice the tiles for few-slab weights)
-    const int pnt = 2 * g.n_slabs * ((M + 255) / 256) >= h->num_sms ? 256 : 128;
+    // 256-token tiles when they cover half the SMs, else 128 (twice the tiles for few-slab weights).
+    // 96-token tiles where they shorten the busiest SM's share (rounds of tiles x tile height) by
+    // at least 15%: the few-slab projections of a 1024-row step (o, down: 132 tiles in one round
+    // instead of 96 of 128 rows).
+    int pnt = 2 * g.n_slabs * ((M + 255) / 256) >= h->num_sms ? 256 : 128;
+    auto share = [&](int nt) {
+      const long long tiles = static_cast<long long>(g.n_slabs) * ((M + nt - 1) / nt);
+      return (tiles + h->num_sms - 1) / h->num_sms * nt;
+    };
+    if (h->tune.persist_nt96 && share(96) * 100 <= share(pnt) * 85) pnt = 96;
     g.n_tok_tiles = (M + pnt - 1) / pnt;
     g.tile_n = pnt;
     const int tiles = g.n_slabs * g.n_tok_tiles;

@@ -1,0 +1,76 @@
+"""Token-tile heights of the persistent projection GEMM (csrc/gemm_tc.cu gemm_tc_persist_kernel).
+
+A 1024-row batched cached step (32 requests x 32 rows, the configs[2] serving step) runs its
+projections on the persistent GEMM.  With FDLLM_TUNING=persist_nt96=1 the few-slab projections
+(o and down: 12 weight slabs at the 1.5B shapes) take 96-token tiles instead of 128; the result must
+match the default plan as two GPU plans of the same arithmetic, and the oracle at the bf16 noise
+floor (tests/_oracle_util.assert_within_bf16_noise).  MID: the 1.5B layer shapes, 2 layers.
+"""
+
+import pytest
+import torch
+
+from fast_dllm_relax_b200.config import ModelConfig, make_synthetic_params
+from tests._oracle_util import assert_within_bf16_noise, bf16_discrepancy, make_oracle, make_reordered_oracle
+
+pytestmark = pytest.mark.gpu
+
+MID = ModelConfig(vocab_size=4096, hidden_size=1536, intermediate_size=8960, num_hidden_layers=2,
+                  num_attention_heads=12, num_key_value_heads=2, head_dim=128, context_window_size=8192)
+
+
+def _dev():
+    return torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="module")
+def engines():
+    import os
+
+    from fast_dllm_relax_b200.engine import Engine
+    params = make_synthetic_params(MID, seed=31, dtype="bfloat16", mask_id=4095)
+    dev_params = [p.to(_dev()) for p in params]
+    old = os.environ.get("FDLLM_TUNING")
+    try:
+        os.environ["FDLLM_TUNING"] = "persist_nt96=0"
+        base = Engine(MID, dev_params, dtype="bfloat16")
+        os.environ["FDLLM_TUNING"] = "persist_nt96=1"
+        nt96 = Engine(MID, dev_params, dtype="bfloat16")
+    finally:
+        if old is None:
+            os.environ.pop("FDLLM_TUNING", None)
+        else:
+            os.environ["FDLLM_TUNING"] = old
+    return base, nt96, make_oracle(MID, params, "bfloat16"), make_reordered_oracle(MID, params, "bfloat16")
+
+
+@pytest.mark.parametrize("n_req", [32, 31])
+def test_batched_step_with_96_token_tiles(engines, n_req):
+    """32 x 32 rows (11 tiles of 96, the last one partial) and 31 x 32 rows; caches of different
+    prefix lengths."""
+    base, nt96, orc, alt = engines
+    g = torch.Generator().manual_seed(n_req)
+    lens = [64 + 16 * i for i in range(n_req)]
+    caches0 = []
+    for P in lens:
+        shape = (MID.num_hidden_layers, 1, P + 32, MID.num_key_value_heads, MID.head_dim)
+        caches0.append([(torch.randn(shape, generator=g) * 0.5).to(torch.bfloat16) for _ in range(2)])
+    x = torch.randn((n_req * 32, MID.hidden_size), generator=g).to(torch.bfloat16)
+    outs = []
+    for eng in (base, nt96):
+        caches = [(k.to(_dev()), v.to(_dev())) for k, v in caches0]
+        reqs = [dict(k=k, v=v, rows=32, prefix_len=P) for (k, v), P in zip(caches, lens)]
+        h = eng.forward_cached_batch(x.to(_dev()), reqs).cpu()
+        assert eng.device_error() == 0
+        outs.append((h, [(k.cpu(), v.cpu()) for k, v in caches]))
+    d = bf16_discrepancy(outs[1][0], outs[0][0])
+    assert d["out"] <= 1e-3 and d["rel"] <= 1e-2, f"96-token tiles vs default: {d}"
+    for i in (0, n_req - 1):
+        P = lens[i]
+        kr, vr = caches0[i][0].clone(), caches0[i][1].clone()
+        ka, va = caches0[i][0].clone(), caches0[i][1].clone()
+        ref = orc.forward_cached(x[None, 32 * i:32 * i + 32], kr, vr, P, P)
+        ref_alt = alt.forward_cached(x[None, 32 * i:32 * i + 32], ka, va, P, P)
+        assert_within_bf16_noise(outs[1][0][32 * i:32 * i + 32], ref[0], ref_alt[0], f"request {i} vs oracle")
+        assert_within_bf16_noise(outs[1][1][i][0][:, :, P:P + 32], kr[:, :, P:P + 32], ka[:, :, P:P + 32],
+                                 f"request {i} K rows vs oracle")
