@@ -39,8 +39,13 @@ struct Tuning {
   int split_max = 16;          // largest split-K cluster of the per-tile GEMM
   int gemm_tune = kGemmTunePrefetch | (2 << kGemmTuneL2Shift);  // kGemmTune* bits
   int persist_min_rows = 256;  // token rows from which projections run on the persistent GEMM (0: never)
-  int persist_splitk = 0;      // split K inside the persistent GEMM while its tiles leave SMs idle
-  int persist_nt96 = 0;        // 96-token persistent tiles where they balance the SMs better
+  int persist_splitk = 2;      // split K inside the persistent GEMM: 1 while its tiles leave half
+                               // the SMs idle (+30% at 1024 rows); 2 only for long-K few-slab
+                               // projections on 256-token tiles (down at 1024 rows: 46.6 -> 45.2 us)
+  int short_k_nt = 64;         // per-tile token tile of short-K few-slab projections of calls the
+                               // persistent kernel covers with <= 1 tile per CTA (0: persistent)
+  int persist_nt96 = 1;        // 96-token persistent tiles where they balance the SMs better
+                               // (o, down at 1024 rows; batched step 4.666 -> 4.470 ms with the two above)
   int attn_splits = 0;         // attention key splits of decode-sized calls (0: planned)
   int gu_fused_rows = 16;      // gate_up normalises its own B tiles up to this many token rows
   int block_graph = 1;         // fdllm_generate runs whole blocks as device-looped CUDA graphs

@@ -111,7 +111,8 @@ int fdllm::parse_tuning(const char* spec, Tuning* t) {
     else if (key == "split_max" && x >= 1 && x <= 16) t->split_max = x;
     else if (key == "gemm_tune" && x >= 0) t->gemm_tune = x;
     else if (key == "persist_min_rows" && x >= 0) t->persist_min_rows = x;
-    else if (key == "persist_splitk" && (x == 0 || x == 1)) t->persist_splitk = x;
+    else if (key == "persist_splitk" && x >= 0 && x <= 2) t->persist_splitk = x;
+    else if (key == "short_k_nt" && (x == 0 || x == 64 || x == 128)) t->short_k_nt = x;
     else if (key == "attn_splits" && x >= 0 && x <= kMaxAttnSplits) t->attn_splits = x;
     else if (key == "gu_fused_rows" && x >= 0 && x <= 64) t->gu_fused_rows = x;
     else if (key == "block_graph" && (x == 0 || x == 1)) t->block_graph = x;
@@ -210,8 +211,9 @@ static int launch_simt_thunk(const GemmArgs& g, const void* w, const void* x, in
   return launch_gemm_simt_f32(g, static_cast<const float*>(w), static_cast<const float*>(x), s);
 }
 
-// Grid, token tile and split-K plan of one projection (no side effects).
-static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g) {
+// Grid, token tile and split-K plan of one projection (no side effects).  nt_cap > 0 caps the
+// token tile.
+static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g, int nt_cap = 0) {
   g->M = M;
   g->N = w.rows;
   g->K = w.cols;
@@ -223,7 +225,7 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g)
     g->kb_per_split = 0;
     return 32;
   }
-  const int nt = pick_nt(h, M);
+  const int nt = nt_cap > 0 ? std::min(pick_nt(h, M), nt_cap) : pick_nt(h, M);
   g->n_tok_tiles = (M + nt - 1) / nt;
   g->n_slabs = w.paired ? (g->N / 2) / 64 : g->N / 128;
   const int kblocks = g->K / 64;
@@ -268,8 +270,15 @@ static int ktrace_reset(fdllm_handle* h) {
 static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epilogue epi, cudaStream_t s,
                     const void* norm_w = nullptr) {
   if (M <= 0) return FDLLM_OK;
+  // Short-K few-slab projections (qkv, o: K = 1536, <= 16 slabs) of a call the persistent kernel
+  // would cover with at most one 128-token tile per CTA (256-1152 rows) stay on the per-tile kernel
+  // with tune.short_k_nt-token tiles: the persistent kernel cannot overlap a lone tile's short
+  // main loop with another tile's epilogue (1024 rows: qkv 24.2 -> 20.3 us, o 13.4 -> 12.4 us).
+  const bool short_k = h->dtype == FDLLM_BFLOAT16 && h->tune.short_k_nt > 0 && norm_w == nullptr &&
+                       use_persist(h, M) && !w.paired && w.cols <= 2048 && w.rows / 128 <= 16 &&
+                       (w.rows / 128) * ((M + 127) / 128) <= h->num_sms;
   GemmArgs g{};
-  const int nt = plan_gemm(h, w, M, &g);
+  const int nt = plan_gemm(h, w, M, &g, short_k ? h->tune.short_k_nt : 0);
   g.err = h->err.p;
   g.epi = epi;
   if (norm_w != nullptr) {
@@ -282,7 +291,7 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
   if (h->dtype == FDLLM_FLOAT32) return timed_launch(h, g, s, launch_simt_thunk, w.ptr, X, 0);
   g.ktrace = ktrace_slot(h, 100 + epi.kind + (norm_w ? 2000 : 0));
   g.tune = h->tune.gemm_tune;
-  if (norm_w == nullptr && use_persist(h, M)) {
+  if (norm_w == nullptr && use_persist(h, M) && !short_k) {
     g.n_slabs = w.paired ? (g.N / 2) / 64 : g.N / 128;
     // 256-token tiles when they cover half the SMs, else 128 (twice the tiles for few-slab weights).
     // 96-token tiles where they shorten the busiest SM's share (rounds of tiles x tile height) by
@@ -294,15 +303,27 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
       return (tiles + h->num_sms - 1) / h->num_sms * nt;
     };
     if (h->tune.persist_nt96 && share(96) * 100 <= share(pnt) * 85) pnt = 96;
+    const int kblocks = g.K / 64;
+    // Long-K few-slab projections (down: K = 8960, 12 slabs) read every weight slab once per token
+    // tile and every token tile once per slab through L2.  With persist_splitk = 2 they take
+    // 256-token tiles with K split 2-4 ways so that the (tile, split) units still fill the SMs:
+    // a third less L2 traffic for down at 1024 rows.
+    int splits = 1;
+    if (h->tune.persist_splitk == 2 && kblocks >= 64) {
+      const int t256 = g.n_slabs * ((M + 255) / 256);
+      const int sp = std::min(4, h->num_sms / std::max(t256, 1));
+      if (sp >= 2 && kblocks / sp >= 32) {
+        pnt = 256;
+        splits = sp;
+      }
+    }
     g.n_tok_tiles = (M + pnt - 1) / pnt;
     g.tile_n = pnt;
     const int tiles = g.n_slabs * g.n_tok_tiles;
-    const int kblocks = g.K / 64;
     // Split K (<= 4 ways, >= 8 k blocks each) only when the tiles cover at most half the SMs (a
     // few-slab projection of a short prefill); with more tiles the last split's serial merge costs
     // more than the idle SMs (1024 rows: +30% per step).
-    int splits = 1;
-    if (h->tune.persist_splitk && tiles * 2 <= h->num_sms)
+    if (h->tune.persist_splitk == 1 && tiles * 2 <= h->num_sms)
       while (splits < 4 && tiles * splits < h->num_sms && kblocks / (2 * splits) >= 8) splits *= 2;
     g.splits = splits;
     g.kb_per_split = (kblocks + splits - 1) / splits;

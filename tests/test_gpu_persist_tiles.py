@@ -1,10 +1,14 @@
-"""Token-tile heights of the persistent projection GEMM (csrc/gemm_tc.cu gemm_tc_persist_kernel).
+"""Projection plans of large calls (csrc/model.cu run_gemm, csrc/gemm_tc.cu).
 
 A 1024-row batched cached step (32 requests x 32 rows, the configs[2] serving step) runs its
-projections on the persistent GEMM.  With FDLLM_TUNING=persist_nt96=1 the few-slab projections
-(o and down: 12 weight slabs at the 1.5B shapes) take 96-token tiles instead of 128; the result must
-match the default plan as two GPU plans of the same arithmetic, and the oracle at the bf16 noise
-floor (tests/_oracle_util.assert_within_bf16_noise).  MID: the 1.5B layer shapes, 2 layers.
+projections on the persistent GEMM by default.  Each alternative plan must match the plain
+persistent plan as two GPU plans of the same arithmetic, and the oracle at the bf16 noise floor
+(tests/_oracle_util.assert_within_bf16_noise).  The plans (FDLLM_TUNING):
+  persist_nt96=1    few-slab projections (o, down: 12 weight slabs) on 96-token tiles;
+  persist_splitk=2  the long-K projection (down: K = 8960) on 256-token tiles with K split 3 ways
+                    (fp32 partials merged in split order by the tile's last split);
+  short_k_nt=64     short-K projections (qkv, o: K = 1536) on the per-tile kernel, 64-token tiles.
+MID: the 1.5B layer shapes, 2 layers.
 """
 
 import pytest
@@ -31,24 +35,29 @@ def engines():
     params = make_synthetic_params(MID, seed=31, dtype="bfloat16", mask_id=4095)
     dev_params = [p.to(_dev()) for p in params]
     old = os.environ.get("FDLLM_TUNING")
+    engs = {}
     try:
-        os.environ["FDLLM_TUNING"] = "persist_nt96=0"
-        base = Engine(MID, dev_params, dtype="bfloat16")
-        os.environ["FDLLM_TUNING"] = "persist_nt96=1"
-        nt96 = Engine(MID, dev_params, dtype="bfloat16")
+        for spec in PLANS:
+            os.environ["FDLLM_TUNING"] = spec
+            engs[spec] = Engine(MID, dev_params, dtype="bfloat16")
     finally:
         if old is None:
             os.environ.pop("FDLLM_TUNING", None)
         else:
             os.environ["FDLLM_TUNING"] = old
-    return base, nt96, make_oracle(MID, params, "bfloat16"), make_reordered_oracle(MID, params, "bfloat16")
+    return engs, make_oracle(MID, params, "bfloat16"), make_reordered_oracle(MID, params, "bfloat16")
 
 
+PLANS = ["persist_nt96=0,persist_splitk=0,short_k_nt=0", "persist_nt96=1", "persist_splitk=2", "short_k_nt=64"]
+
+
+@pytest.mark.parametrize("plan", PLANS[1:])
 @pytest.mark.parametrize("n_req", [32, 31])
-def test_batched_step_with_96_token_tiles(engines, n_req):
+def test_batched_step_plans(engines, plan, n_req):
     """32 x 32 rows (11 tiles of 96, the last one partial) and 31 x 32 rows; caches of different
     prefix lengths."""
-    base, nt96, orc, alt = engines
+    engs, orc, alt = engines
+    base, nt96 = engs[PLANS[0]], engs[plan]
     g = torch.Generator().manual_seed(n_req)
     lens = [64 + 16 * i for i in range(n_req)]
     caches0 = []
@@ -64,13 +73,13 @@ def test_batched_step_with_96_token_tiles(engines, n_req):
         assert eng.device_error() == 0
         outs.append((h, [(k.cpu(), v.cpu()) for k, v in caches]))
     d = bf16_discrepancy(outs[1][0], outs[0][0])
-    assert d["out"] <= 1e-3 and d["rel"] <= 1e-2, f"96-token tiles vs default: {d}"
+    assert d["out"] <= 1e-3 and d["rel"] <= 1e-2, f"{plan} vs the plain persistent plan: {d}"
     for i in (0, n_req - 1):
         P = lens[i]
         kr, vr = caches0[i][0].clone(), caches0[i][1].clone()
         ka, va = caches0[i][0].clone(), caches0[i][1].clone()
         ref = orc.forward_cached(x[None, 32 * i:32 * i + 32], kr, vr, P, P)
         ref_alt = alt.forward_cached(x[None, 32 * i:32 * i + 32], ka, va, P, P)
-        assert_within_bf16_noise(outs[1][0][32 * i:32 * i + 32], ref[0], ref_alt[0], f"request {i} vs oracle")
+        assert_within_bf16_noise(outs[1][0][32 * i:32 * i + 32], ref[0], ref_alt[0], f"{plan} request {i} vs oracle")
         assert_within_bf16_noise(outs[1][1][i][0][:, :, P:P + 32], kr[:, :, P:P + 32], ka[:, :, P:P + 32],
-                                 f"request {i} K rows vs oracle")
+                                 f"{plan} request {i} K rows vs oracle")
