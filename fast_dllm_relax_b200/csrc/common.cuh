@@ -144,6 +144,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Wait until the global counter *p reaches `target` (acquire at GPU scope: what the arriving
+// CTAs wrote before their release is then visible); false if kWaitLimitNs elapsed first.
+__device__ __forceinline__ bool wait_count_geq(const unsigned* p, unsigned target) {
+  auto ld = [&]() {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+  };
+  if (ld() >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i) {
+      __nanosleep(32);
+      if (ld() >= target) return true;
+    }
+    if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
 // Barrier `id` over the first `nthr` threads that reach it (a multiple of 32); id 0 with
 // nthr == blockDim.x is __syncthreads().
 __device__ __forceinline__ void named_sync(int id, int nthr) {

@@ -430,6 +430,18 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
       // ---------------- TMA producer ----------------
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
+      // Weight k blocks this far beyond the one being loaded are prefetched into L2: the CTAs that
+      // share a slab walk it in step, so without it each k block arrives at HBM latency and only
+      // the shared-memory ring covers that latency.
+      const int l2a = (g.tune >> kGemmTunePersistL2Shift) & 0xff;
+      auto prefetch_a = [&](int kb, int slab) {
+        if (g.paired) {
+          tma_prefetch_l2_2d(&tmA, kb * 64, slab * 64);
+          tma_prefetch_l2_2d(&tmA, kb * 64, g.N / 2 + slab * 64);
+        } else {
+          tma_prefetch_l2_2d(&tmA, kb * 64, slab * 128);
+        }
+      };
       pdl_wait();
       ktrace_stamp<KT>(g.ktrace, 1);
       uint32_t it = 0;
@@ -439,7 +451,9 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
         const int slab = t / g.n_tok_tiles, tok0 = (t % g.n_tok_tiles) * kPNT;
         int kb0, kb1;
         kb_range(u, &kb0, &kb1);
+        for (int kb = kb0; kb < min(kb1, kb0 + l2a); ++kb) prefetch_a(kb, slab);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          if (kb + l2a < kb1) prefetch_a(kb + l2a, slab);
           const int s = it % kPStages;
           if (!mbar_wait(&empty[s], ((it / kPStages) & 1u) ^ 1u)) {
             report_wait(g.err, kErrTimeoutProducer, 11, g.M, g.splits);
@@ -533,19 +547,28 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
       named_sync(1, kPEpi);
       if (tid == 0) mbar_arrive(&tempty[buf]);  // the accumulator is free for the tile after next
       if (S > 1) {
+        // pmerge_all (each CTA holds at most one unit, so a tile's S splits run at the same time):
+        // every split waits for all S partials and merges every S-th 32-column chunk of the tile.
+        // Otherwise the tile's last split merges the whole tile.
         if (tid == 0) {
           __threadfence();
           const unsigned old = atomicAdd(g.pctr + t, 1u);
-          s_last = (old == static_cast<unsigned>(S) - 1u) ? 1 : 0;
-          if (s_last) {
-            __threadfence();
-            g.pctr[t] = 0u;  // the last arrival: nobody else touches this counter in this launch
+          if (g.pmerge_all) {
+            s_last = wait_count_geq(g.pctr + t, static_cast<unsigned>(S)) ? 1 : 0;
+            if (!s_last) report_wait(g.err, kErrTimeoutEpilogue, 16, g.M, g.splits);
+          } else {
+            s_last = (old == static_cast<unsigned>(S) - 1u) ? 1 : 0;
+            if (s_last) {
+              __threadfence();
+              g.pctr[t] = 0u;  // the last arrival: nobody else touches this counter in this launch
+            }
           }
         }
         named_sync(1, kPEpi);
         if (s_last) {  // sum the S partials in split order (deterministic), then the epilogue
           const float4* p0 = reinterpret_cast<const float4*>(g.ppart + static_cast<size_t>(t) * S * kPNT * 128);
-          for (int cb = 0; cb < kPNT && tok0 + cb < g.M; cb += kPChunk) {
+          for (int cb = g.pmerge_all ? sp * kPChunk : 0; cb < kPNT && tok0 + cb < g.M;
+               cb += g.pmerge_all ? S * kPChunk : kPChunk) {
             float4* a4 = reinterpret_cast<float4*>(acc);
             for (int i = tid; i < kPChunk * 32; i += kPEpi) {
               float4 v[4];
@@ -568,6 +591,13 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
             gemm_epilogue<bf16>(g, acc - static_cast<size_t>(cb) * 128, kPNT, tok0, slab, cb, cb + kPChunk, s_epi, tid,
                                 kPEpi, 1);
             named_sync(1, kPEpi);
+          }
+        }
+        if (g.pmerge_all && tid == 0) {  // the tile's last split to finish resets both counters
+          unsigned* done = g.pctr + n_tiles;
+          if (atomicAdd(done + t, 1u) == static_cast<unsigned>(S) - 1u) {
+            g.pctr[t] = 0u;
+            done[t] = 0u;
           }
         }
       }

@@ -46,6 +46,11 @@ struct Tuning {
                                // persistent kernel covers with <= 1 tile per CTA (0: persistent)
   int persist_nt96 = 1;        // 96-token persistent tiles where they balance the SMs better
                                // (o, down at 1024 rows; batched step 4.666 -> 4.470 ms with the two above)
+  int persist_l2_ahead = 0;    // weight k blocks the persistent GEMM prefetches into L2 ahead of its ring
+                               // (8: 8 x 4096 prefill 142.5 -> 139.5 ms, 1024-row step +1.3%)
+  int persist_merge_all = 1;   // persistent split-K in one wave: every split waits for the tile's
+                               // partials and merges its share (down at 1024 rows 44.7 -> 32.0 us)
+                               // instead of the last split merging the whole tile
   int attn_splits = 0;         // attention key splits of decode-sized calls (0: planned)
   int gu_fused_rows = 16;      // gate_up normalises its own B tiles up to this many token rows
   int block_graph = 1;         // fdllm_generate runs whole blocks as device-looped CUDA graphs

@@ -82,6 +82,7 @@ struct Epilogue {
 // ring (more bytes in flight per SM than the ring holds).
 constexpr int kGemmTunePrefetch = 1;
 constexpr int kGemmTuneL2Shift = 8;
+constexpr int kGemmTunePersistL2Shift = 16;  // bits 16-23: the persistent GEMM's L2 prefetch distance
 
 struct GemmArgs {
   int M, N, K;              // tokens, output features (weight rows), reduction
@@ -102,7 +103,8 @@ struct GemmArgs {
   // persistent GEMM split-K (splits <= 4): fp32 partial tiles [tiles][splits][NT][128] and per-tile
   // arrival counters (zero between launches; the last split resets its tile's counter)
   float* ppart;
-  unsigned* pctr;
+  unsigned* pctr;           // [2][tiles]: partials arrived, splits done (pmerge_all)
+  int pmerge_all;           // every split merges its share (only when each CTA holds <= 1 unit)
   unsigned long long* ktrace;  // phase stamps of this launch (kernel trace), or null
   int tune;                 // kGemmTune* bits
   int* err;

@@ -119,6 +119,8 @@ int fdllm::parse_tuning(const char* spec, Tuning* t) {
     else if (key == "attn_tc_min_q" && x >= 0) t->attn_tc_min_q = x;
     else if (key == "attn_tc_min_ctas" && x >= 0) t->attn_tc_min_ctas = x;
     else if (key == "persist_nt96" && (x == 0 || x == 1)) t->persist_nt96 = x;
+    else if (key == "persist_l2_ahead" && x >= 0 && x <= 64) t->persist_l2_ahead = x;
+    else if (key == "persist_merge_all" && (x == 0 || x == 1)) t->persist_merge_all = x;
     else return fail(FDLLM_ERR_INVALID, "unknown tuning key or value out of range: " + item);
   }
   return FDLLM_OK;
@@ -292,6 +294,7 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
   g.ktrace = ktrace_slot(h, 100 + epi.kind + (norm_w ? 2000 : 0));
   g.tune = h->tune.gemm_tune;
   if (norm_w == nullptr && use_persist(h, M) && !short_k) {
+    g.tune |= (h->tune.persist_l2_ahead & 0xff) << kGemmTunePersistL2Shift;
     g.n_slabs = w.paired ? (g.N / 2) / 64 : g.N / 128;
     // 256-token tiles when they cover half the SMs, else 128 (twice the tiles for few-slab weights).
     // 96-token tiles where they shorten the busiest SM's share (rounds of tiles x tile height) by
@@ -327,13 +330,15 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
       while (splits < 4 && tiles * splits < h->num_sms && kblocks / (2 * splits) >= 8) splits *= 2;
     g.splits = splits;
     g.kb_per_split = (kblocks + splits - 1) / splits;
+    const int grid = std::min(h->num_sms, tiles * splits);
     if (splits > 1) {
       FDLLM_TRY(h->persist_part.ensure(static_cast<size_t>(tiles) * splits * pnt * 128));
-      FDLLM_TRY(h->persist_ctr.ensure(static_cast<size_t>(tiles), true));
+      FDLLM_TRY(h->persist_ctr.ensure(2 * static_cast<size_t>(tiles), true));
       g.ppart = h->persist_part.p;
       g.pctr = h->persist_ctr.p;
+      // all splits of a tile run at once only when no CTA holds two units (one wave)
+      g.pmerge_all = h->tune.persist_merge_all && tiles * splits <= grid ? 1 : 0;
     }
-    const int grid = std::min(h->num_sms, tiles * splits);
     CUtensorMap tmB;
     FDLLM_TRY(make_map(&tmB, X, M, g.K, pnt));
     return timed_launch(h, g, s, launch_persist_thunk, &w.map, &tmB, grid);

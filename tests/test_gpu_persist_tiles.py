@@ -7,7 +7,10 @@ persistent plan as two GPU plans of the same arithmetic, and the oracle at the b
   persist_nt96=1    few-slab projections (o, down: 12 weight slabs) on 96-token tiles;
   persist_splitk=2  the long-K projection (down: K = 8960) on 256-token tiles with K split 3 ways
                     (fp32 partials merged in split order by the tile's last split);
-  short_k_nt=64     short-K projections (qkv, o: K = 1536) on the per-tile kernel, 64-token tiles.
+  short_k_nt=64     short-K projections (qkv, o: K = 1536) on the per-tile kernel, 64-token tiles;
+  persist_merge_all=1  with the split plan, every split of a tile waits for the others and merges
+                    every third 32-column chunk (instead of the last split merging them all);
+  persist_l2_ahead=8  the persistent producer prefetches weight k blocks 8 ahead into L2.
 MID: the 1.5B layer shapes, 2 layers.
 """
 
@@ -48,7 +51,8 @@ def engines():
     return engs, make_oracle(MID, params, "bfloat16"), make_reordered_oracle(MID, params, "bfloat16")
 
 
-PLANS = ["persist_nt96=0,persist_splitk=0,short_k_nt=0", "persist_nt96=1", "persist_splitk=2", "short_k_nt=64"]
+PLANS = ["persist_nt96=0,persist_splitk=0,short_k_nt=0,persist_merge_all=0", "persist_nt96=1", "persist_splitk=2",
+         "short_k_nt=64", "persist_splitk=2,persist_merge_all=1", "persist_l2_ahead=8"]
 
 
 @pytest.mark.parametrize("plan", PLANS[1:])
