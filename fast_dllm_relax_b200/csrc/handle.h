@@ -38,10 +38,12 @@ struct Tuning {
   int split_target = 0;        // CTAs per SM the split-K plan aims for (0: 2 at <= 32 rows, else 1)
   int split_max = 16;          // largest split-K cluster of the per-tile GEMM
   int gemm_tune = kGemmTunePrefetch | (2 << kGemmTuneL2Shift);  // kGemmTune* bits
-  int persist_min_rows = 256;  // token rows from which projections run on the persistent GEMM (0: never)
-  int persist_splitk = 2;      // split K inside the persistent GEMM: 1 while its tiles leave half
-                               // the SMs idle (+30% at 1024 rows); 2 only for long-K few-slab
-                               // projections on 256-token tiles (down at 1024 rows: 46.6 -> 45.2 us)
+  int persist_min_rows = 65;   // token rows from which projections run on the persistent GEMM (0:
+                               // never); prefix builds of 96 / 160 / 224 rows: 2.17 / 2.38 / 2.44 ->
+                               // 1.95 / 2.33 / 2.39 ms against 256 (64 rows: 1.53 -> 1.84, so not below)
+  int persist_splitk = 3;      // split K inside the persistent GEMM (bits): 1 while its tiles leave
+                               // half the SMs idle; 2 for long-K few-slab projections on 256-token
+                               // tiles (down at 1024 rows: 46.6 -> 45.2 us, 32.0 with merge_all)
   int short_k_nt = 64;         // per-tile token tile of short-K few-slab projections of calls the
                                // persistent kernel covers with <= 1 tile per CTA (0: persistent)
   int persist_nt96 = 1;        // 96-token persistent tiles where they balance the SMs better

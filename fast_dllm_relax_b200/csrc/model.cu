@@ -111,7 +111,7 @@ int fdllm::parse_tuning(const char* spec, Tuning* t) {
     else if (key == "split_max" && x >= 1 && x <= 16) t->split_max = x;
     else if (key == "gemm_tune" && x >= 0) t->gemm_tune = x;
     else if (key == "persist_min_rows" && x >= 0) t->persist_min_rows = x;
-    else if (key == "persist_splitk" && x >= 0 && x <= 2) t->persist_splitk = x;
+    else if (key == "persist_splitk" && x >= 0 && x <= 3) t->persist_splitk = x;
     else if (key == "short_k_nt" && (x == 0 || x == 64 || x == 128)) t->short_k_nt = x;
     else if (key == "attn_splits" && x >= 0 && x <= kMaxAttnSplits) t->attn_splits = x;
     else if (key == "gu_fused_rows" && x >= 0 && x <= 64) t->gu_fused_rows = x;
@@ -311,11 +311,18 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
     // tile and every token tile once per slab through L2.  With persist_splitk = 2 they take
     // 256-token tiles with K split 2-4 ways so that the (tile, split) units still fill the SMs:
     // a third less L2 traffic for down at 1024 rows.
+    // Split K (<= 4 ways, >= 8 k blocks each) when the tiles cover at most half the SMs (the
+    // projections of a short prefill).
     int splits = 1;
-    if (h->tune.persist_splitk == 2 && kblocks >= 64) {
+    const int tiles0 = g.n_slabs * ((M + pnt - 1) / pnt);
+    if ((h->tune.persist_splitk & 1) && tiles0 * 2 <= h->num_sms)
+      while (splits < 4 && tiles0 * splits < h->num_sms && kblocks / (2 * splits) >= 8) splits *= 2;
+    // The long-K plan wins when it covers at least as many SMs (down at 1024 rows: 48 tiles x 3
+    // splits against 132 unsplit 96-token tiles; at 224 rows 12 x 4 loses to 36 x 4).
+    if ((h->tune.persist_splitk & 2) && kblocks >= 64) {
       const int t256 = g.n_slabs * ((M + 255) / 256);
       const int sp = std::min(4, h->num_sms / std::max(t256, 1));
-      if (sp >= 2 && kblocks / sp >= 32) {
+      if (sp >= 2 && kblocks / sp >= 32 && t256 * sp >= tiles0 * splits) {
         pnt = 256;
         splits = sp;
       }
@@ -323,11 +330,6 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
     g.n_tok_tiles = (M + pnt - 1) / pnt;
     g.tile_n = pnt;
     const int tiles = g.n_slabs * g.n_tok_tiles;
-    // Split K (<= 4 ways, >= 8 k blocks each) only when the tiles cover at most half the SMs (a
-    // few-slab projection of a short prefill); with more tiles the last split's serial merge costs
-    // more than the idle SMs (1024 rows: +30% per step).
-    if (h->tune.persist_splitk == 1 && tiles * 2 <= h->num_sms)
-      while (splits < 4 && tiles * splits < h->num_sms && kblocks / (2 * splits) >= 8) splits *= 2;
     g.splits = splits;
     g.kb_per_split = (kblocks + splits - 1) / splits;
     const int grid = std::min(h->num_sms, tiles * splits);
