@@ -24,7 +24,7 @@ LIB_DIR = PKG / "lib"
 LIB = LIB_DIR / "libfdllm_sm100.so"
 INCLUDE = PKG.parent / "include"
 
-SOURCES = ["gemm_tc.cu", "gemm_simt.cu", "attention.cu", "attention_tc.cu", "elementwise.cu", "model.cu", "decode.cu"]
+SOURCES = ["gemm_tc.cu", "gemm_simt.cu", "attention.cu", "attention_tc.cu", "attention_tc_long.cu", "elementwise.cu", "model.cu", "decode.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-DNDEBUG"]

@@ -344,19 +344,26 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const AttnArgs a, const
   if (threadIdx.x == 0) ktrace_stamp<KT>(a.ktrace, 7);
 }
 
-int attention_tc_smem_bytes() { return kSmem; }
+int init_attention_tc_long_attributes();
+int launch_attention_tc_long(const AttnArgs& a, const CUtensorMap* maps_dev, dim3 grid, int tq, cudaStream_t s);
 
 int init_attention_tc_attributes() {
   cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (e == cudaSuccess) e = static_cast<cudaError_t>(init_attention_tc_long_attributes());
   return e;
 }
 
-int launch_attention_tc(const AttnArgs& a, const CUtensorMap* maps_dev, int max_q, cudaStream_t s) {
+// A grid that fits one CTA per SM (batched steps, short prefills) runs this kernel; a larger one
+// runs the O-in-TMEM variant of attention_tc_long.cu at two CTAs per SM (4 x 2048-token prefill:
+// 143 against 157 us a layer; 8 x 4096: 344 against 391 us; the 1024-row batched step keeps 20.4
+// us here against 22.0 there, where most key tiles would rescale O in TMEM).
+int launch_attention_tc(const AttnArgs& a, const CUtensorMap* maps_dev, int max_q, int num_sms, cudaStream_t s) {
   const int G = a.hq / a.hkv;
   if (a.hd != 128 || G < 1 || G > kRows / 8) return cudaErrorInvalidValue;
   const int tq = kRows / G;
   dim3 grid((max_q + tq - 1) / tq, a.hkv, a.n_reqs);
+  if (static_cast<long long>(grid.x) * grid.y * grid.z > num_sms) return launch_attention_tc_long(a, maps_dev, grid, tq, s);
   if (a.ktrace != nullptr) return launch_k(attn_tc_kernel<true>, grid, dim3(192), kSmem, s, a, maps_dev, tq);
   return launch_k(attn_tc_kernel<false>, grid, dim3(192), kSmem, s, a, maps_dev, tq);
 }

@@ -672,28 +672,6 @@ int init_gemm_tc_attributes() {
   return e;
 }
 
-int gemm_tc_smem_bytes(int nt) {
-  switch (nt) {
-    case 16: return TcCfg<16>::kSmem;
-    case 32: return TcCfg<32>::kSmem;
-    case 64: return TcCfg<64>::kSmem;
-    case 128: return TcCfg<128>::kSmem;
-    case 256: return TcCfg<256>::kSmem;
-    default: return -1;
-  }
-}
-
-int gemm_tc_stages(int nt) {
-  switch (nt) {
-    case 16: return TcCfg<16>::kStages;
-    case 32: return TcCfg<32>::kStages;
-    case 64: return TcCfg<64>::kStages;
-    case 128: return TcCfg<128>::kStages;
-    case 256: return TcCfg<256>::kStages;
-    default: return -1;
-  }
-}
-
 int launch_gemm_tc(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int nt, cudaStream_t s) {
   switch (nt) {
     case 16: return launch_nt<16>(a, tmA, tmB, s);

@@ -58,6 +58,7 @@ struct Tuning {
   int block_graph = 1;         // fdllm_generate runs whole blocks as device-looped CUDA graphs
   int attn_tc_min_q = 64;      // tcgen05 attention from this many query tokens per request (0: never)
   int attn_tc_min_ctas = 64;   // ... or from this many (request, KV head, query tile) CTAs
+  int attn_lazy_log2 = 0;      // tcgen05 attention: exponent base moves when a row's max grows by > 2^x
 };
 int parse_tuning(const char* spec, Tuning* t);
 

@@ -125,6 +125,8 @@ struct AttnArgs {
   int n_splits;             // key splits per (request, kv head, q tile) = cluster size
   int split_len;            // minimum keys per split (multiple of 64)
   int m_total;              // M: activation rows of all requests
+  float lazy_log2;          // tcgen05 kernel: a row's exponent base moves when its maximum grows by
+                            //   more than 2^lazy_log2 (0: whenever it grows)
   unsigned long long* ktrace;  // phase stamps of this launch (kernel trace), or null
   int* err;
 };
@@ -184,13 +186,11 @@ int launch_gemm_tc(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap&
 int launch_gemm_tc_persist(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int nt, int grid,
                            cudaStream_t s);
 int launch_gemm_simt_f32(const GemmArgs& a, const float* W, const float* X, cudaStream_t s);
-int gemm_tc_smem_bytes(int nt);
-int gemm_tc_stages(int nt);
 
 int launch_attention(const AttnArgs& a, int max_q, int dtype, cudaStream_t s);
 // tcgen05 attention (bf16, head_dim 128, no explicit bias): maps_dev holds two 3D tensor maps per
 // request (K then V: {kv_heads * head_dim, attended keys, layers}, box {64, 64, 1}, 128-byte swizzle).
-int launch_attention_tc(const AttnArgs& a, const CUtensorMap* maps_dev, int max_q, cudaStream_t s);
+int launch_attention_tc(const AttnArgs& a, const CUtensorMap* maps_dev, int max_q, int num_sms, cudaStream_t s);
 int init_attention_tc_attributes();
 int init_kernel_attributes();  // opt-in shared memory sizes; once per device, before any capture
 

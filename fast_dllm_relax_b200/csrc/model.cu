@@ -121,6 +121,7 @@ int fdllm::parse_tuning(const char* spec, Tuning* t) {
     else if (key == "persist_nt96" && (x == 0 || x == 1)) t->persist_nt96 = x;
     else if (key == "persist_l2_ahead" && x >= 0 && x <= 64) t->persist_l2_ahead = x;
     else if (key == "persist_merge_all" && (x == 0 || x == 1)) t->persist_merge_all = x;
+    else if (key == "attn_lazy_log2" && x >= 0 && x <= 16) t->attn_lazy_log2 = x;
     else return fail(FDLLM_ERR_INVALID, "unknown tuning key or value out of range: " + item);
   }
   return FDLLM_OK;
@@ -514,7 +515,8 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     a.err = h->err.p;
     a.ktrace = h->dtype == FDLLM_BFLOAT16 ? ktrace_slot(h, attn_tc ? 2 : 1) : nullptr;
     if (attn_tc) {
-      CUDA_TRY(launch_attention_tc(a, h->attn_maps.p, max_q, s));
+      a.lazy_log2 = static_cast<float>(h->tune.attn_lazy_log2);
+      CUDA_TRY(launch_attention_tc(a, h->attn_maps.p, max_q, h->num_sms, s));
     } else {
       CUDA_TRY(launch_attention(a, max_q, h->dtype, s));
     }
