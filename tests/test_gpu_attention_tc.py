@@ -1,5 +1,6 @@
-"""The tcgen05 attention (csrc/attention_tc.cu) against the oracle and against the mma.sync
-attention it replaces for calls with many query tokens.
+"""The tcgen05 attention (csrc/attention_tc.cu; csrc/attention_tc_long.cu for grids of more CTAs
+than SMs) against the oracle and against the mma.sync attention it replaces for calls with many
+query tokens.
 
 Two engines share one set of MID weights (the 1.5B layer shapes, 2 layers): the default one runs
 attention on the tensor cores from 64 query tokens per request; the other has it turned off
@@ -40,12 +41,18 @@ def engines():
         tc = Engine(MID, dev_params, dtype="bfloat16")
         os.environ["FDLLM_TUNING"] = "attn_tc_min_q=0"
         legacy = Engine(MID, dev_params, dtype="bfloat16")
+        os.environ["FDLLM_TUNING"] = "attn_lazy_log2=8"
+        lazy = Engine(MID, dev_params, dtype="bfloat16")
     finally:
         if old is None:
             os.environ.pop("FDLLM_TUNING", None)
         else:
             os.environ["FDLLM_TUNING"] = old
+    LAZY.append(lazy)
     return tc, legacy, make_oracle(MID, params, "bfloat16"), make_reordered_oracle(MID, params, "bfloat16")
+
+
+LAZY: list = []  # the engine whose long-prefill kernel moves its exponent base lazily (2^8)
 
 
 def _act(n, seed):
@@ -58,8 +65,10 @@ def _consistent(a, b, label):
     assert d["out"] <= 1e-3 and d["rel"] <= 1e-2, f"{label}: {d}"
 
 
-@pytest.mark.parametrize("P", [64, 96, 200, 1000])
+@pytest.mark.parametrize("P", [64, 96, 200, 1000, 2048])
 def test_prefix_build_matches_oracle_and_legacy(engines, P):
+    """P = 2048 is 98 query tiles x 2 KV heads = 196 CTAs: the O-in-TMEM kernel of
+    attention_tc_long.cu; the others fit one CTA per SM."""
     tc, legacy, orc, alt = engines
     x = _act(P, P)
     caches = []
@@ -114,3 +123,21 @@ def test_batched_ragged_prefix_and_cached_forward(engines):
         assert_within_bf16_noise(h_tc[o:o + 96], hr[0], ha[0], f"request {i} cached forward")
         o += 96
     assert tc.device_error() == 0 and legacy.device_error() == 0
+
+
+def test_long_prefill_with_lazy_base_matches_oracle(engines):
+    """attn_lazy_log2=8: the long-prefill kernel moves a row's exponent base only when its maximum
+    outgrows it by more than 2^8 -- equal in exact arithmetic, rounded differently; still at the
+    bf16 noise floor against the oracle."""
+    tc, legacy, orc, alt = engines
+    lazy = LAZY[0]
+    P = 2048
+    x = _act(P, 77)
+    k, v = lazy.new_cache(P + 32)
+    lazy.build_prefix_cache(x.to(_dev()), None, k, v)
+    ref = [torch.zeros((2, 1, P + 32, 2, 128), dtype=torch.bfloat16) for _ in range(4)]
+    orc.build_prefix_cache(x, build_block_bias(0, P, 32), ref[0], ref[1])
+    alt.build_prefix_cache(x, build_block_bias(0, P, 32), ref[2], ref[3])
+    for got, i, name in ((k, 0, "k"), (v, 1, "v")):
+        assert_within_bf16_noise(got[:, :, :P].cpu(), ref[i][:, :, :P], ref[2 + i][:, :, :P], f"lazy base {name}")
+    assert lazy.device_error() == 0
