@@ -345,7 +345,8 @@ __global__ void __launch_bounds__(192, 1) attn_tc_kernel(const AttnArgs a, const
 }
 
 int init_attention_tc_long_attributes();
-int launch_attention_tc_long(const AttnArgs& a, const CUtensorMap* maps_dev, dim3 grid, int tq, cudaStream_t s);
+int launch_attention_tc_long(const AttnArgs& a, const CUtensorMap* maps_dev, dim3 grid, int tq, int num_sms,
+                             cudaStream_t s);
 
 int init_attention_tc_attributes() {
   cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
@@ -363,7 +364,8 @@ int launch_attention_tc(const AttnArgs& a, const CUtensorMap* maps_dev, int max_
   if (a.hd != 128 || G < 1 || G > kRows / 8) return cudaErrorInvalidValue;
   const int tq = kRows / G;
   dim3 grid((max_q + tq - 1) / tq, a.hkv, a.n_reqs);
-  if (static_cast<long long>(grid.x) * grid.y * grid.z > num_sms) return launch_attention_tc_long(a, maps_dev, grid, tq, s);
+  if (a.n_splits > 1 || static_cast<long long>(grid.x) * grid.y * grid.z > num_sms)
+    return launch_attention_tc_long(a, maps_dev, grid, tq, num_sms, s);  // key splits are that kernel's
   if (a.ktrace != nullptr) return launch_k(attn_tc_kernel<true>, grid, dim3(192), kSmem, s, a, maps_dev, tq);
   return launch_k(attn_tc_kernel<false>, grid, dim3(192), kSmem, s, a, maps_dev, tq);
 }

@@ -38,7 +38,7 @@ namespace {
 
 constexpr int kRows = 128;                    // MMA M: packed (token, head) query rows
 constexpr int kKeys = 64;                     // keys per tile (S columns, P.V reduction)
-constexpr int kMaxStages = 2;                 // K/V ring depth (P_j is written over K_j)
+constexpr int kMaxStages = 3;                 // K/V ring depth (P_j is written over K_j): 2 or 3
 constexpr int kQBytes = kRows * 128 * 2;      // Q tile: two 64-column sub-tiles of 128 rows (32 KB)
 constexpr int kKvHalf = kKeys * 64 * 2;       // one 64-column box of 64 keys (8 KB)
 constexpr int kKvStage = 4 * kKvHalf;         // K (2 boxes) + V (2 boxes) = 32 KB
@@ -55,7 +55,8 @@ constexpr uint32_t kTmemS = 0;                // S buffers: columns [0, 64), [64
 constexpr uint32_t kTmemO = 128;              // O accumulator: columns [128, 256)
 constexpr uint32_t kTmemCols = 256;
 constexpr float kLog2e = 1.4426950408889634f;
-static_assert(RingCfg<2>::kSmem <= 227 * 1024 / 2, "two CTAs per SM");
+static_assert(RingCfg<2>::kSmem <= 227 * 1024 / 2, "two CTAs per SM with two stages");
+static_assert(RingCfg<3>::kSmem <= 227 * 1024, "shared memory budget");
 
 struct TcBars {
   uint64_t kv_full[kMaxStages], kv_empty[kMaxStages];
@@ -98,13 +99,22 @@ __global__ void __launch_bounds__(192, 2) attn_tc_long_kernel(const AttnArgs a, 
   pdl_trigger();
   if (threadIdx.x == 0) ktrace_stamp<KT>(a.ktrace, 1);
   const int G = a.hq / a.hkv;
-  const int qtile = blockIdx.x, kvh = blockIdx.y, req = blockIdx.z;
+  const int S = a.n_splits > 1 ? a.n_splits : 1;  // key splits (cached calls only)
+  const int qtile = blockIdx.x, kvh = blockIdx.y, req = blockIdx.z / S, split = blockIdx.z % S;
   const ReqDesc r = a.reqs[req];
   const int tok0 = qtile * tq;  // first request-local token of this tile
   if (tok0 >= r.n_q) return;    // uniform over the CTA: nothing allocated yet
   const int tok_last = min(tok0 + tq, r.n_q) - 1;
   const int key_end = row_key_limit(r, tok_last, a.causal_block);  // the last token attends the most
-  const int n_tiles = (key_end + kKeys - 1) / kKeys;
+  // this split's keys [kbeg, kend): equal 64-aligned shares of the request's own length (read on
+  // the device), the last one shorter, trailing ones possibly empty
+  int kbeg = 0, kend = key_end;
+  if (S > 1) {
+    const int share = ((key_end + S - 1) / S + kKeys - 1) / kKeys * kKeys;
+    kbeg = min(key_end, split * share);
+    kend = min(key_end, kbeg + share);
+  }
+  const int n_tiles = (kend - kbeg + kKeys - 1) / kKeys;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -156,8 +166,9 @@ __global__ void __launch_bounds__(192, 2) attn_tc_long_kernel(const AttnArgs a, 
         mbar_arrive_expect_tx(&bar->kv_full[st], kKvStage);
         uint8_t* kvs = sKv + st * kKvStage;
         for (int h = 0; h < 2; ++h) {
-          tma_load_3d(kvs + h * kKvHalf, mk, &bar->kv_full[st], kvh * a.hd + h * 64, j * kKeys, layer_c, pol);
-          tma_load_3d(kvs + (2 + h) * kKvHalf, mv, &bar->kv_full[st], kvh * a.hd + h * 64, j * kKeys, layer_c, pol);
+          tma_load_3d(kvs + h * kKvHalf, mk, &bar->kv_full[st], kvh * a.hd + h * 64, kbeg + j * kKeys, layer_c, pol);
+          tma_load_3d(kvs + (2 + h) * kKvHalf, mv, &bar->kv_full[st], kvh * a.hd + h * 64, kbeg + j * kKeys, layer_c,
+                      pol);
         }
         ++issued;
       }
@@ -219,7 +230,7 @@ __global__ void __launch_bounds__(192, 2) attn_tc_long_kernel(const AttnArgs a, 
     const int tl = tok0 + row / G;  // request-local token of this row
     const int head = kvh * G + row % G;
     const bool valid = row < tq * G && tl < r.n_q;
-    const int lim = valid ? row_key_limit(r, tl, a.causal_block) : 0;
+    const int lim = valid ? min(row_key_limit(r, tl, a.causal_block), kend) : 0;
     const size_t qstride = static_cast<size_t>(a.hq) * a.hd;
     {  // Q row -> the two swizzled 64-column sub-tiles (zeros for padding rows)
       const uint4* src = reinterpret_cast<const uint4*>(static_cast<const bf16*>(a.q) +
@@ -261,7 +272,7 @@ __global__ void __launch_bounds__(192, 2) attn_tc_long_kernel(const AttnArgs a, 
       if (lane == 0) mbar_arrive(&bar->s_free[sb]);
 
       // mask, scale to the log2 domain, tile maximum
-      const int key0 = j * kKeys;
+      const int key0 = kbeg + j * kKeys;
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kKeys; ++c) {
@@ -320,7 +331,32 @@ __global__ void __launch_bounds__(192, 2) attn_tc_long_kernel(const AttnArgs a, 
     }
     // every P.V has landed (its own one-phase barrier: o_done may be two phases on by now): O / l
     if (ok && n_tiles > 0) ok = warp_wait(&bar->o_final, 0, a.err, 26, a.m_total);
-    if (ok) {
+    if (ok && S > 1) {
+      // a split's partial: O / l in fp32 and the row's log2-sum-exp, for attn_split_merge_kernel
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const size_t prow = (static_cast<size_t>(split) * a.m_total + r.q_tok0 + (valid ? tl : 0)) * a.hq + head;
+      float4* dst = reinterpret_cast<float4*>(a.part + prow * a.hd);
+      tc_fence_after_sync();
+#pragma unroll
+      for (int c0 = 0; c0 < 128; c0 += 32) {
+        uint32_t v[32];
+        if (n_tiles > 0) {
+          tmem_ld_32x32b_x32(tmem + lane_base + kTmemO + c0, v);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[c] = 0u;
+        }
+        if (valid) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            dst[c0 / 4 + c] = make_float4(__uint_as_float(v[4 * c]) * inv, __uint_as_float(v[4 * c + 1]) * inv,
+                                          __uint_as_float(v[4 * c + 2]) * inv, __uint_as_float(v[4 * c + 3]) * inv);
+        }
+      }
+      if (valid) a.part_lse[prow] = l_run > 0.f ? m_base + log2f(l_run) : -INFINITY;
+      tc_fence_before_sync();
+    } else if (ok) {
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       uint4* dst = reinterpret_cast<uint4*>(static_cast<bf16*>(a.out) + static_cast<size_t>(r.q_tok0 + (valid ? tl : 0)) * qstride +
                                             static_cast<size_t>(head) * a.hd);
@@ -361,17 +397,67 @@ __global__ void __launch_bounds__(192, 2) attn_tc_long_kernel(const AttnArgs a, 
 }
 
 int init_attention_tc_long_attributes() {
-  cudaError_t e = cudaFuncSetAttribute(attn_tc_long_kernel<false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       RingCfg<2>::kSmem);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(attn_tc_long_kernel<true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, RingCfg<2>::kSmem);
+  cudaError_t e = cudaSuccess;
+  for (auto f : {attn_tc_long_kernel<false, 2>, attn_tc_long_kernel<true, 2>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, RingCfg<2>::kSmem);
+  for (auto f : {attn_tc_long_kernel<false, 3>, attn_tc_long_kernel<true, 3>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, RingCfg<3>::kSmem);
   return e;
 }
 
-int launch_attention_tc_long(const AttnArgs& a, const CUtensorMap* maps_dev, dim3 grid, int tq, cudaStream_t s) {
-  if (a.ktrace != nullptr)
-    return launch_k(attn_tc_long_kernel<true, 2>, grid, dim3(192), RingCfg<2>::kSmem, s, a, maps_dev, tq);
-  return launch_k(attn_tc_long_kernel<false, 2>, grid, dim3(192), RingCfg<2>::kSmem, s, a, maps_dev, tq);
+// Key-split merge: one warp per (token, query head); each lane merges 4 of the 128 columns over
+// the S splits in split order: out = sum_s w_s o_s / sum_s w_s, w_s = 2^(lse_s - max lse).
+__global__ void __launch_bounds__(256) attn_split_merge_kernel(const AttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int pair = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (pair >= a.m_total * a.hq) return;
+  const int S = a.n_splits;
+  const size_t plane = static_cast<size_t>(a.m_total) * a.hq;
+  float l[kMaxAttnSplits];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int m = 0; m < kMaxAttnSplits; ++m) {
+    l[m] = m < S ? a.part_lse[m * plane + pair] : -INFINITY;
+    mx = fmaxf(mx, l[m]);
+  }
+  float4 v[kMaxAttnSplits];
+#pragma unroll
+  for (int m = 0; m < kMaxAttnSplits; ++m)
+    v[m] = m < S ? reinterpret_cast<const float4*>(a.part + (m * plane + pair) * a.hd)[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+  float den = 0.f;
+  float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int m = 0; m < kMaxAttnSplits; ++m) {
+    const float w = (m < S && l[m] != -INFINITY) ? exp2f(l[m] - mx) : 0.f;
+    den += w;
+    num.x += w * v[m].x;
+    num.y += w * v[m].y;
+    num.z += w * v[m].z;
+    num.w += w * v[m].w;
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  bf16* op = static_cast<bf16*>(a.out) + static_cast<size_t>(pair) * a.hd + lane * 4;
+  *reinterpret_cast<uint2*>(op) = make_uint2(pack_bf16x2(num.x * inv, num.y * inv), pack_bf16x2(num.z * inv, num.w * inv));
+}
+
+// Two CTAs per SM (2-stage ring) for grids of more CTAs than SMs, else one with a 3-stage ring (two
+// K/V tiles in flight ahead of the one being computed).
+int launch_attention_tc_long(const AttnArgs& a, const CUtensorMap* maps_dev, dim3 grid, int tq, int num_sms,
+                             cudaStream_t s) {
+  const int S = a.n_splits > 1 ? a.n_splits : 1;
+  grid.z *= S;
+  const bool two = static_cast<long long>(grid.x) * grid.y * grid.z > num_sms;
+  cudaError_t e;
+  if (two)
+    e = a.ktrace != nullptr ? launch_k(attn_tc_long_kernel<true, 2>, grid, dim3(192), RingCfg<2>::kSmem, s, a, maps_dev, tq)
+                            : launch_k(attn_tc_long_kernel<false, 2>, grid, dim3(192), RingCfg<2>::kSmem, s, a, maps_dev, tq);
+  else
+    e = a.ktrace != nullptr ? launch_k(attn_tc_long_kernel<true, 3>, grid, dim3(192), RingCfg<3>::kSmem, s, a, maps_dev, tq)
+                            : launch_k(attn_tc_long_kernel<false, 3>, grid, dim3(192), RingCfg<3>::kSmem, s, a, maps_dev, tq);
+  if (e != cudaSuccess || S == 1) return e;
+  const int pairs = a.m_total * a.hq;
+  return launch_k(attn_split_merge_kernel, dim3((pairs + 7) / 8), dim3(256), 0, s, a);
 }
 
 }  // namespace fdllm

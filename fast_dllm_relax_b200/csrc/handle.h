@@ -59,6 +59,11 @@ struct Tuning {
   int attn_tc_min_q = 64;      // tcgen05 attention from this many query tokens per request (0: never)
   int attn_tc_min_ctas = 64;   // ... or from this many (request, KV head, query tile) CTAs
   int attn_lazy_log2 = 0;      // tcgen05 attention: exponent base moves when a row's max grows by > 2^x
+  int attn_tc_split_min_keys = 1024;  // cached calls from this many keys whose tcgen05 grid leaves SMs
+                               // idle: the keys split over CTAs and merged (8 x 32 rows at 4096 keys:
+                               // 3.28 -> 2.92 ms a forward; 512 slows the 32 x 32-row step at 768 keys)
+  int attn_tc_split_target = 1;  // ... as many splits as give this many CTAs per SM (1: a 3-stage ring
+                               // each, 2.92 ms; 2: two CTAs per SM on 2 stages, 2.97 ms)
 };
 int parse_tuning(const char* spec, Tuning* t);
 
@@ -185,7 +190,8 @@ struct fdllm_handle {
   DevBuf<int> tok_req, tok_pos, tok_row, tmp_ids, targets;
   DevBuf<ReqDesc> reqs;
   DevBuf<float> conf_part, tmp_maxp, ss;  // ss: per-slab row sums of squares
-  DevBuf<CUtensorMap> attn_maps;            // tcgen05 attention: K and V tensor maps per request
+  DevBuf<CUtensorMap> attn_maps;
+  DevBuf<float> attn_part, attn_part_lse;  // tcgen05 key-split partials            // tcgen05 attention: K and V tensor maps per request
   DevBuf<float> persist_part;               // persistent-GEMM split-K partial tiles
   DevBuf<unsigned> persist_ctr;             // persistent-GEMM per-tile split counters (zero between launches)
   // kernel trace (fdllm_kernel_trace_enable / _read): phase stamps of every projection and

@@ -127,6 +127,8 @@ struct AttnArgs {
   int m_total;              // M: activation rows of all requests
   float lazy_log2;          // tcgen05 kernel: a row's exponent base moves when its maximum grows by
                             //   more than 2^lazy_log2 (0: whenever it grows)
+  float* part;              // tcgen05 key splits: [n_splits][m_total][hq][hd] fp32 partial O / l
+  float* part_lse;          //   [n_splits][m_total][hq] log2-sum-exp of each partial row
   unsigned long long* ktrace;  // phase stamps of this launch (kernel trace), or null
   int* err;
 };

@@ -122,6 +122,8 @@ int fdllm::parse_tuning(const char* spec, Tuning* t) {
     else if (key == "persist_l2_ahead" && x >= 0 && x <= 64) t->persist_l2_ahead = x;
     else if (key == "persist_merge_all" && (x == 0 || x == 1)) t->persist_merge_all = x;
     else if (key == "attn_lazy_log2" && x >= 0 && x <= 16) t->attn_lazy_log2 = x;
+    else if (key == "attn_tc_split_min_keys" && x >= 0) t->attn_tc_split_min_keys = x;
+    else if (key == "attn_tc_split_target" && (x == 1 || x == 2)) t->attn_tc_split_target = x;
     else return fail(FDLLM_ERR_INVALID, "unknown tuning key or value out of range: " + item);
   }
   return FDLLM_OK;
@@ -442,8 +444,19 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
   // prefix 384: 1.41 ms per step against 1.55; 32 requests x 32 rows: 4.68 ms against 4.96).
   const int gqa = c.num_attention_heads / c.num_key_value_heads;
   const int tc_ctas = nreq * c.num_key_value_heads * ((max_q + 128 / gqa - 1) / (128 / gqa));
+  // Long cached key ranges with few (request, KV head, query tile) CTAs: the tcgen05 kernel with the
+  // keys split (up to 8 ways, >= 256 keys each) so that the grid covers the SMs, and a merge launch
+  // (8 requests x 32 rows over 4096 keys: 27 against 43.5 us a layer on the mma.sync kernel).
+  int tc_splits = 1;
+  if (bias == nullptr && causal_block == 0 && h->tune.attn_tc_split_min_keys > 0 &&
+      max_l >= h->tune.attn_tc_split_min_keys && tc_ctas > 0)
+    tc_splits = std::max(1, std::min({kMaxAttnSplits,
+                                      h->tune.attn_tc_split_target == 2 ? (2 * h->num_sms + tc_ctas - 1) / tc_ctas
+                                                                        : h->num_sms / tc_ctas,
+                                      max_l / 256}));
   bool attn_tc = h->dtype == FDLLM_BFLOAT16 && c.head_dim == 128 && bias == nullptr && !h->capturing && gqa <= 16 &&
-                 h->tune.attn_tc_min_q > 0 && (max_q >= h->tune.attn_tc_min_q || tc_ctas >= h->tune.attn_tc_min_ctas);
+                 h->tune.attn_tc_min_q > 0 &&
+                 (max_q >= h->tune.attn_tc_min_q || tc_ctas >= h->tune.attn_tc_min_ctas || tc_splits > 1);
   for (const ReqDesc& r : reqs) attn_tc = attn_tc && r.plen_dev == nullptr && r.attend_len > 0;
   if (attn_tc) {
     std::vector<CUtensorMap> maps(2 * static_cast<size_t>(nreq));
@@ -458,6 +471,11 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
                             layer_bytes));
     }
     FDLLM_TRY(h->attn_maps.ensure(maps.size()));
+    if (tc_splits > 1) {
+      const size_t rows = static_cast<size_t>(tc_splits) * M * c.num_attention_heads;
+      FDLLM_TRY(h->attn_part.ensure(rows * c.head_dim));
+      FDLLM_TRY(h->attn_part_lse.ensure(rows));
+    }
     CUDA_TRY(cudaMemcpyAsync(h->attn_maps.p, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, s));
   }
 
@@ -516,6 +534,9 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
     a.ktrace = h->dtype == FDLLM_BFLOAT16 ? ktrace_slot(h, attn_tc ? 2 : 1) : nullptr;
     if (attn_tc) {
       a.lazy_log2 = static_cast<float>(h->tune.attn_lazy_log2);
+      a.n_splits = tc_splits;
+      a.part = h->attn_part.p;
+      a.part_lse = h->attn_part_lse.p;
       CUDA_TRY(launch_attention_tc(a, h->attn_maps.p, max_q, h->num_sms, s));
     } else {
       CUDA_TRY(launch_attention(a, max_q, h->dtype, s));

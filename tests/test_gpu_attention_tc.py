@@ -43,6 +43,8 @@ def engines():
         legacy = Engine(MID, dev_params, dtype="bfloat16")
         os.environ["FDLLM_TUNING"] = "attn_lazy_log2=8"
         lazy = Engine(MID, dev_params, dtype="bfloat16")
+        os.environ["FDLLM_TUNING"] = "attn_tc_split_min_keys=1024"
+        SPLIT.append(Engine(MID, dev_params, dtype="bfloat16"))
     finally:
         if old is None:
             os.environ.pop("FDLLM_TUNING", None)
@@ -53,6 +55,7 @@ def engines():
 
 
 LAZY: list = []  # the engine whose long-prefill kernel moves its exponent base lazily (2^8)
+SPLIT: list = []  # the engine that splits long cached key ranges over tcgen05 CTAs (from 1024 keys)
 
 
 def _act(n, seed):
@@ -141,3 +144,44 @@ def test_long_prefill_with_lazy_base_matches_oracle(engines):
     for got, i, name in ((k, 0, "k"), (v, 1, "v")):
         assert_within_bf16_noise(got[:, :, :P].cpu(), ref[i][:, :, :P], ref[2 + i][:, :, :P], f"lazy base {name}")
     assert lazy.device_error() == 0
+
+
+def _random_caches(P, seed):
+    g = torch.Generator().manual_seed(seed)
+    shape = (MID.num_hidden_layers, 1, P + 32, MID.num_key_value_heads, MID.head_dim)
+    return [(torch.randn(shape, generator=g) * 0.5).to(torch.bfloat16) for _ in range(2)]
+
+
+def test_cached_key_splits_match_oracle_and_legacy(engines):
+    """Long cached key ranges with few CTAs (decode steps over 1100-3000 prefix tokens): the tcgen05
+    kernel with the keys split over up to 8 CTAs per (request, KV head, query tile), partials merged
+    by log-sum-exp in a second launch -- against the oracle at the bf16 noise floor and against the
+    default plan (the mma.sync key-split kernel)."""
+    tc, legacy, orc, alt = engines
+    split = SPLIT[0]
+    lens = [1100, 1500, 2600]
+    caches0 = [_random_caches(P, 300 + P) for P in lens]
+    x = torch.cat([_act(32, 400 + i)[0] for i in range(len(lens))])
+    outs = {}
+    for name, eng in (("split", split), ("default", tc)):
+        caches = [(k.to(_dev()), v.to(_dev())) for k, v in caches0]
+        reqs = [dict(k=k, v=v, rows=32, prefix_len=P) for (k, v), P in zip(caches, lens)]
+        outs[name] = eng.forward_cached_batch(x.to(_dev()), reqs).cpu()
+        assert eng.device_error() == 0, name
+    _consistent(outs["split"], outs["default"], "key-split tcgen05 vs default plan")
+    for i, P in enumerate(lens):
+        kr, vr = caches0[i][0].clone(), caches0[i][1].clone()
+        ka, va = caches0[i][0].clone(), caches0[i][1].clone()
+        ref = orc.forward_cached(x[None, 32 * i:32 * i + 32], kr, vr, P, P)
+        ref_alt = alt.forward_cached(x[None, 32 * i:32 * i + 32], ka, va, P, P)
+        assert_within_bf16_noise(outs["split"][32 * i:32 * i + 32], ref[0], ref_alt[0], f"request {i} (P={P})")
+    # one request alone: 4 (KV head, query tile) CTAs, 8 splits
+    P = 3000
+    k0, v0 = _random_caches(P, 9)
+    x1 = _act(32, 10)
+    k, v = k0.to(_dev()), v0.to(_dev())
+    got = split.forward_cached(x1.to(_dev()), k, v, P, P).cpu()
+    ref = orc.forward_cached(x1, k0.clone(), v0.clone(), P, P)
+    ref_alt = alt.forward_cached(x1, k0.clone(), v0.clone(), P, P)
+    assert_within_bf16_noise(got, ref, ref_alt, "one request, P=3000")
+    assert split.device_error() == 0
