@@ -166,9 +166,13 @@ __device__ void epi_prefetch(const GemmArgs& g, int tok0, int slab, int row0, in
 // tid = 0..nthr-1 (a multiple of 32); they synchronise with named barrier `bar_id` (0 with
 // nthr == blockDim.x is __syncthreads()).
 // pre: inputs loaded by epi_prefetch for the same rows and threads, or null.
+// setup0 / setup1 (QkvRope): the tile rows whose per-token destinations are (re)built into s_epi
+// by this call; -1 (default) = [row0, row1).  A caller that walks one tile in chunks builds them
+// for the whole tile with its first chunk and passes an empty range afterwards.
 template <typename T>
 __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, int slab, int row0, int row1,
-                              unsigned char* s_epi, int tid, int nthr, int bar_id, const EpiPre<T>* pre = nullptr) {
+                              unsigned char* s_epi, int tid, int nthr, int bar_id, const EpiPre<T>* pre = nullptr,
+                              int setup0 = -1, int setup1 = -1) {
   const Epilogue& e = g.epi;
   const bool have_pre = pre != nullptr && pre->n > 0;
   constexpr int V = Chunk<T>::V;
@@ -317,7 +321,11 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
       T** s_kb = reinterpret_cast<T**>(s_epi + 1024);            // [256]
       T** s_vb = reinterpret_cast<T**>(s_epi + 1024 + 2048);     // [256]
       const T* bias = static_cast<const T*>(e.bias);
-      for (int t = row0 + tid; t < row1; t += nthr) {
+      if (setup0 < 0) {
+        setup0 = row0;
+        setup1 = row1;
+      }
+      for (int t = setup0 + tid; t < setup1; t += nthr) {
         const int tok = tok0 + t;
         T* kb = nullptr;
         T* vb = nullptr;

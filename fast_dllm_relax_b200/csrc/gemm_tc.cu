@@ -537,9 +537,9 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
         if (S > 1) {  // publish this split's chunk; the tile's last split finishes the tile
           const float4* a4 = reinterpret_cast<const float4*>(acc);
           for (int i = tid; i < kPChunk * 32; i += kPEpi) __stcg(mine + cb * 32 + i, a4[i]);
-        } else {
+        } else {  // the tile's per-token destinations are built with its first chunk
           gemm_epilogue<bf16>(g, acc - static_cast<size_t>(cb) * 128, kPNT, tok0, slab, cb, cb + kPChunk, s_epi, tid,
-                              kPEpi, 1);
+                              kPEpi, 1, nullptr, 0, cb == 0 ? kPNT : 0);
         }
         named_sync(1, kPEpi);
       }
