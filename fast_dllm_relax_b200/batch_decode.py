@@ -199,6 +199,7 @@ def generate_batch(engine: Engine, prompts: Sequence[Sequence[int]], *, max_new_
             pending.pop(i, None)
 
     ev = []  # (start, end) CUDA event pairs around prefix-cache builds
+    staging = None  # pinned host buffer of a step's token ids and unmask descriptors
     t0 = torch.cuda.Event(enable_timing=True) if timing is not None else None
     if t0 is not None:
         t0.record()
@@ -229,9 +230,13 @@ def generate_batch(engine: Engine, prompts: Sequence[Sequence[int]], *, max_new_
         if not steps:
             continue
         # every pending cached step in one batched forward, one fused confidence launch and one
-        # unmask launch; the token ids and the unmask descriptors go up in one copy
+        # unmask launch; the token ids and the unmask descriptors go up in one copy, from a pinned
+        # staging buffer (a copy from pageable memory blocks the host for the whole transfer)
         n_ids = sum(len(op[2]) for _, op in steps)
-        buf = np.empty(n_ids + 5 * len(steps), dtype=np.int32)
+        need = n_ids + 5 * len(steps)
+        if staging is None or staging.numel() < need:
+            staging = torch.empty(max(need, 4096), dtype=torch.int32, pin_memory=torch.device(dev).type == "cuda")
+        buf = staging.numpy()[:need]
         reqs, o = [], 0
         for j, (_, (_, cache, ids, write_rel, attend_rel, base, win, bits)) in enumerate(steps):
             rows = len(ids)
@@ -240,7 +245,7 @@ def generate_batch(engine: Engine, prompts: Sequence[Sequence[int]], *, max_new_
             reqs.append(dict(k=cache.k, v=cache.v, rows=rows, prefix_len=cache.prefix_len, write_rel=write_rel,
                              attend_rel=attend_rel))
             o += rows
-        up = torch.from_numpy(buf).to(dev)
+        up = staging[:need].to(dev, non_blocking=True)
         hidden = engine.forward_cached_batch(engine.embed(up[:n_ids]), reqs)
         cid, cmax = engine.confidence(hidden)
         dec = engine.unmask_batch(cid, cmax, up[n_ids:].view(len(steps), 5), threshold).cpu().numpy()

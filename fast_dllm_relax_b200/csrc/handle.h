@@ -75,6 +75,12 @@ struct Weight {
   CUtensorMap map{};
 };
 
+struct BMapEntry {  // an encoded 2D activation tensor map and what it was encoded for
+  const void* base;
+  int rows, cols, box_rows;
+  CUtensorMap map;
+};
+
 struct LayerW {
   Weight qkv, o, gu, down;
   const void* qkv_b = nullptr;
@@ -191,6 +197,8 @@ struct fdllm_handle {
   DevBuf<ReqDesc> reqs;
   DevBuf<float> conf_part, tmp_maxp, ss;  // ss: per-slab row sums of squares
   DevBuf<CUtensorMap> attn_maps;
+  std::vector<long long> attn_maps_key;  // the requests whose maps attn_maps holds
+  std::vector<BMapEntry> bmaps;          // encoded activation maps of the projections
   DevBuf<float> attn_part, attn_part_lse;  // tcgen05 key-split partials            // tcgen05 attention: K and V tensor maps per request
   DevBuf<float> persist_part;               // persistent-GEMM split-K partial tiles
   DevBuf<unsigned> persist_ctr;             // persistent-GEMM per-tile split counters (zero between launches)

@@ -68,6 +68,20 @@ static int make_map(CUtensorMap* map, const void* base, int rows, int cols, int 
   return FDLLM_OK;
 }
 
+// make_map through the handle's cache of activation maps: the projections of a forward read the
+// same few workspace buffers at the same sizes in every layer, so each map is encoded once.
+static int cached_map(fdllm_handle* h, CUtensorMap* map, const void* base, int rows, int cols, int box_rows) {
+  for (const BMapEntry& e : h->bmaps)
+    if (e.base == base && e.rows == rows && e.cols == cols && e.box_rows == box_rows) {
+      *map = e.map;
+      return FDLLM_OK;
+    }
+  FDLLM_TRY(make_map(map, base, rows, cols, box_rows));
+  if (h->bmaps.size() >= 64) h->bmaps.erase(h->bmaps.begin());
+  h->bmaps.push_back(BMapEntry{base, rows, cols, box_rows, *map});
+  return FDLLM_OK;
+}
+
 // K or V cache of one request as a 3D bf16 tensor {kv_heads * head_dim, keys, layers} (row stride
 // row_bytes, layer stride layer_bytes), box {64, 64, 1}, 128-byte swizzle.  `keys` is the attended
 // length, so keys past it read as zeros whatever the cache rows beyond it hold.
@@ -345,11 +359,11 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
       g.pmerge_all = h->tune.persist_merge_all && tiles * splits <= grid ? 1 : 0;
     }
     CUtensorMap tmB;
-    FDLLM_TRY(make_map(&tmB, X, M, g.K, pnt));
+    FDLLM_TRY(cached_map(h, &tmB, X, M, g.K, pnt));
     return timed_launch(h, g, s, launch_persist_thunk, &w.map, &tmB, grid);
   }
   CUtensorMap tmB;
-  FDLLM_TRY(make_map(&tmB, X, M, g.K, nt));
+  FDLLM_TRY(cached_map(h, &tmB, X, M, g.K, nt));
   return timed_launch(h, g, s, launch_tc_thunk, &w.map, &tmB, nt);
 }
 
@@ -459,9 +473,20 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
                  (max_q >= h->tune.attn_tc_min_q || tc_ctas >= h->tune.attn_tc_min_ctas || tc_splits > 1);
   for (const ReqDesc& r : reqs) attn_tc = attn_tc && r.plen_dev == nullptr && r.attend_len > 0;
   if (attn_tc) {
-    std::vector<CUtensorMap> maps(2 * static_cast<size_t>(nreq));
+    // The maps depend on each request's caches and attended length only: a call with the same
+    // requests as the previous one (the steps of one block) reuses the uploaded maps.
+    std::vector<long long> key;
+    key.reserve(4 * static_cast<size_t>(nreq));
+    for (const ReqDesc& r : reqs) {
+      key.push_back(reinterpret_cast<long long>(r.k));
+      key.push_back(reinterpret_cast<long long>(r.v));
+      key.push_back((static_cast<long long>(r.cap) << 32) | static_cast<unsigned>(r.attend_len));
+      key.push_back(r.layer_stride);
+    }
+    const bool reuse = key == h->attn_maps_key && h->attn_maps.n >= 2 * static_cast<size_t>(nreq);
+    std::vector<CUtensorMap> maps(reuse ? 0 : 2 * static_cast<size_t>(nreq));
     const size_t row_bytes = static_cast<size_t>(c.num_key_value_heads) * c.head_dim * h->esz;
-    for (int i = 0; i < nreq; ++i) {
+    for (int i = 0; i < nreq && !reuse; ++i) {
       const ReqDesc& r = reqs[i];
       const int layers = r.layer_stride != 0 ? c.num_hidden_layers : 1;
       const size_t layer_bytes = static_cast<size_t>(r.cap) * row_bytes;
@@ -470,13 +495,17 @@ int fdllm::forward_core(fdllm_handle* h, const void* x, int M, std::vector<ReqDe
       FDLLM_TRY(make_kv_map(&maps[2 * i + 1], r.v, c.num_key_value_heads * c.head_dim, r.attend_len, layers, row_bytes,
                             layer_bytes));
     }
-    FDLLM_TRY(h->attn_maps.ensure(maps.size()));
+    if (!reuse) h->attn_maps_key.clear();  // set again below once the upload is queued
+    FDLLM_TRY(h->attn_maps.ensure(2 * static_cast<size_t>(nreq)));
     if (tc_splits > 1) {
       const size_t rows = static_cast<size_t>(tc_splits) * M * c.num_attention_heads;
       FDLLM_TRY(h->attn_part.ensure(rows * c.head_dim));
       FDLLM_TRY(h->attn_part_lse.ensure(rows));
     }
-    CUDA_TRY(cudaMemcpyAsync(h->attn_maps.p, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, s));
+    if (!reuse) {
+      CUDA_TRY(cudaMemcpyAsync(h->attn_maps.p, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice, s));
+      h->attn_maps_key = std::move(key);
+    }
   }
 
   Epilogue base{};
