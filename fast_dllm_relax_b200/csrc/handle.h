@@ -196,10 +196,10 @@ struct fdllm_handle {
   DevBuf<int> tok_req, tok_pos, tok_row, tmp_ids, targets;
   DevBuf<ReqDesc> reqs;
   DevBuf<float> conf_part, tmp_maxp, ss;  // ss: per-slab row sums of squares
-  DevBuf<CUtensorMap> attn_maps;
-  std::vector<long long> attn_maps_key;  // the requests whose maps attn_maps holds
-  std::vector<BMapEntry> bmaps;          // encoded activation maps of the projections
-  DevBuf<float> attn_part, attn_part_lse;  // tcgen05 key-split partials            // tcgen05 attention: K and V tensor maps per request
+  DevBuf<CUtensorMap> attn_maps;          // tcgen05 attention: K and V tensor maps per request
+  std::vector<long long> attn_maps_key;   // the requests whose maps attn_maps holds
+  std::vector<fdllm::BMapEntry> bmaps;    // encoded activation maps of the projections
+  DevBuf<float> attn_part, attn_part_lse;  // tcgen05 key-split partials
   DevBuf<float> persist_part;               // persistent-GEMM split-K partial tiles
   DevBuf<unsigned> persist_ctr;             // persistent-GEMM per-tile split counters (zero between launches)
   // kernel trace (fdllm_kernel_trace_enable / _read): phase stamps of every projection and
