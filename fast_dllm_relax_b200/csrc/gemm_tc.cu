@@ -360,6 +360,9 @@ __global__ void __launch_bounds__(128, 4)
 // the other accumulator 32 token columns at a time through shared memory into the fused epilogue
 // (two warps per TMEM lane quarter, 16 columns each).
 // The epilogue of tile i therefore overlaps the mainloop of tile i + 1.
+// The lm_head's confidence epilogues (g.conf_t) swap the operands: 128 tokens are the MMA's M and a
+// pair of weight slabs its N = 256, so TMEM lane = token and each epilogue thread reduces one
+// token's 128 logits of one slab without crossing lanes.
 template <int NT>
 struct PCfg {
   static_assert(NT == 96 || NT == 128 || NT == 256, "persistent token tiles: 96, 128 or 256");
@@ -373,7 +376,72 @@ struct PCfg {
 };
 constexpr int kPEpi = 256;  // epilogue threads (warps 2-9)
 
-template <int NT, bool KT>
+// Confidence / log-softmax-gather partial of one token and one 128-row vocabulary slab
+// (model/metal.py:316-374), from the token's 128 fp32 logits in TMEM columns [taddr, taddr + 128)
+// of this thread's lane (the tokens-on-M tile).  Same result, bit for bit, as the shared-memory
+// path of gemm_epilogue (kEpiConf / kEpiLseGather), whose warp gives lane l the values f = l,
+// l + 32, l + 64, l + 96: the logits are rounded to bf16; the maximum and its first index; then
+// exp(v - max) summed into 32 four-term column sums in that order, which are added in lane 0's
+// xor-butterfly tree (offsets 16, 8, 4, 2, 1).  kFull: all 128 rows are below N.
+template <bool kFull>
+__device__ __forceinline__ void conf_slab_from_tmem(const GemmArgs& g, uint32_t taddr, int tok, int slab, int tg) {
+  const int f0 = slab * 128;
+  const int nv = kFull ? 128 : min(128, g.N - f0);
+  float best = -INFINITY, tv = 0.f;
+  int best_i = 0x7fffffff;
+  // 16 columns per TMEM load keeps the live set small (the column sums plus one load)
+  uint32_t r[16];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    tmem_ld_32x32b_x16(taddr + c * 16, r);
+    tmem_ld_wait();
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      const float2 p = round2_bf16(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+      v[j] = (kFull || c * 16 + j < nv) ? p.x : __int_as_float(0x7fc00000);  // rows >= N: NaN, never chosen
+      v[j + 1] = (kFull || c * 16 + j + 1 < nv) ? p.y : __int_as_float(0x7fc00000);
+      if (c * 16 + j == tg) tv = p.x;
+      if (c * 16 + j + 1 == tg) tv = p.y;
+    }
+    float m = v[0];
+#pragma unroll
+    for (int j = 1; j < 16; ++j) m = fmaxf(m, v[j]);  // NaN-ignoring; -inf only if no value is larger
+    int mi = 0x7fffffff;
+#pragma unroll
+    for (int j = 15; j >= 0; --j)
+      if (v[j] == m) mi = f0 + c * 16 + j;  // first index of the group's maximum
+    // groups ascend, so an equal later maximum keeps the earlier index; an all-NaN group has none
+    if (m > best || (best_i == 0x7fffffff && m == best)) {
+      best = m;
+      best_i = mi;
+    }
+  }
+  float s[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) s[j] = 0.f;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    tmem_ld_32x32b_x16(taddr + c * 16, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      const float2 p = round2_bf16(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+      const int f = c * 16 + j;  // column sum f % 32
+      if (kFull || f < nv) s[f & 31] += expf(p.x - best);
+      if (kFull || f + 1 < nv) s[(f + 1) & 31] += expf(p.y - best);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int j = 0; j < off; ++j) s[j] += s[j + off];
+  if (tok < g.M)
+    *reinterpret_cast<float4*>(g.epi.part + (static_cast<size_t>(tok) * g.n_slabs + slab) * 4) =
+        make_float4(best, __int_as_float(best_i), s[0], tv);
+}
+
+template <int NT, bool KT, bool TR = false>
 __global__ void __launch_bounds__(64 + kPEpi, 1)
     gemm_tc_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const GemmArgs g) {
@@ -393,7 +461,13 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
   __shared__ __align__(16) unsigned char s_epi[5120];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_tiles = g.n_slabs * g.n_tok_tiles;
+  // tokens-on-M tiles (g.conf_t): A = 128 token rows, B = two weight slabs (256 rows), so a tile is
+  // (slab pair, 128-token tile); the ring stage has the same 16 + 32 KB split as NT = 256
+  static_assert(!TR || NT == 256, "tokens-on-M tiles use the 256-column stage");
+  constexpr bool tr = TR;
+  const int n_wt = tr ? (g.n_slabs + 1) / 2 : g.n_slabs;  // weight tiles
+  const int tok_h = tr ? 128 : kPNT;                      // token rows per tile
+  const int n_tiles = n_wt * g.n_tok_tiles;
   const int nk = g.K / 64;
   const int S = g.splits > 1 ? g.splits : 1;  // split-K: unit = (tile, split), neighbours split one tile
   const int n_units = n_tiles * S;
@@ -435,7 +509,10 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
       // the shared-memory ring covers that latency.
       const int l2a = (g.tune >> kGemmTunePersistL2Shift) & 0xff;
       auto prefetch_a = [&](int kb, int slab) {
-        if (g.paired) {
+        if (tr) {
+          tma_prefetch_l2_2d(&tmA, kb * 64, slab * 256);
+          tma_prefetch_l2_2d(&tmA, kb * 64, slab * 256 + 128);
+        } else if (g.paired) {
           tma_prefetch_l2_2d(&tmA, kb * 64, slab * 64);
           tma_prefetch_l2_2d(&tmA, kb * 64, g.N / 2 + slab * 64);
         } else {
@@ -448,7 +525,7 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
       bool ok = true;
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const int t = u / S;
-        const int slab = t / g.n_tok_tiles, tok0 = (t % g.n_tok_tiles) * kPNT;
+        const int slab = t / g.n_tok_tiles, tok0 = (t % g.n_tok_tiles) * tok_h;
         int kb0, kb1;
         kb_range(u, &kb0, &kb1);
         for (int kb = kb0; kb < min(kb1, kb0 + l2a); ++kb) prefetch_a(kb, slab);
@@ -460,8 +537,18 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], kPStage);
           uint8_t* a = ring + s * kPStage;
+          if (tr) {
+            // an odd slab count leaves the last pair one slab: its second half is not loaded, and
+            // the accumulator columns it feeds are never read
+            const bool second = 2 * slab + 1 < g.n_slabs;
+            mbar_arrive_expect_tx(&full[s], second ? kPStage : kPStage - 16384);
+            tma_load_2d(a, &tmB, &full[s], kb * 64, tok0, pol_x);
+            tma_load_2d(a + 16384, &tmA, &full[s], kb * 64, slab * 256, pol_w);
+            if (second) tma_load_2d(a + 32768, &tmA, &full[s], kb * 64, slab * 256 + 128, pol_w);
+            continue;
+          }
+          mbar_arrive_expect_tx(&full[s], kPStage);
           if (g.paired) {
             tma_load_2d(a, &tmA, &full[s], kb * 64, slab * 64, pol_w);
             tma_load_2d(a + 8192, &tmA, &full[s], kb * 64, g.N / 2 + slab * 64, pol_w);
@@ -517,13 +604,32 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
     uint32_t ti = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++ti) {
       const int t = u / S, sp = u % S;
-      const int slab = t / g.n_tok_tiles, tok0 = (t % g.n_tok_tiles) * kPNT;
+      const int slab = t / g.n_tok_tiles, tok0 = (t % g.n_tok_tiles) * tok_h;
       const uint32_t buf = ti & 1u;
       if (!mbar_wait(&tfull[buf], (ti >> 1) & 1u)) {
         report_wait(g.err, kErrTimeoutEpilogue, 15, g.M, g.splits);
         break;
       }
       tc_fence_after_sync();
+      if (tr) {
+        // tokens-on-M tile: lane quarter q holds tokens tok0 + 32 q + lane, and `half` picks the
+        // pair's slab (accumulator columns [128 half, 128 half + 128))
+        const int sl = 2 * slab + half;
+        if (sl < g.n_slabs) {  // warp-uniform
+          const int tok = tok0 + q * 32 + lane;
+          const int tg = (g.epi.kind == kEpiLseGather && tok < g.M) ? g.epi.target[tok] - sl * 128 : -1;
+          const uint32_t taddr = tmem + buf * PCfg<NT>::kAccStride + (static_cast<uint32_t>(q * 32) << 16) +
+                                 static_cast<uint32_t>(half * 128);
+          if ((sl + 1) * 128 <= g.N)
+            conf_slab_from_tmem<true>(g, taddr, tok, sl, tg);
+          else
+            conf_slab_from_tmem<false>(g, taddr, tok, sl, tg);
+        }
+        tc_fence_before_sync();
+        named_sync(1, kPEpi);
+        if (tid == 0) mbar_arrive(&tempty[buf]);  // the accumulator is free for the tile after next
+        continue;
+      }
       // split-K: this unit's fp32 partial tile [NT][128] (tile t, split sp)
       float4* mine = S > 1 ? reinterpret_cast<float4*>(g.ppart + (static_cast<size_t>(t) * S + sp) * kPNT * 128) : nullptr;
       for (int cb = 0; cb < kPNT && tok0 + cb < g.M; cb += kPChunk) {
@@ -616,6 +722,9 @@ __global__ void __launch_bounds__(64 + kPEpi, 1)
 int launch_gemm_tc_persist(const GemmArgs& a, const CUtensorMap& tmA, const CUtensorMap& tmB, int nt, int grid,
                            cudaStream_t s) {
   const bool kt = a.ktrace != nullptr;
+  if (nt == 256 && a.conf_t)
+    return kt ? launch_k(gemm_tc_persist_kernel<256, true, true>, dim3(grid), dim3(64 + kPEpi), PCfg<256>::kSmem, s, tmA, tmB, a)
+              : launch_k(gemm_tc_persist_kernel<256, false, true>, dim3(grid), dim3(64 + kPEpi), PCfg<256>::kSmem, s, tmA, tmB, a);
   if (nt == 256)
     return kt ? launch_k(gemm_tc_persist_kernel<256, true>, dim3(grid), dim3(64 + kPEpi), PCfg<256>::kSmem, s, tmA, tmB, a)
               : launch_k(gemm_tc_persist_kernel<256, false>, dim3(grid), dim3(64 + kPEpi), PCfg<256>::kSmem, s, tmA, tmB, a);
@@ -656,6 +765,10 @@ int init_gemm_tc_attributes() {
                                        PCfg<256>::kSmem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(gemm_tc_persist_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<256>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc_persist_kernel<256, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<256>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc_persist_kernel<256, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<256>::kSmem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(gemm_tc_persist_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg<128>::kSmem);
   if (e == cudaSuccess)

@@ -53,7 +53,11 @@ struct Tuning {
   int persist_merge_all = 1;   // persistent split-K in one wave: every split waits for the tile's
                                // partials and merges its share (down at 1024 rows 44.7 -> 32.0 us)
                                // instead of the last split merging the whole tile
-  int attn_splits = 0;         // attention key splits of decode-sized calls (0: planned)
+  int persist_conf_t = 1;      // the persistent lm_head + confidence / log-softmax-gather GEMM puts
+                               // 128 tokens on the MMA's M side, so each epilogue thread reduces one
+                               // token's 128-logit slab in registers (0: tokens on N, lane-tree
+                               // reductions through shared memory)
+  int attn_splits = 0;        // attention key splits of decode-sized calls (0: planned)
   int gu_fused_rows = 16;      // gate_up normalises its own B tiles up to this many token rows
   int block_graph = 1;         // fdllm_generate runs whole blocks as device-looped CUDA graphs
   int attn_tc_min_q = 64;      // tcgen05 attention from this many query tokens per request (0: never)

@@ -105,6 +105,10 @@ struct GemmArgs {
   float* ppart;
   unsigned* pctr;           // [2][tiles]: partials arrived, splits done (pmerge_all)
   int pmerge_all;           // every split merges its share (only when each CTA holds <= 1 unit)
+  // persistent GEMM (tile_n 256), confidence / log-softmax-gather epilogues only: 128 token rows on
+  // the MMA's M side and two 128-row weight slabs on N, so TMEM lane = token; n_tok_tiles counts
+  // 128-token tiles and the B map's box is 128 rows
+  int conf_t;
   unsigned long long* ktrace;  // phase stamps of this launch (kernel trace), or null
   int tune;                 // kGemmTune* bits
   int* err;

@@ -135,6 +135,7 @@ int fdllm::parse_tuning(const char* spec, Tuning* t) {
     else if (key == "persist_nt96" && (x == 0 || x == 1)) t->persist_nt96 = x;
     else if (key == "persist_l2_ahead" && x >= 0 && x <= 64) t->persist_l2_ahead = x;
     else if (key == "persist_merge_all" && (x == 0 || x == 1)) t->persist_merge_all = x;
+    else if (key == "persist_conf_t" && (x == 0 || x == 1)) t->persist_conf_t = x;
     else if (key == "attn_lazy_log2" && x >= 0 && x <= 16) t->attn_lazy_log2 = x;
     else if (key == "attn_tc_split_min_keys" && x >= 0) t->attn_tc_split_min_keys = x;
     else if (key == "attn_tc_split_target" && (x == 1 || x == 2)) t->attn_tc_split_target = x;
@@ -312,6 +313,21 @@ static int run_gemm(fdllm_handle* h, const Weight& w, const void* X, int M, Epil
   g.tune = h->tune.gemm_tune;
   if (norm_w == nullptr && use_persist(h, M) && !short_k) {
     g.tune |= (h->tune.persist_l2_ahead & 0xff) << kGemmTunePersistL2Shift;
+    if (h->tune.persist_conf_t && !w.paired && (epi.kind == kEpiConf || epi.kind == kEpiLseGather)) {
+      // lm_head + confidence: 128-token tiles on the MMA's M side against slab pairs, each
+      // epilogue thread reducing one token's slab in registers (1024 rows: 0.80 ms with the
+      // tokens on N and the reductions across lanes)
+      g.conf_t = 1;
+      g.n_slabs = g.N / 128;
+      g.n_tok_tiles = (M + 127) / 128;
+      g.tile_n = 256;
+      g.splits = 1;
+      g.kb_per_split = g.K / 64;
+      const int tiles = (g.n_slabs + 1) / 2 * g.n_tok_tiles;
+      CUtensorMap tmB;
+      FDLLM_TRY(cached_map(h, &tmB, X, M, g.K, 128));
+      return timed_launch(h, g, s, launch_persist_thunk, &w.map, &tmB, std::min(h->num_sms, tiles));
+    }
     g.n_slabs = w.paired ? (g.N / 2) / 64 : g.N / 128;
     // 256-token tiles when they cover half the SMs, else 128 (twice the tiles for few-slab weights).
     // 96-token tiles where they shorten the busiest SM's share (rounds of tiles x tile height) by
