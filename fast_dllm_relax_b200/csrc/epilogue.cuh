@@ -345,22 +345,27 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
         s_kb[t] = kb;
         s_vb[t] = vb;
       }
-      // Phase 1: projection + bias, rounded to the model dtype (the op's output tensor).
-      for (int idx = row0 * 128 + 2 * tid; idx < row1 * 128; idx += 2 * nthr) {  // pairs of features
-        const int F = slab * 128 + (idx & 127);
-        if (F < g.N) {
-          const float2 y = round_pair<T>(acc[idx] + to_f<T>(bias[F]), acc[idx + 1] + to_f<T>(bias[F + 1]));
-          acc[idx] = y.x;
-          acc[idx + 1] = y.y;
-        }
-      }
-      named_sync(bar_id, nthr);
-      // Phase 2: rotate q and k (partner element d +- hd/2 of the same head, inside this slab),
-      // scatter q to qout and k / v to the request's cache row.
+      if (setup1 > setup0) named_sync(bar_id, nthr);  // the destinations are visible
+      // One pass over the chunks: a chunk's bias, and its RoPE partner's, are added and rounded
+      // here (the partner's value recomputed from the accumulator, as the prefetched path above
+      // does), so the tile needs neither a rounding pass nor a barrier between the two.  When nthr
+      // is a multiple of CPR (the tcgen05 kernels' 128 and 256 threads) every chunk of a thread
+      // covers the same 8 features, and its two bias chunks are loaded once.
       const int hd = e.hd, half = e.hd >> 1, hq = e.hq, hkv = e.hkv;
       const T* cos_t = static_cast<const T*>(e.rope_cos);
       const T* sin_t = static_cast<const T*>(e.rope_sin);
       T* q = static_cast<T*>(e.qout);
+      auto load_bias = [&](int c, Chunk<T>& a, Chunk<T>& bp) {
+        const int F0 = slab * 128 + (c % CPR) * V;
+        if (F0 >= g.N) return;
+        const int head = F0 / hd, d0 = F0 - head * hd;
+        a = ld_const_chunk(bias + F0);
+        if (head < hq + hkv) bp = ld_const_chunk(bias + (d0 < half ? F0 + half : F0 - half));
+      };
+      const bool fixed = nthr % CPR == 0;
+      Chunk<T> ba, bb;
+      ba.u = bb.u = make_uint4(0u, 0u, 0u, 0u);
+      if (fixed) load_bias(cbeg + tid, ba, bb);
       for (int c0 = cbeg + tid; c0 < cend; c0 += nthr * kEpiBatch) {
         Chunk<T> cs[kEpiBatch], sn[kEpiBatch];
 #pragma unroll
@@ -381,17 +386,23 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
           const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
           if (c >= cend || tok >= g.M || F0 >= g.N) continue;
           const int head = F0 / hd, d0 = F0 - head * hd;
-          const float* x = acc + t * 128 + f0;
+          Chunk<T> a = ba, bp = bb;
+          if (!fixed) load_bias(c, a, bp);
+          float x[V];
+          ld_acc<V>(acc + t * 128 + f0, x);
           Chunk<T> o;
           if (head < hq + hkv) {
             const bool lo = d0 < half;
-            const float* xp = lo ? x + half : x - half;
+            float xp[V];
+            ld_acc<V>(acc + t * 128 + (lo ? f0 + half : f0 - half), xp);
 #pragma unroll
             for (int v = 0; v < V; v += 2) {
-              const float r0 = lo ? -xp[v] : xp[v], r1 = lo ? -xp[v + 1] : xp[v + 1];
-              const float2 c = round_pair<T>(x[v] * to_f<T>(cs[b].e[v]), x[v + 1] * to_f<T>(cs[b].e[v + 1]));
+              const float2 y = round_pair<T>(x[v] + to_f<T>(a.e[v]), x[v + 1] + to_f<T>(a.e[v + 1]));
+              const float2 yp = round_pair<T>(xp[v] + to_f<T>(bp.e[v]), xp[v + 1] + to_f<T>(bp.e[v + 1]));
+              const float r0 = lo ? -yp.x : yp.x, r1 = lo ? -yp.y : yp.y;
+              const float2 cv = round_pair<T>(y.x * to_f<T>(cs[b].e[v]), y.y * to_f<T>(cs[b].e[v + 1]));
               const float2 sv = round_pair<T>(r0 * to_f<T>(sn[b].e[v]), r1 * to_f<T>(sn[b].e[v + 1]));
-              set_pair<T>(&o.e[v], c.x + sv.x, c.y + sv.y);  // T(round(c + s)) == T(c + s)
+              set_pair<T>(&o.e[v], cv.x + sv.x, cv.y + sv.y);  // T(round(c + s)) == T(c + s)
             }
             if (head < hq) {
               st_chunk(q + (size_t)tok * (hq * hd) + F0, o);
@@ -400,7 +411,10 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
             }
           } else if (s_vb[t] != nullptr) {
 #pragma unroll
-            for (int v = 0; v < V; v += 2) set_pair<T>(&o.e[v], x[v], x[v + 1]);
+            for (int v = 0; v < V; v += 2) {
+              const float2 y = round_pair<T>(x[v] + to_f<T>(a.e[v]), x[v + 1] + to_f<T>(a.e[v + 1]));
+              set_pair<T>(&o.e[v], y.x, y.y);
+            }
             st_chunk(s_vb[t] + (head - hq - hkv) * hd + d0, o);
           }
         }
