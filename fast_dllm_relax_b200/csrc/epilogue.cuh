@@ -161,6 +161,48 @@ __device__ void epi_prefetch(const GemmArgs& g, int tok0, int slab, int row0, in
   }
 }
 
+// Per-token destinations of a qkv tile's rows [t0, t1) into s_epi (RoPE position, the K and V
+// cache row bases of this layer, null where the token has no cache row), so that the element loop
+// of the epilogue carries no dependent global loads.  l2: also prefetch each token's K and V rows
+// into L2, for a caller that builds them while the main loop still runs: the epilogue's stores
+// then find their lines and address translations warm (one step of 32 requests scatters each
+// layer's rows over 64 cache allocations).
+template <typename T>
+__device__ void qkv_dest_setup(const GemmArgs& g, int tok0, int t0, int t1, unsigned char* s_epi, int tid, int nthr,
+                               bool l2) {
+  const Epilogue& e = g.epi;
+  int* s_pos = reinterpret_cast<int*>(s_epi);              // [256]
+  T** s_kb = reinterpret_cast<T**>(s_epi + 1024);         // [256]
+  T** s_vb = reinterpret_cast<T**>(s_epi + 1024 + 2048);  // [256]
+  for (int t = t0 + tid; t < t1; t += nthr) {
+    const int tok = tok0 + t;
+    T* kb = nullptr;
+    T* vb = nullptr;
+    int pos = 0;
+    if (tok < g.M) {
+      pos = e.tok.pos[tok];
+      pos = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // range checked in prepare
+      const ReqDesc& r = e.reqs[e.tok.req[tok]];
+      const int row = e.tok.row[tok];
+      if (row >= 0 && row < r.cap) {
+        const size_t off = (size_t)e.layer * r.layer_stride + (size_t)row * e.hkv * e.hd;
+        kb = static_cast<T*>(r.k) + off;
+        vb = static_cast<T*>(r.v) + off;
+        if (l2) {
+          const int bytes = e.hkv * e.hd * static_cast<int>(sizeof(T));
+          for (int o = 0; o < bytes; o += 128) {
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(kb) + o));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(vb) + o));
+          }
+        }
+      }
+    }
+    s_pos[t] = pos;
+    s_kb[t] = kb;
+    s_vb[t] = vb;
+  }
+}
+
 // Rows [row0, row1) of the tile are processed (a split-K cluster member owns a share of the rows).
 // s_epi: 5120 bytes of shared scratch owned by the calling kernel.  The calling threads are
 // tid = 0..nthr-1 (a multiple of 32); they synchronise with named barrier `bar_id` (0 with
@@ -315,36 +357,15 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
         }
         break;
       }
-      // Per-token destinations (RoPE position, cache row, K / V bases) once per tile, in shared
-      // memory, so the element loop below carries no dependent global loads.
-      int* s_pos = reinterpret_cast<int*>(s_epi);                 // [256]
-      T** s_kb = reinterpret_cast<T**>(s_epi + 1024);            // [256]
-      T** s_vb = reinterpret_cast<T**>(s_epi + 1024 + 2048);     // [256]
-      const T* bias = static_cast<const T*>(e.bias);
       if (setup0 < 0) {
         setup0 = row0;
         setup1 = row1;
       }
-      for (int t = setup0 + tid; t < setup1; t += nthr) {
-        const int tok = tok0 + t;
-        T* kb = nullptr;
-        T* vb = nullptr;
-        int pos = 0;
-        if (tok < g.M) {
-          pos = e.tok.pos[tok];
-          pos = pos < 0 ? 0 : (pos >= e.max_pos ? e.max_pos - 1 : pos);  // range checked in prepare
-          const ReqDesc& r = e.reqs[e.tok.req[tok]];
-          const int row = e.tok.row[tok];
-          if (row >= 0 && row < r.cap) {
-            const size_t off = (size_t)e.layer * r.layer_stride + (size_t)row * e.hkv * e.hd;
-            kb = static_cast<T*>(r.k) + off;
-            vb = static_cast<T*>(r.v) + off;
-          }
-        }
-        s_pos[t] = pos;
-        s_kb[t] = kb;
-        s_vb[t] = vb;
-      }
+      qkv_dest_setup<T>(g, tok0, setup0, setup1, s_epi, tid, nthr, false);
+      int* s_pos = reinterpret_cast<int*>(s_epi);
+      T** s_kb = reinterpret_cast<T**>(s_epi + 1024);
+      T** s_vb = reinterpret_cast<T**>(s_epi + 1024 + 2048);
+      const T* bias = static_cast<const T*>(e.bias);
       if (setup1 > setup0) named_sync(bar_id, nthr);  // the destinations are visible
       // One pass over the chunks: a chunk's bias, and its RoPE partner's, are added and rounded
       // here (the partner's value recomputed from the accumulator, as the prefetched path above
@@ -366,57 +387,60 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
       Chunk<T> ba, bb;
       ba.u = bb.u = make_uint4(0u, 0u, 0u, 0u);
       if (fixed) load_bias(cbeg + tid, ba, bb);
-      for (int c0 = cbeg + tid; c0 < cend; c0 += nthr * kEpiBatch) {
-        Chunk<T> cs[kEpiBatch], sn[kEpiBatch];
-#pragma unroll
-        for (int b = 0; b < kEpiBatch; ++b) {  // table loads first
-          const int c = c0 + b * nthr;
-          const int t = c / CPR, f0 = (c % CPR) * V, F0 = slab * 128 + f0;
-          if (c >= cend || tok0 + t >= g.M || F0 >= g.N) continue;
-          const int head = F0 / hd, d0 = F0 - head * hd;
-          if (head < hq + hkv) {
-            const size_t ti = (size_t)s_pos[t] * half + (d0 < half ? d0 : d0 - half);
-            cs[b] = ld_const_chunk(cos_t + ti);
-            sn[b] = ld_const_chunk(sin_t + ti);
-          }
+      // A rolled loop, the next chunk's table loads issued before this chunk's arithmetic: the body
+      // is one chunk of code.  (A batch of chunks unrolled is several KB of straight-line code that
+      // a large call fetches cold into the instruction cache, the other kernels of a layer having
+      // run in between: its first batch took 7 of a 10 us epilogue at 1024 rows.)
+      auto load_tables = [&](int c, Chunk<T>& cs, Chunk<T>& sn) {
+        const int t = c / CPR, f0 = (c % CPR) * V, F0 = slab * 128 + f0;
+        if (c >= cend || tok0 + t >= g.M || F0 >= g.N) return;
+        const int head = F0 / hd, d0 = F0 - head * hd;
+        if (head < hq + hkv) {
+          const size_t ti = (size_t)s_pos[t] * half + (d0 < half ? d0 : d0 - half);
+          cs = ld_const_chunk(cos_t + ti);
+          sn = ld_const_chunk(sin_t + ti);
         }
+      };
+      Chunk<T> cs_n, sn_n;
+      cs_n.u = sn_n.u = make_uint4(0u, 0u, 0u, 0u);
+      load_tables(cbeg + tid, cs_n, sn_n);
+#pragma unroll 1
+      for (int c = cbeg + tid; c < cend; c += nthr) {
+        const Chunk<T> cs = cs_n, sn = sn_n;
+        load_tables(c + nthr, cs_n, sn_n);
+        const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
+        if (tok >= g.M || F0 >= g.N) continue;
+        const int head = F0 / hd, d0 = F0 - head * hd;
+        Chunk<T> a = ba, bp = bb;
+        if (!fixed) load_bias(c, a, bp);
+        float x[V];
+        ld_acc<V>(acc + t * 128 + f0, x);
+        Chunk<T> o;
+        if (head < hq + hkv) {
+          const bool lo = d0 < half;
+          float xp[V];
+          ld_acc<V>(acc + t * 128 + (lo ? f0 + half : f0 - half), xp);
 #pragma unroll
-        for (int b = 0; b < kEpiBatch; ++b) {
-          const int c = c0 + b * nthr;
-          const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
-          if (c >= cend || tok >= g.M || F0 >= g.N) continue;
-          const int head = F0 / hd, d0 = F0 - head * hd;
-          Chunk<T> a = ba, bp = bb;
-          if (!fixed) load_bias(c, a, bp);
-          float x[V];
-          ld_acc<V>(acc + t * 128 + f0, x);
-          Chunk<T> o;
-          if (head < hq + hkv) {
-            const bool lo = d0 < half;
-            float xp[V];
-            ld_acc<V>(acc + t * 128 + (lo ? f0 + half : f0 - half), xp);
-#pragma unroll
-            for (int v = 0; v < V; v += 2) {
-              const float2 y = round_pair<T>(x[v] + to_f<T>(a.e[v]), x[v + 1] + to_f<T>(a.e[v + 1]));
-              const float2 yp = round_pair<T>(xp[v] + to_f<T>(bp.e[v]), xp[v + 1] + to_f<T>(bp.e[v + 1]));
-              const float r0 = lo ? -yp.x : yp.x, r1 = lo ? -yp.y : yp.y;
-              const float2 cv = round_pair<T>(y.x * to_f<T>(cs[b].e[v]), y.y * to_f<T>(cs[b].e[v + 1]));
-              const float2 sv = round_pair<T>(r0 * to_f<T>(sn[b].e[v]), r1 * to_f<T>(sn[b].e[v + 1]));
-              set_pair<T>(&o.e[v], cv.x + sv.x, cv.y + sv.y);  // T(round(c + s)) == T(c + s)
-            }
-            if (head < hq) {
-              st_chunk(q + (size_t)tok * (hq * hd) + F0, o);
-            } else if (s_kb[t] != nullptr) {
-              st_chunk(s_kb[t] + (head - hq) * hd + d0, o);
-            }
-          } else if (s_vb[t] != nullptr) {
-#pragma unroll
-            for (int v = 0; v < V; v += 2) {
-              const float2 y = round_pair<T>(x[v] + to_f<T>(a.e[v]), x[v + 1] + to_f<T>(a.e[v + 1]));
-              set_pair<T>(&o.e[v], y.x, y.y);
-            }
-            st_chunk(s_vb[t] + (head - hq - hkv) * hd + d0, o);
+          for (int v = 0; v < V; v += 2) {
+            const float2 y = round_pair<T>(x[v] + to_f<T>(a.e[v]), x[v + 1] + to_f<T>(a.e[v + 1]));
+            const float2 yp = round_pair<T>(xp[v] + to_f<T>(bp.e[v]), xp[v + 1] + to_f<T>(bp.e[v + 1]));
+            const float r0 = lo ? -yp.x : yp.x, r1 = lo ? -yp.y : yp.y;
+            const float2 cv = round_pair<T>(y.x * to_f<T>(cs.e[v]), y.y * to_f<T>(cs.e[v + 1]));
+            const float2 sv = round_pair<T>(r0 * to_f<T>(sn.e[v]), r1 * to_f<T>(sn.e[v + 1]));
+            set_pair<T>(&o.e[v], cv.x + sv.x, cv.y + sv.y);  // T(round(c + s)) == T(c + s)
           }
+          if (head < hq) {
+            st_chunk(q + (size_t)tok * (hq * hd) + F0, o);
+          } else if (s_kb[t] != nullptr) {
+            st_chunk(s_kb[t] + (head - hq) * hd + d0, o);
+          }
+        } else if (s_vb[t] != nullptr) {
+#pragma unroll
+          for (int v = 0; v < V; v += 2) {
+            const float2 y = round_pair<T>(x[v] + to_f<T>(a.e[v]), x[v + 1] + to_f<T>(a.e[v + 1]));
+            set_pair<T>(&o.e[v], y.x, y.y);
+          }
+          st_chunk(s_vb[t] + (head - hq - hkv) * hd + d0, o);
         }
       }
       break;

@@ -275,6 +275,13 @@ __global__ void __launch_bounds__(128, 4)
   EpiPre<bf16> pre;
   if (NT <= 64 && (g.tune & kGemmTunePrefetch))
     epi_prefetch<bf16>(g, tok0, slab, S > 1 ? lr0 : 0, S > 1 ? lr1 : NT, threadIdx.x, blockDim.x, pre);
+  // qkv without a prefetched chunk (large calls): warps 2-3, idle while the main loop runs, build the
+  // tile's per-token destinations and prefetch its K / V cache rows into L2 (the barrier after the
+  // accumulator wait publishes them).  Not with the fused norm, whose weights s_epi holds.
+  const bool early_dest = g.epi.kind == kEpiQkvRope && g.norm_x == nullptr && pre.n == 0;
+  if (early_dest && warp >= 2)
+    qkv_dest_setup<bf16>(g, tok0, 0, NT, s_epi, static_cast<int>(threadIdx.x) - 64, static_cast<int>(blockDim.x) - 64,
+                         true);
   if (!mbar_wait(accf, 0)) report_wait(g.err, kErrTimeoutEpilogue, 5, g.M, g.splits);
   if (threadIdx.x == 0) ktrace_stamp<KT>(g.ktrace, 2);
   tc_fence_after_sync();
@@ -345,7 +352,8 @@ __global__ void __launch_bounds__(128, 4)
     // acc holds token columns [cb, cb + kChunk); the epilogue indexes it as the whole tile
     gemm_epilogue<bf16>(g, acc - static_cast<size_t>(cb) * 128, NT, tok0, slab, S > 1 ? cb + lr0 : cb,
                         S > 1 ? cb + lr1 : cb + C::kChunk, s_epi, static_cast<int>(threadIdx.x),
-                        static_cast<int>(blockDim.x), 0, NT <= 64 ? &pre : nullptr);
+                        static_cast<int>(blockDim.x), 0, NT <= 64 ? &pre : nullptr, early_dest ? 0 : -1,
+                        early_dest ? 0 : -1);
   }
   if (threadIdx.x == 0) ktrace_stamp<KT>(g.ktrace, 5);
 
