@@ -252,39 +252,49 @@ __device__ void gemm_epilogue(const GemmArgs& g, float* acc, int nt, int tok0, i
       const T* hs = e.resid_src ? static_cast<const T*>(e.resid_src) : h;
       float* s_ss = reinterpret_cast<float*>(s_epi);  // [nt <= 64][CPR] chunk sums of squares
       const bool want_ss = e.ss_out != nullptr && nt <= 64;
-      for (int c0 = cbeg + tid; c0 < cend; c0 += nthr * kEpiBatch) {
-        Chunk<T> r[kEpiBatch];
+      // the chunk's residual add, rounded as the reference rounds it, and its sum of squares
+      auto finish = [&](int c, const Chunk<T>& r) {
+        const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
+        Chunk<T> o;
+        float ss = 0.f;
+        float x[V];
+        ld_acc<V>(acc + t * 128 + f0, x);
 #pragma unroll
-        for (int b = 0; b < kEpiBatch; ++b) {  // loads first
-          const int c = c0 + b * nthr;
-          const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
-          if (c < cend && tok < g.M && F0 < g.N) {
-            if (!have_pre) {
-              r[b] = ld_chunk(hs + (size_t)tok * e.ld_resid + F0);
-            } else if (b < kEpiPre) {  // prefetched (chunks past kEpiPre per thread do not exist then)
-              r[b] = pre->a[b < kEpiPre ? b : 0];
-            }
-          }
+        for (int v = 0; v < V; v += 2) {
+          const float2 y = round_pair<T>(x[v], x[v + 1]);
+          const float2 z = round_pair<T>(to_f<T>(r.e[v]) + y.x, to_f<T>(r.e[v + 1]) + y.y);
+          set_pair<T>(&o.e[v], z.x, z.y);
+          ss = fmaf(z.x, z.x, ss);
+          ss = fmaf(z.y, z.y, ss);
         }
-#pragma unroll
-        for (int b = 0; b < kEpiBatch; ++b) {
-          const int c = c0 + b * nthr;
-          const int t = c / CPR, f0 = (c % CPR) * V, tok = tok0 + t, F0 = slab * 128 + f0;
-          if (c >= cend || tok >= g.M || F0 >= g.N) continue;
-          Chunk<T> o;
-          float ss = 0.f;
-          float x[V];
-          ld_acc<V>(acc + t * 128 + f0, x);
-#pragma unroll
-          for (int v = 0; v < V; v += 2) {
-            const float2 y = round_pair<T>(x[v], x[v + 1]);
-            const float2 z = round_pair<T>(to_f<T>(r[b].e[v]) + y.x, to_f<T>(r[b].e[v + 1]) + y.y);
-            set_pair<T>(&o.e[v], z.x, z.y);
-            ss = fmaf(z.x, z.x, ss);
-            ss = fmaf(z.y, z.y, ss);
-          }
-          st_chunk(h + (size_t)tok * e.ld_resid + F0, o);
-          if (want_ss) s_ss[t * CPR + (c % CPR)] = ss;
+        st_chunk(h + (size_t)tok * e.ld_resid + F0, o);
+        if (want_ss) s_ss[t * CPR + (c % CPR)] = ss;
+      };
+      // prefetched (decode): each thread owns at most kEpiPre chunks, so no batch loop -- a short
+      // code path for a latency-bound launch whose instructions arrive cold
+      for (int b = 0; have_pre && b < kEpiPre; ++b) {
+        const int c = cbeg + tid + b * nthr;
+        const int t = c / CPR, F0 = slab * 128 + (c % CPR) * V;
+        if (c < cend && tok0 + t < g.M && F0 < g.N) finish(c, pre->a[b]);
+      }
+      // otherwise a rolled loop over the thread's chunks with the next two chunks' residual loads
+      // in flight: one chunk of code, whose instructions a large call fetches cold
+      if (!have_pre) {
+        auto load = [&](int c, Chunk<T>& r) {
+          const int t = c / CPR, tok = tok0 + t, F0 = slab * 128 + (c % CPR) * V;
+          if (c < cend && tok < g.M && F0 < g.N) r = ld_chunk(hs + (size_t)tok * e.ld_resid + F0);
+        };
+        Chunk<T> r1, r2;
+        r1.u = r2.u = make_uint4(0u, 0u, 0u, 0u);
+        load(cbeg + tid, r1);
+        load(cbeg + tid + nthr, r2);
+#pragma unroll 1
+        for (int c = cbeg + tid; c < cend; c += nthr) {
+          const Chunk<T> r = r1;
+          r1 = r2;
+          load(c + 2 * nthr, r2);
+          const int t = c / CPR, F0 = slab * 128 + (c % CPR) * V;
+          if (tok0 + t < g.M && F0 < g.N) finish(c, r);
         }
       }
       if (want_ss) {  // per-row sum over this slab's 128 features, in chunk order (deterministic)
