@@ -111,11 +111,12 @@ def test_tuning_overrides_are_parsed_before_any_device_use(monkeypatch):
     c = _lib.FdllmConfig(1024, 256, 512, 2, 4, 2, 64, 1e-6, 1e6, 1, 32, 4096, 1)
     h = ctypes.c_void_p()
     for spec, needle in (("bogus=1", "unknown tuning key"), ("nt_max=96", "out of range"),
-                         ("split_max", "without '='"), ("attn_splits=x", "bad tuning value")):
+                         ("split_max", "without '='"), ("attn_splits=x", "bad tuning value"),
+                         ("persist_conf_t=2", "out of range")):
         monkeypatch.setenv("FDLLM_TUNING", spec)
         assert lib.fdllm_create(ctypes.byref(c), 0, ctypes.byref(h)) == _lib.FDLLM_ERR_INVALID, spec
         assert needle in lib.fdllm_last_error().decode(), spec
-    monkeypatch.setenv("FDLLM_TUNING", "nt_max=128,split_max=8,persist_min_rows=0,block_graph=0")
+    monkeypatch.setenv("FDLLM_TUNING", "nt_max=128,split_max=8,persist_min_rows=0,block_graph=0,persist_conf_t=0")
     rc = lib.fdllm_create(ctypes.byref(c), 0, ctypes.byref(h))
     assert rc != _lib.FDLLM_ERR_INVALID  # a valid spec passes parsing (then needs a device)
     if rc == _lib.FDLLM_OK:
