@@ -86,8 +86,16 @@ __global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const bf16* __res
                                                                bf16* __restrict__ copy_to) {
   __shared__ float red[32];
   pdl_trigger();
-  pdl_wait();
   const int nch = hidden / 8;
+  // the weights do not depend on the previous kernel: load them while it finishes
+  const uint4* w4 = reinterpret_cast<const uint4*>(w);
+  uint4 wv[kNormChunks];
+#pragma unroll
+  for (int k = 0; k < kNormChunks; ++k) {
+    const int c = threadIdx.x + k * blockDim.x;
+    if (c < nch) wv[k] = __ldg(w4 + c);
+  }
+  pdl_wait();
   const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<size_t>(blockIdx.x) * hidden);
   uint4 xv[kNormChunks];
   float ss = 0.f;
@@ -110,14 +118,12 @@ __global__ void __launch_bounds__(256) rmsnorm_bf16_vec_kernel(const bf16* __res
   const float rs = rsqrtf(block_sum(ss, red) / static_cast<float>(hidden) + eps);
   uint4* orow = reinterpret_cast<uint4*>(out + static_cast<size_t>(blockIdx.x) * hidden);
   uint4* crow = copy_to ? reinterpret_cast<uint4*>(copy_to + static_cast<size_t>(blockIdx.x) * hidden) : nullptr;
-  const uint4* w4 = reinterpret_cast<const uint4*>(w);
 #pragma unroll
   for (int k = 0; k < kNormChunks; ++k) {
     const int c = threadIdx.x + k * blockDim.x;
     if (c >= nch) continue;
-    const uint4 wv = __ldg(w4 + c);
     const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv[k]);
-    const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv);
+    const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wv[k]);
     uint4 o;
     __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
