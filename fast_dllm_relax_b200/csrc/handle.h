@@ -37,6 +37,10 @@ struct Tuning {
                                // (224-row prefill: 2.62 ms at 128 against 3.71 at 256)
   int split_target = 0;        // CTAs per SM the split-K plan aims for (0: 2 at <= 32 rows, else 1)
   int split_max = 16;          // largest split-K cluster of the per-tile GEMM
+  int short_split_max = 8;     // ... of projections with K <= 2048 (qkv, o, gate_up; 0: split_max):
+                               // qkv and o of a decode step in clusters of 8 instead of 12, each CTA's
+                               // 3 weight k blocks still in its ring before the dependency wait
+                               // (8-row step 1.3225 -> 1.3077 ms, 32-row 1.503 -> 1.4996; 6 and 4 slower)
   int gemm_tune = kGemmTunePrefetch | (2 << kGemmTuneL2Shift);  // kGemmTune* bits
   int persist_min_rows = 65;   // token rows from which projections run on the persistent GEMM (0:
                                // never); prefix builds of 96 / 160 / 224 rows: 2.17 / 2.38 / 2.44 ->

@@ -123,6 +123,7 @@ int fdllm::parse_tuning(const char* spec, Tuning* t) {
     if (key == "nt_max" && (x == 64 || x == 128 || x == 256)) t->nt_max = x;
     else if (key == "split_target" && x >= 0 && x <= 4) t->split_target = x;
     else if (key == "split_max" && x >= 1 && x <= 16) t->split_max = x;
+    else if (key == "short_split_max" && x >= 0 && x <= 16) t->short_split_max = x;
     else if (key == "gemm_tune" && x >= 0) t->gemm_tune = x;
     else if (key == "persist_min_rows" && x >= 0) t->persist_min_rows = x;
     else if (key == "persist_splitk" && x >= 0 && x <= 3) t->persist_splitk = x;
@@ -255,7 +256,8 @@ static int plan_gemm(const fdllm_handle* h, const Weight& w, int M, GemmArgs* g,
   // 1.329 ms at prefix 384; the 32-row block step 1.517 -> 1.511 ms, 700 -> 707 tokens/s; 3 or 4
   // slower at both), else 1.
   const int target = h->tune.split_target > 0 ? h->tune.split_target : (M <= 32 ? 2 : 1);
-  const int split_max = h->tune.split_max;
+  const int split_max = h->tune.short_split_max > 0 && g->K <= 2048 ? std::min(h->tune.split_max, h->tune.short_split_max)
+                                                                   : h->tune.split_max;
   if (tiles < target * h->num_sms) {  // split K over a cluster of at most 16 CTAs
     splits = std::max(1, std::min({kblocks, target * h->num_sms / tiles, split_max}));
     const int kpb = (kblocks + splits - 1) / splits;

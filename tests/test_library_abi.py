@@ -112,7 +112,7 @@ def test_tuning_overrides_are_parsed_before_any_device_use(monkeypatch):
     h = ctypes.c_void_p()
     for spec, needle in (("bogus=1", "unknown tuning key"), ("nt_max=96", "out of range"),
                          ("split_max", "without '='"), ("attn_splits=x", "bad tuning value"),
-                         ("persist_conf_t=2", "out of range")):
+                         ("persist_conf_t=2", "out of range"), ("short_split_max=17", "out of range")):
         monkeypatch.setenv("FDLLM_TUNING", spec)
         assert lib.fdllm_create(ctypes.byref(c), 0, ctypes.byref(h)) == _lib.FDLLM_ERR_INVALID, spec
         assert needle in lib.fdllm_last_error().decode(), spec
