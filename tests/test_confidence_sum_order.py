@@ -1,4 +1,7 @@
-"""The two summation orders of a vocabulary slab's sum of exponentials (CPU, float32).
+"""The two reduction orders of a vocabulary slab's confidence partial (CPU, float32).
+
+Besides the sum below, both kernels find the slab's maximum and its first index; the last test
+emulates both scans (ties, NaN, -inf, all-NaN slabs) and requires the same (value, index).
 
 The lm_head's confidence partial of one token and one 128-row slab includes sum_f exp(v_f - max).
 Two kernels compute it (csrc/epilogue.cuh, kEpiConf; csrc/gemm_tc.cu, conf_slab_from_tmem):
@@ -66,3 +69,67 @@ def test_orders_differ_from_a_plain_sequential_sum():
             seq = np.float32(seq + x)
         differs += int(seq.tobytes() != _lane_tree(e).tobytes())
     assert differs > 0
+
+
+def _lane_tree_argmax(v: np.ndarray, f0: int):
+    """tokens on N: lane l scans f = l + 32 i, then the xor butterfly merges (value, index) pairs;
+    a pair replaces the running one if its value is larger, or equal with a smaller index."""
+    best = [np.float32(-np.inf)] * 32
+    idx = [0x7FFFFFFF] * 32
+    for lane in range(32):
+        for i in range(4):
+            x, F = v[lane + 32 * i], f0 + lane + 32 * i
+            if x > best[lane] or (x == best[lane] and F < idx[lane]):
+                best[lane], idx[lane] = x, F
+    for off in (16, 8, 4, 2, 1):
+        nb, ni = list(best), list(idx)
+        for lane in range(32):
+            ob, oi = best[lane ^ off], idx[lane ^ off]
+            if ob > best[lane] or (ob == best[lane] and oi < idx[lane]):
+                nb[lane], ni[lane] = ob, oi
+        best, idx = nb, ni
+    return best[0], idx[0]
+
+
+def _register_argmax(v: np.ndarray, f0: int):
+    """tokens on M: per group of 16 columns, a NaN-ignoring maximum and the first index holding it
+    (reverse scan); groups ascend, and a group replaces the running pair if its maximum is larger,
+    or if no index was found yet and it equals the running maximum."""
+    best, best_i = np.float32(-np.inf), 0x7FFFFFFF
+    for c in range(8):
+        g = v[16 * c:16 * c + 16]
+        m = g[0]
+        for x in g[1:]:
+            m = np.float32(np.fmax(m, x))
+        mi = 0x7FFFFFFF
+        for j in range(15, -1, -1):
+            if g[j] == m:
+                mi = f0 + 16 * c + j
+        if m > best or (best_i == 0x7FFFFFFF and m == best):
+            best, best_i = m, mi
+    return best, best_i
+
+
+def test_maximum_and_first_index_agree_with_nan_inf_and_ties():
+    rng = np.random.default_rng(2)
+    for trial in range(400):
+        v = rng.standard_normal(128).astype(np.float32)
+        kind = trial % 6
+        if kind == 1:  # ties of the maximum across lanes, groups and quarters
+            top = np.float32(5.0)
+            v[rng.choice(128, 4, replace=False)] = top
+        elif kind == 2:  # NaNs never win
+            v[rng.choice(128, 10, replace=False)] = np.float32(np.nan)
+        elif kind == 3:  # every value -inf: the first index
+            v[:] = np.float32(-np.inf)
+        elif kind == 4:  # -inf and NaN only
+            v[:] = np.float32(-np.inf)
+            v[rng.choice(128, 20, replace=False)] = np.float32(np.nan)
+        elif kind == 5:  # all NaN: no index
+            v[:] = np.float32(np.nan)
+        f0 = 128 * int(rng.integers(0, 1187))
+        (b1, i1), (b2, i2) = _lane_tree_argmax(v, f0), _register_argmax(v, f0)
+        assert i1 == i2, (trial, kind, i1, i2)
+        assert (np.isnan(b1) and np.isnan(b2)) or b1 == b2, (trial, kind, b1, b2)
+        if kind == 5:
+            assert i1 == 0x7FFFFFFF and b1 == -np.inf
